@@ -1,0 +1,816 @@
+// Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM),
+// fed by TMA.  One persistent, warp-specialised kernel template covers every
+// contraction of the scattermoe expert layer:
+//
+//   MODE_ROWS  out[rows of expert e, :] = A[rows, :K] @ B_e^T
+//              (scatter2scatter, scattermoe/kernels/ops.py:128-190; forward
+//               up/down projections and the input-gradient GEMMs)
+//   MODE_XTY   out_e = A[rows of e]^T @ B[rows of e]
+//              (groupXtY, scattermoe/kernels/ops.py:320-438; weight gradients)
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer (one elected lane) + TMEM allocator
+//   warp 1      MMA issuer (lane 0 issues tcgen05.mma, whole warp zero-fills
+//               reduction tails in MODE_XTY)
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> global
+// Pipelines: STAGES shared-memory stages (full/empty mbarriers) between the
+// producer and the MMA warp; two TMEM accumulator buffers (tfull/tempty)
+// between the MMA warp and the epilogue, so the epilogue of tile i overlaps
+// the main loop of tile i+1.
+//
+// Tiles are 128 x BN x 64 (BM x BN x BK), bf16/f16 operands in 128-byte
+// swizzled shared memory, f32 accumulation in TMEM.  A tile never spans two
+// experts: every expert's rows start a new M tile, and the tile list is built
+// on the device from the expert boundaries, so no host sync is needed.
+#include "zs_common.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace zs {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int MAX_EXPERTS_GEMM = 1024;
+
+enum { MODE_ROWS = 0, MODE_XTY = 1 };
+enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
+
+struct GemmArgs {
+  int mode;
+  int num_experts;
+  int n_tiles;           // output tiles along N
+  int m_tiles_xty;       // MODE_XTY: tiles along M
+  int kb_rows;           // MODE_ROWS: number of BK blocks along K
+  int M_xty;             // MODE_XTY: M extent (masking)
+  int N_out;             // output columns (masking)
+  int ab_fmt;            // 0 = f16, 1 = bf16
+  int64_t n_rows;        // sorted rows in total
+  int64_t out_rows;      // MODE_ROWS: rows of the output (row_map values must lie below)
+  const int64_t* expert_offsets;      // inclusive cumsum, or null
+  const int64_t* sorted_expert_idxs;  // used when expert_offsets is null
+  const int64_t* row_map;             // MODE_ROWS: output row per sorted row (null: identity)
+  char* out;
+  int64_t ldo_m, ldo_n, out_se;       // element strides of the output
+  char* out2;                          // EPI_SWIGLU: pre-activation rows (nullable)
+  int64_t ldo2;
+  const char* bias;                    // MODE_ROWS + EPI_STORE (nullable)
+  int64_t bias_se, bias_sn;
+  int out_dtype;                       // ZS_F32 / ZS_BF16 / ZS_F16
+  int b_rows_per_expert;               // rows of B's 2-D view per expert
+  int swiglu_half;                     // EPI_SWIGLU: B-row offset of the gate half
+  int vec_ok;                          // 16-byte vector stores allowed for row-contiguous output
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OFF_STAGES = 0;
+  static constexpr int OFF_BARS = STAGES * STAGE_BYTES;
+  // full[S], empty[S], tfull[2], tempty[2], done
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int OFF_MISC = OFF_BARS + NUM_BARS * 8;  // tmem addr, abort flag
+  static constexpr int OFF_TPREFIX = OFF_MISC + 16;
+  static constexpr int OFF_RSTART = OFF_TPREFIX + (MAX_EXPERTS_GEMM + 1) * 4;
+  static constexpr int TOTAL = OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4;
+  static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
+};
+
+struct TileInfo {
+  int e;
+  int mt, nt;
+  int r0, r1;   // MODE_ROWS: rows [r0, r1) of this tile; MODE_XTY: expert rows [r0, r1)
+  int nkb;      // k-blocks in the main loop
+};
+
+__device__ __forceinline__ int64_t lower_bound_i64(const int64_t* a, int64_t n, int64_t v) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    int64_t mid = (lo + hi) >> 1;
+    if (__ldg(a + mid) < v)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+template <int BN>
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const int* tprefix, const int* rstart) {
+  TileInfo ti;
+  int lo = 0, hi = a.num_experts;
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (tprefix[mid] <= t)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  ti.e = lo;
+  int local = t - tprefix[lo];
+  ti.mt = local / a.n_tiles;
+  ti.nt = local - ti.mt * a.n_tiles;
+  if (a.mode == MODE_ROWS) {
+    ti.r0 = rstart[lo] + ti.mt * BM;
+    ti.r1 = min(ti.r0 + BM, rstart[lo + 1]);
+    ti.nkb = a.kb_rows;
+  } else {
+    ti.r0 = rstart[lo];
+    ti.r1 = rstart[lo + 1];
+    ti.nkb = (ti.r1 - ti.r0 + BK - 1) / BK;
+  }
+  return ti;
+}
+
+__device__ __forceinline__ void store_val(char* base, int64_t idx, int dtype, float v) {
+  if (dtype == ZS_BF16)
+    reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+  else if (dtype == ZS_F16)
+    reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+  else
+    reinterpret_cast<float*>(base)[idx] = v;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, int dtype) {
+  if (dtype == ZS_F16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// Store 32 consecutive columns [col0, col0 + 32) of one output row.
+// Element (m, n) lives at out[row_off + n * ldn].
+__device__ __forceinline__ void store_chunk(char* out, int64_t row_off, int64_t ldn, int col0, int ncols,
+                                            const float (&v)[32], int dtype, bool vec_ok) {
+  if (ldn == 1 && vec_ok && ncols >= 32 && dtype != ZS_F32) {
+    uint4* dst = reinterpret_cast<uint4*>(out + (row_off + col0) * 2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack2(v[q * 8 + 0], v[q * 8 + 1], dtype);
+      w.y = pack2(v[q * 8 + 2], v[q * 8 + 3], dtype);
+      w.z = pack2(v[q * 8 + 4], v[q * 8 + 5], dtype);
+      w.w = pack2(v[q * 8 + 6], v[q * 8 + 7], dtype);
+      dst[q] = w;
+    }
+  } else if (ldn == 1 && vec_ok && ncols >= 32 && dtype == ZS_F32) {
+    float4* dst = reinterpret_cast<float4*>(out + (row_off + col0) * 4);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols) store_val(out, row_off + (int64_t)(col0 + j) * ldn, dtype, v[j]);
+  }
+}
+
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == ZS_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == ZS_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+// silu as torch computes it for a reduced-precision tensor: x / (1 + exp(-x))
+// in f32, rounded to the storage dtype.
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmArgs args) {
+  using L = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BARS);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* done = bars + 2 * STAGES + 4;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  int* s_tprefix = reinterpret_cast<int*>(smem + L::OFF_TPREFIX);
+  int* s_rstart = reinterpret_cast<int*>(smem + L::OFF_RSTART);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = args.num_experts;
+  constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+
+  // ---- set-up: barriers, TMEM, expert boundaries
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 1 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    int64_t s;
+    if (e == 0)
+      s = 0;
+    else if (args.expert_offsets != nullptr)
+      s = __ldg(args.expert_offsets + (e - 1));
+    else
+      s = lower_bound_i64(args.sorted_expert_idxs, args.n_rows, e);
+    s = s < 0 ? 0 : (s > args.n_rows ? args.n_rows : s);
+    s_rstart[e] = (int)s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int per = (E + 31) / 32;
+    const int beg = lane * per;
+    const int end = min(beg + per, E);
+    int local = 0;
+    for (int e = beg; e < end; ++e) {
+      int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
+      local += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+    }
+    int incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int run = incl - local;
+    for (int e = beg; e < end; ++e) {
+      s_tprefix[e] = run;
+      int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
+      run += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+    }
+    if (lane == 31) s_tprefix[E] = incl;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total_tiles = s_tprefix[E];
+
+  constexpr uint32_t STAGE_TX = (uint32_t)L::STAGE_BYTES;
+  constexpr uint32_t IDESC_BF16 = idesc_f16(BM, BN, 1, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t IDESC_F16 = idesc_f16(BM, BN, 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;       // stages that received at least one load
+      uint32_t issued_parity = 0;     // parity of the last load per stage
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+        for (int kb = 0; kb < ti.nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + L::OFF_STAGES + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
+          if (args.mode == MODE_ROWS) {
+            if (!A_MN) tma_load_2d(sA, &tmA, &full[stage], kb * BK, ti.r0);
+            if (!B_MN) {
+              const int brow = ti.e * args.b_rows_per_expert;
+              if (EPI == EPI_SWIGLU) {
+                tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * (BN / 2));
+                tma_load_2d(sB + (BN / 2) * 128, &tmB, &full[stage], kb * BK,
+                            brow + args.swiglu_half + ti.nt * (BN / 2));
+              } else {
+                tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * BN);
+              }
+            } else {
+              const int brow = ti.e * args.b_rows_per_expert + kb * BK;
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + j * 64, brow);
+            }
+          } else {
+            const int row = ti.r0 + kb * BK;
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sA + j * (BK * 128), &tmA, &full[stage], ti.mt * BM + j * 64, row);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + j * 64, row);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: never leave the CTA with a TMA write still in flight.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t acc_iter = 0;
+    bool ok = true;
+    const uint32_t idesc = args.ab_fmt ? IDESC_BF16 : IDESC_F16;
+    bool issued_any = false;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+      if (ti.nkb == 0) continue;
+      const uint32_t buf = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      if (!warp_wait(&tempty[buf], acc_phase ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = 0; kb < ti.nkb; ++kb) {
+        if (!warp_wait(&full[stage], phase, s_abort, ZS_DEVERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* sA = smem + L::OFF_STAGES + stage * L::STAGE_BYTES;
+        uint8_t* sB = sA + L::A_BYTES;
+        if (args.mode == MODE_XTY) {
+          // Reduction tail: rows past the expert's end belong to the next
+          // expert.  Zero them in both operands (K-rows of the MN-major tiles).
+          const int valid = min(BK, ti.r1 - (ti.r0 + kb * BK));
+          if (valid < BK) {
+            const int nrow = BK - valid;
+            const int chunks_a = (BM / 64) * nrow * 8;
+            const int chunks_b = (BN / 64) * nrow * 8;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            for (int c = lane; c < chunks_a + chunks_b; c += 32) {
+              const bool isA = c < chunks_a;
+              const int cc = isA ? c : c - chunks_a;
+              const int atom = cc / (nrow * 8);
+              const int rem = cc - atom * nrow * 8;
+              const int row = valid + (rem >> 3);
+              const int ch = rem & 7;
+              uint8_t* base = isA ? sA : sB;
+              *reinterpret_cast<uint4*>(base + atom * (BK * 128) + row * 128 + ch * 16) = z;
+            }
+            fence_proxy_async_smem();
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {
+          const uint32_t a_base = smem_u32(sA);
+          const uint32_t b_base = smem_u32(sB);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? smem_desc(a_base + kk * 2048, BK * 128, 1024, 2)
+                                        : smem_desc(a_base + kk * 32, 16, 1024, 2);
+            const uint64_t bdesc = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024, 2)
+                                        : smem_desc(b_base + kk * 32, 16, 1024, 2);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          issued_any = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(&tfull[buf]);
+      __syncwarp();
+      ++acc_iter;
+    }
+    // Make sure every MMA this thread issued has finished before TMEM is freed.
+    if (lane == 0 && issued_any) {
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    uint32_t acc_iter = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+      if (args.mode == MODE_XTY && ti.nkb == 0) {
+        // Expert without rows: its weight gradient is zero.
+        const int m = ti.mt * BM + row_in_tile;
+        if (m < args.M_xty) {
+          float z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0.f;
+          for (int c = 0; c < BN / 32; ++c) {
+            const int col0 = ti.nt * BN + c * 32;
+            const int ncols = min(32, args.N_out - col0);
+            if (ncols <= 0) break;
+            store_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, args.ldo_n, col0, ncols, z,
+                        args.out_dtype, args.vec_ok);
+          }
+        }
+        continue;
+      }
+      const uint32_t buf = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      if (!warp_wait(&tfull[buf], acc_phase, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+
+      if (args.mode == MODE_ROWS) {
+        const int row = ti.r0 + row_in_tile;
+        int64_t out_row = row;
+        bool valid = row < ti.r1;
+        if (valid && args.row_map != nullptr) {
+          out_row = __ldg(args.row_map + row);
+          if (out_row < 0 || out_row >= args.out_rows) {
+            record_error(ZS_DEVERR_INDEX);
+            valid = false;
+          }
+        }
+        if (EPI == EPI_SWIGLU) {
+          // D columns [0, BN/2) hold the "up" half, [BN/2, BN) the "gate" half.
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            uint32_t ru[32], rg[32];
+            tmem_ld_32x32b_x32(t_row + c * 32, ru);
+            tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
+            tc_wait_ld();
+            const int col0 = ti.nt * (BN / 2) + c * 32;
+            const int ncols = min(32, args.N_out - col0);
+            if (valid && ncols > 0) {
+              float u[32], g[32], h[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                u[j] = round_to(__uint_as_float(ru[j]), args.out_dtype);
+                g[j] = round_to(__uint_as_float(rg[j]), args.out_dtype);
+                const float s = round_to(silu_f32(g[j]), args.out_dtype);
+                h[j] = s * u[j];
+              }
+              store_chunk(args.out, out_row * args.ldo_m, 1, col0, ncols, h, args.out_dtype, args.vec_ok);
+              if (args.out2 != nullptr) {
+                store_chunk(args.out2, out_row * args.ldo2, 1, col0, ncols, u, args.out_dtype, args.vec_ok);
+                store_chunk(args.out2, out_row * args.ldo2, 1, args.swiglu_half + col0, ncols, g, args.out_dtype,
+                            args.vec_ok);
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + c * 32, r);
+            tc_wait_ld();
+            const int col0 = ti.nt * BN + c * 32;
+            const int ncols = min(32, args.N_out - col0);
+            if (valid && ncols > 0) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              if (args.bias != nullptr) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  if (j < ncols) {
+                    const int64_t bi = ti.e * args.bias_se + (int64_t)(col0 + j) * args.bias_sn;
+                    float b;
+                    if (args.out_dtype == ZS_BF16)
+                      b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi]);
+                    else if (args.out_dtype == ZS_F16)
+                      b = __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
+                    else
+                      b = reinterpret_cast<const float*>(args.bias)[bi];
+                    v[j] += b;
+                  }
+                }
+              }
+              store_chunk(args.out, out_row * args.ldo_m, args.ldo_n, col0, ncols, v, args.out_dtype, args.vec_ok);
+            }
+          }
+        }
+      } else {
+        const int m = ti.mt * BM + row_in_tile;
+        const bool valid = m < args.M_xty;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tc_wait_ld();
+          const int col0 = ti.nt * BN + c * 32;
+          const int ncols = min(32, args.N_out - col0);
+          if (valid && ncols > 0) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, args.ldo_n, col0, ncols, v,
+                        args.out_dtype, args.vec_ok);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+      ++acc_iter;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16/f16 tensor map with 128-byte swizzle.  inner/outer are the extents
+// in elements/rows, row_bytes the row pitch.
+static int make_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                     uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return ZS_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return ZS_ERR_ALIGN;
+  if ((row_bytes & 15) != 0) return ZS_ERR_ALIGN;
+  if (inner == 0 || outer == 0) return ZS_ERR_SHAPE;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dtype == ZS_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ZS_OK : ZS_ERR_CUDA;
+}
+
+int num_sms() {
+  static int n = 0;
+  static int dev_cached = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != dev_cached) {
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    dev_cached = dev;
+  }
+  return n > 0 ? n : 148;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
+                       cudaStream_t stream) {
+  using L = Smem<BN, STAGES>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  int64_t grid = num_sms();
+  if (max_tiles < grid) grid = max_tiles;
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, 192, L::ALLOC, stream>>>(tmA, tmB, args);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+}  // namespace zs
+
+// Declared in zs_moe.cu.
+namespace zs {
+int launch_group(const void* A, int64_t a_sm, int64_t K, void* Y, int64_t y_sm, int64_t n, const void* coeff,
+                 int coeff_dtype, int fan_out, const int64_t* ssi, int dtype, cudaStream_t stream);
+}
+
+using namespace zs;
+
+static inline int elem_size(int dtype) { return dtype == ZS_F32 ? 4 : 2; }
+
+extern "C" size_t zs_scatter2scatter_workspace(int64_t n, int64_t K, int dtype, int x_grouped) {
+  if (x_grouped) return 0;
+  // gathered rows, padded so the row pitch is a multiple of 16 bytes
+  const int64_t pitch = ((K * elem_size(dtype) + 15) / 16) * 16;
+  return (size_t)(n * pitch + 256);
+}
+
+extern "C" int zs_scatter2scatter(void* out, int64_t out_sm, const void* W, int64_t num_experts, int64_t K,
+                                  int64_t N, int64_t w_se, int64_t w_sk, int64_t w_sn, const void* X, int64_t x_rows,
+                                  int64_t x_sm, const void* bias, int64_t b_se, int64_t b_sn, int fan_out,
+                                  const int64_t* sorted_expert_idxs, const int64_t* sorted_scattered_idxs,
+                                  const int64_t* expert_offsets, int64_t n, int x_grouped, int y_grouped, int dtype,
+                                  void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(out && W && X && sorted_expert_idxs && sorted_scattered_idxs, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0 && fan_out >= 1, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
+  ZS_REQUIRE(x_grouped ? (x_rows == n) : (x_rows * fan_out == n), ZS_ERR_SHAPE);
+  if (n == 0) return ZS_OK;
+  const int es = elem_size(dtype);
+
+  // B operand layout
+  bool b_mn;
+  if (w_sk == 1 && w_se == N * w_sn && w_sn >= K)
+    b_mn = false;
+  else if (w_sn == 1 && w_se == K * w_sk && w_sk >= N)
+    b_mn = true;
+  else
+    return ZS_ERR_LAYOUT;
+
+  // A operand: grouped rows, gathered into the workspace when needed
+  const void* A = X;
+  int64_t a_sm = x_sm;
+  if (!x_grouped) {
+    const size_t need = zs_scatter2scatter_workspace(n, K, dtype, 0);
+    ZS_REQUIRE(workspace != nullptr && workspace_bytes >= need, ZS_ERR_WORKSPACE);
+    char* ws = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    const int64_t pitch = ((K * es + 15) / 16) * 16 / es;
+    int rc = launch_group(X, x_sm, K, ws, pitch, n, nullptr, dtype, fan_out, sorted_scattered_idxs, dtype, stream);
+    if (rc != ZS_OK) return rc;
+    A = ws;
+    a_sm = pitch;
+  }
+
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, A, dtype, (uint64_t)K, (uint64_t)n, (uint64_t)a_sm * es, 64, 128);
+  if (rc != ZS_OK) return rc;
+  constexpr int BN = 256;
+  if (!b_mn)
+    rc = make_tmap(&tmB, W, dtype, (uint64_t)K, (uint64_t)(num_experts * N), (uint64_t)w_sn * es, 64, BN);
+  else
+    rc = make_tmap(&tmB, W, dtype, (uint64_t)N, (uint64_t)(num_experts * K), (uint64_t)w_sk * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+
+  GemmArgs a{};
+  a.mode = MODE_ROWS;
+  a.num_experts = (int)num_experts;
+  a.n_tiles = (int)((N + BN - 1) / BN);
+  a.kb_rows = (int)((K + BK - 1) / BK);
+  a.N_out = (int)N;
+  a.ab_fmt = dtype == ZS_BF16 ? 1 : 0;
+  a.n_rows = n;
+  a.expert_offsets = expert_offsets;
+  a.sorted_expert_idxs = sorted_expert_idxs;
+  a.row_map = y_grouped ? nullptr : sorted_scattered_idxs;
+  a.out_rows = n;
+  a.out = reinterpret_cast<char*>(out);
+  a.ldo_m = out_sm;
+  a.ldo_n = 1;
+  a.bias = reinterpret_cast<const char*>(bias);
+  a.bias_se = b_se;
+  a.bias_sn = b_sn;
+  a.out_dtype = dtype;
+  a.b_rows_per_expert = (int)(b_mn ? K : N);
+  a.vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && ((out_sm * es) % 16 == 0);
+  const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
+  if (!b_mn) return launch_gemm<BN, 4, false, false, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
+  return launch_gemm<BN, 4, false, true, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
+}
+
+extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db,
+                            int64_t db_se, int64_t db_sn, const void* DY, int64_t dy_sm, const void* X, int64_t x_sm,
+                            int64_t n, int64_t K, int64_t N, const int64_t* expert_offsets, int dtype,
+                            void* stream_);
+
+namespace zs {
+int launch_colsum_per_expert(void* Db, int64_t db_se, int64_t db_sn, const void* DY, int64_t dy_sm, int64_t N,
+                             int num_experts, const int64_t* expert_offsets, int dtype, cudaStream_t stream);
+}
+
+extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db,
+                            int64_t db_se, int64_t db_sn, const void* DY, int64_t dy_sm, const void* X, int64_t x_sm,
+                            int64_t n, int64_t K, int64_t N, const int64_t* expert_offsets, int dtype,
+                            void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(DW && DY && X && expert_offsets, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+
+  // Orientation: GEMM rows m run along the stride-1 side when possible so the
+  // epilogue writes 16-byte row segments.
+  //   dw_sn == 1: m = k (A = X^T), n = n (B = DY^T), element at m*dw_sk + n
+  //   dw_sk == 1: m = n (A = DY^T), n = k (B = X^T), element at m*dw_sn + k
+  bool swap;
+  if (dw_sn == 1)
+    swap = false;
+  else if (dw_sk == 1)
+    swap = true;
+  else
+    return ZS_ERR_LAYOUT;
+  const void* Aop = swap ? DY : X;
+  const int64_t a_sm = swap ? dy_sm : x_sm;
+  const int64_t Mext = swap ? N : K;
+  const void* Bop = swap ? X : DY;
+  const int64_t b_sm = swap ? x_sm : dy_sm;
+  const int64_t Next = swap ? K : N;
+
+  GemmArgs a{};
+  a.mode = MODE_XTY;
+  a.num_experts = num_experts;
+  a.n_tiles = (int)((Next + BN - 1) / BN);
+  a.m_tiles_xty = (int)((Mext + BM - 1) / BM);
+  a.M_xty = (int)Mext;
+  a.N_out = (int)Next;
+  a.ab_fmt = dtype == ZS_BF16 ? 1 : 0;
+  a.n_rows = n;
+  a.expert_offsets = expert_offsets;
+  a.out = reinterpret_cast<char*>(DW);
+  a.ldo_m = swap ? dw_sn : dw_sk;
+  a.ldo_n = 1;
+  a.out_se = dw_se;
+  a.out_dtype = dtype;
+  a.vec_ok = ((reinterpret_cast<uintptr_t>(DW) & 15) == 0) && ((a.ldo_m * es) % 16 == 0) &&
+             ((dw_se * es) % 16 == 0);
+
+  const int64_t max_tiles = (int64_t)num_experts * a.m_tiles_xty * a.n_tiles;
+  if (n == 0) {
+    // every expert is empty: the kernel only writes zeros; TMA maps need a
+    // nonzero extent, so point them at a 1-row view of the (unused) inputs.
+    n = 1;
+  }
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, Aop, dtype, (uint64_t)Mext, (uint64_t)n, (uint64_t)a_sm * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmB, Bop, dtype, (uint64_t)Next, (uint64_t)n, (uint64_t)b_sm * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+  rc = launch_gemm<BN, 4, true, true, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
+  if (rc != ZS_OK) return rc;
+  if (Db != nullptr)
+    rc = launch_colsum_per_expert(Db, db_se, db_sn, DY, dy_sm, N, num_experts, expert_offsets, dtype, stream);
+  return rc;
+}
+
+extern "C" int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64_t num_experts, int64_t K, int64_t F,
+                                   const void* Xg, int64_t xg_sm, const int64_t* sorted_expert_idxs,
+                                   const int64_t* expert_offsets, int64_t n, int dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(act && W1 && Xg && (sorted_expert_idxs || expert_offsets), ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && F >= 1 && n >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && F < (int64_t)1 << 23, ZS_ERR_SHAPE);
+  ZS_REQUIRE(num_experts * 2 * F < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  if (n == 0) return ZS_OK;
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, Xg, dtype, (uint64_t)K, (uint64_t)n, (uint64_t)xg_sm * es, 64, 128);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmB, W1, dtype, (uint64_t)K, (uint64_t)(num_experts * 2 * F), (uint64_t)K * es, 64, BN / 2);
+  if (rc != ZS_OK) return rc;
+  GemmArgs a{};
+  a.mode = MODE_ROWS;
+  a.num_experts = (int)num_experts;
+  a.n_tiles = (int)((F + BN / 2 - 1) / (BN / 2));
+  a.kb_rows = (int)((K + BK - 1) / BK);
+  a.N_out = (int)F;
+  a.ab_fmt = dtype == ZS_BF16 ? 1 : 0;
+  a.n_rows = n;
+  a.expert_offsets = expert_offsets;
+  a.sorted_expert_idxs = sorted_expert_idxs;
+  a.row_map = nullptr;
+  a.out_rows = n;
+  a.out = reinterpret_cast<char*>(act);
+  a.ldo_m = F;
+  a.ldo_n = 1;
+  a.out2 = reinterpret_cast<char*>(hfull);
+  a.ldo2 = 2 * F;
+  a.out_dtype = dtype;
+  a.b_rows_per_expert = (int)(2 * F);
+  a.swiglu_half = (int)F;
+  a.vec_ok = ((reinterpret_cast<uintptr_t>(act) | reinterpret_cast<uintptr_t>(hfull)) % 16 == 0) &&
+             ((F * es) % 16 == 0);
+  const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
+  return launch_gemm<BN, 4, false, false, EPI_SWIGLU>(tmA, tmB, a, max_tiles, stream);
+}

@@ -1,0 +1,7 @@
+// Single translation unit for libzs.so: the kernels share one device-global
+// error word, so they are compiled together rather than with separate device
+// linking.
+#include "zs_gemm.cu"
+#include "zs_moe.cu"
+#include "zs_routing.cu"
+#include "zs_api.cu"

@@ -1,0 +1,160 @@
+"""scattermoe.mlp on the B200 kernels.
+
+MLP and GLUMLP keep the reference's constructor arguments, parameter names
+and shapes (scattermoe/mlp.py:6-95): experts.weight [E, 2f, d] for GLUMLP with
+the first f rows the "up" half and the last f rows the "gate" half, and
+output_experts.weight [E, d, f].
+
+GLUMLP.forward runs one autograd function whose forward is
+  sort -> gather -> grouped GEMM with SwiGLU fused in its epilogue ->
+  grouped GEMM scattered to (token, slot) rows -> gate-weighted combine
+and whose backward is the reference's ParallelLinear backward for both
+projections with the SwiGLU backward in between.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from zs_b200 import _lib as Z
+from .kernels import ops
+from .parallel_experts import ParallelExperts, flatten_sort_count
+
+
+def _compute_dtype(x: torch.Tensor) -> torch.dtype:
+    return x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+
+
+def weighted_row_sum(rows: torch.Tensor, weights, T: int, k: int) -> torch.Tensor:
+    """out[t] = sum_j w[t, j] * rows[t*k + j] (plain sum when weights is None)."""
+    C = rows.size(1)
+    out = torch.empty((T, C), dtype=rows.dtype, device=rows.device)
+    w = None if weights is None else weights.contiguous()
+    Z.count(1)
+    Z.check(Z.lib().zs_weighted_row_sum(out.data_ptr(), out.stride(0), rows.data_ptr(), rows.stride(0), Z.ptr(w),
+                                        Z.dtype_code(w.dtype) if w is not None else 0, T, k, C,
+                                        Z.dtype_code(rows.dtype), Z.stream_of(rows)), "zs_weighted_row_sum")
+    return out
+
+
+def up_swiglu(xg, W1, sorted_expert_idxs, expert_offsets):
+    """(act [n, f], hfull [n, 2f]) of the fused up projection."""
+    n, d = xg.shape
+    E, f2, _ = W1.shape
+    f = f2 // 2
+    act = torch.empty((n, f), dtype=xg.dtype, device=xg.device)
+    hfull = torch.empty((n, f2), dtype=xg.dtype, device=xg.device)
+    Z.count(1)
+    with Z.timed("up_swiglu"):
+        Z.check(Z.lib().zs_expert_up_swiglu(act.data_ptr(), hfull.data_ptr(), W1.data_ptr(), E, d, f,
+                                            xg.data_ptr(), xg.stride(0), sorted_expert_idxs.data_ptr(),
+                                            expert_offsets.data_ptr(), n, Z.dtype_code(xg.dtype), Z.stream_of(xg)),
+                "zs_expert_up_swiglu")
+    return act, hfull
+
+
+def swiglu_backward(dact, hfull):
+    n, f = dact.shape
+    dh = torch.empty((n, 2 * f), dtype=dact.dtype, device=dact.device)
+    Z.count(1)
+    Z.check(Z.lib().zs_swiglu_backward(dh.data_ptr(), dact.data_ptr(), hfull.data_ptr(), n, f,
+                                       Z.dtype_code(dact.dtype), Z.stream_of(dact)), "zs_swiglu_backward")
+    return dh
+
+
+class GLUExpertsFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k):
+        Z.require_cuda(x, expert_p, expert_idxs, W1, W2)
+        cdt = _compute_dtype(x)
+        xc = x.to(cdt).contiguous()
+        W1c = W1.to(cdt).contiguous()
+        W2c = W2.to(cdt).contiguous()
+        pc = expert_p.to(cdt).contiguous()
+        T = xc.size(0)
+        sei, ssi, offs = flatten_sort_count(expert_idxs, num_experts)
+        xg = ops.group(xc, ssi, fan_out=k)
+        act, hfull = up_swiglu(xg, W1c, sei, offs)
+        y_rows = torch.empty((T * k, W2c.size(1)), dtype=cdt, device=x.device)
+        ops._launch_scatter2scatter(y_rows, W2c.permute(0, 2, 1), act, 1, sei, ssi, None, True, False,
+                                    expert_offsets=offs)
+        y = weighted_row_sum(y_rows, pc, T, k)
+        ctx.save_for_backward(xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c)
+        ctx.meta = (x.dtype, expert_p.dtype, W1.dtype, W2.dtype, num_experts, k, T)
+        return y.to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c = ctx.saved_tensors
+        x_dt, p_dt, w1_dt, w2_dt, E, k, T = ctx.meta
+        cdt = xg.dtype
+        dyc = dy.to(cdt).contiguous()
+        d = dyc.size(1)
+        d_p = ops.rowwise_sum_product(y_rows.view(T, k, d), dyc, dtype=p_dt)
+        dyg = ops.group(dyc, ssi, fan_out=k, coeff=pc.flatten())
+        dact = torch.empty_like(act)
+        ops._launch_scatter2scatter(dact, W2c, dyg, 1, sei, ssi, None, True, True, expert_offsets=offs)
+        dW2, _ = ops.group_bwd_W(dyg, act, offs, E)             # [E, f, d] view of [E, d, f]
+        dhfull = swiglu_backward(dact, hfull)
+        dW1, _ = ops.group_bwd_W(dhfull, xg, offs, E)           # [E, d, 2f] view of [E, 2f, d]
+        dx_rows = torch.empty((T * k, xg.size(1)), dtype=cdt, device=dy.device)
+        ops._launch_scatter2scatter(dx_rows, W1c, dhfull, 1, sei, ssi, None, True, False, expert_offsets=offs)
+        dx = weighted_row_sum(dx_rows, None, T, k)
+        return (dx.to(x_dt), d_p, None, dW1.permute(0, 2, 1).to(w1_dt), dW2.permute(0, 2, 1).to(w2_dt), None,
+                None)
+
+
+class MLP(nn.Module):
+    def __init__(self, input_size, hidden_size, num_experts, top_k, bias=False, activation=None):
+        super().__init__()
+        self.num_experts = num_experts
+        self.input_size = input_size
+        self.hidden_size = hidden_size
+        self.experts = ParallelExperts(num_experts, input_size, hidden_size, bias=bias)
+        self.output_experts = ParallelExperts(num_experts, hidden_size, input_size, bias=bias)
+        self.top_k = min(top_k, self.num_experts)
+        self.activation = activation
+
+    def extra_repr(self):
+        return "k={}".format(self.top_k)
+
+    def forward(self, x: torch.Tensor, expert_p: torch.Tensor, expert_idxs: torch.Tensor):
+        x_shape = x.size()
+        x = x.view(-1, x_shape[-1])
+        sei, ssi, offs = flatten_sort_count(expert_idxs, num_experts=self.num_experts)
+        h = self.experts(x, self.top_k, sei, ssi, offs, grouped_out=True)
+        h = self.activation(h)
+        y = self.output_experts(h, 1, sei, ssi, offs, grouped_in=True, gates=expert_p)
+        return y.view(*x_shape[:-1], y.size(-1))
+
+
+class GLUMLP(nn.Module):
+    def __init__(self, input_size, hidden_size, num_experts, top_k, bias=False, activation=nn.SiLU()):
+        super().__init__()
+        self.num_experts = num_experts
+        self.input_size = input_size
+        self.hidden_size = hidden_size
+        self.experts = ParallelExperts(num_experts, input_size, 2 * hidden_size, bias=bias)
+        self.output_experts = ParallelExperts(num_experts, hidden_size, input_size, bias=bias)
+        self.top_k = min(top_k, self.num_experts)
+        self.activation = activation
+
+    def extra_repr(self):
+        return "k={}".format(self.top_k)
+
+    def _fused_ok(self) -> bool:
+        return self.experts.bias is None and isinstance(self.activation, nn.SiLU)
+
+    def forward(self, x: torch.Tensor, expert_p: torch.Tensor, expert_idxs: torch.Tensor):
+        x_shape = x.size()
+        x = x.view(-1, x_shape[-1])
+        if self._fused_ok():
+            y = GLUExpertsFunction.apply(x, expert_p.reshape(x.size(0), -1), expert_idxs.reshape(x.size(0), -1),
+                                         self.experts.weight, self.output_experts.weight, self.num_experts,
+                                         self.top_k)
+        else:
+            sei, ssi, offs = flatten_sort_count(expert_idxs, num_experts=self.num_experts)
+            h, gates = self.experts(x, self.top_k, sei, ssi, offs, grouped_out=True).chunk(2, dim=-1)
+            h = self.activation(gates) * h
+            y = self.output_experts(h, 1, sei, ssi, offs, grouped_in=True, gates=expert_p)
+        return y.view(*x_shape[:-1], y.size(-1))

@@ -1,0 +1,149 @@
+"""ctypes binding of libzs.so, the C ABI declared in include/zs.h.
+
+There is no CPU fallback: every op requires CUDA tensors and the compiled
+library, and raises when either is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB = None
+_LOCK = threading.Lock()
+LIB_PATH = Path(__file__).resolve().parent / "libzs.so"
+
+ZS_F32, ZS_BF16, ZS_F16 = 0, 1, 2
+_DTYPE_CODE = {torch.float32: ZS_F32, torch.bfloat16: ZS_BF16, torch.float16: ZS_F16}
+
+_vp, _i64, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/zs.h
+_SIGNATURES = {
+    "zs_version": (_i32, []),
+    "zs_error_string": (ctypes.c_char_p, [_i32]),
+    "zs_device_error_get": (_i32, [ctypes.POINTER(_i32), _vp]),
+    "zs_device_error_clear": (_i32, [_vp]),
+    "zs_moe_gate_topk": (_i32, [_vp, _i32, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "zs_flatten_sort_count_workspace": (_sz, [_i64, _i32]),
+    "zs_flatten_sort_count": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "zs_bincount": (_i32, [_vp, _i64, _i32, _vp, _vp]),
+    "zs_expert_counts": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "zs_bias_sign_update": (_i32, [_vp, _i32, _f32, _vp, _vp]),
+    "zs_scatter2scatter_workspace": (_sz, [_i64, _i64, _i32, _i32]),
+    "zs_scatter2scatter": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
+                                  _i64, _i32, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "zs_group_xty": (_i32, [_i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
+                            _vp, _i32, _vp]),
+    "zs_group": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp]),
+    "zs_rowwise_sum_product": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
+                                      _i64, _i64, _i64, _vp]),
+    "zs_weighted_row_sum": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i64, _i32, _vp]),
+    "zs_expert_up_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
+    "zs_swiglu_backward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
+}
+
+
+class ZsError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not LIB_PATH.exists():
+                raise ZsError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
+                              "(the zs ops have no CPU fallback)")
+            h = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(h, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = h
+    return _LIB
+
+
+def exported_symbols():
+    return list(_SIGNATURES)
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().zs_error_string(rc).decode()
+        raise ZsError(f"{what} failed: {msg} (zs code {rc})")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise ZsError(f"unsupported dtype {dt}") from None
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ZsError("zs ops run only on CUDA tensors (no CPU fallback); got a tensor on " + str(t.device))
+
+
+def device_error(device=None) -> int:
+    out = ctypes.c_int(0)
+    check(lib().zs_device_error_get(ctypes.byref(out), torch.cuda.current_stream(device).cuda_stream),
+          "zs_device_error_get")
+    return out.value
+
+
+def clear_device_error(device=None) -> None:
+    check(lib().zs_device_error_clear(torch.cuda.current_stream(device).cuda_stream), "zs_device_error_clear")
+
+
+# ------------------------------------------------------------ instrumentation
+# Counters and CUDA-event timers used by bench.py; off by default.
+
+class _Instr:
+    launches = 0          # kernels of libzs.so launched through these bindings
+    timing = False        # record CUDA events around the grouped GEMM launches
+    events = {}           # name -> [(start_event, end_event), ...]
+
+
+INSTR = _Instr()
+
+
+def count(n: int = 1) -> None:
+    INSTR.launches += n
+
+
+class timed:
+    """Record a CUDA event pair around a launch when INSTR.timing is set."""
+
+    __slots__ = ("name", "s")
+
+    def __init__(self, name):
+        self.name = name
+        self.s = None
+
+    def __enter__(self):
+        if INSTR.timing:
+            self.s = torch.cuda.Event(enable_timing=True)
+            self.s.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.s is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            INSTR.events.setdefault(self.name, []).append((self.s, e))
+        return False

@@ -1,0 +1,201 @@
+/*
+ * zs.h — C ABI of the B200 (sm_100a) kernels for the Zarelga-Superposition
+ * MoE training step.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * and a CUDA stream passed as `void*` (a cudaStream_t / CUstream; NULL is the
+ * legacy default stream).  Nothing here allocates device memory: callers pass
+ * outputs and, where a kernel needs scratch, a workspace whose size the
+ * matching *_workspace() function returns.  Calls are asynchronous on the
+ * given stream and never synchronise the host, so they can be captured in a
+ * CUDA graph.
+ *
+ * Return value: ZS_OK (0) or one of the ZS_ERR_* codes below for a rejected
+ * argument or a failed launch.  Faults detected on the device (a bounded wait
+ * that ran out, an index out of range) never trap: they set bits in a
+ * device-global error word read with zs_device_error_get().
+ *
+ * Each declaration names the reference function it replaces
+ * (CoffeeVampir3/Architecture-Zarelga-Superposition, path:line).
+ */
+#ifndef ZS_H_
+#define ZS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define ZS_OK 0
+#define ZS_ERR_ARG 1         /* null pointer or invalid enum */
+#define ZS_ERR_SHAPE 2       /* sizes inconsistent or out of the supported range */
+#define ZS_ERR_DTYPE 3       /* unsupported dtype combination */
+#define ZS_ERR_ALIGN 4       /* pointer or stride alignment required by TMA not met */
+#define ZS_ERR_CUDA 5        /* a CUDA runtime/driver call failed */
+#define ZS_ERR_WORKSPACE 6   /* workspace missing or too small */
+#define ZS_ERR_LAYOUT 7      /* stride pattern not supported by the kernel */
+
+/* device error bits (zs_device_error_get) */
+#define ZS_DEVERR_TIMEOUT_PRODUCER 0x01
+#define ZS_DEVERR_TIMEOUT_MMA 0x02
+#define ZS_DEVERR_TIMEOUT_EPILOGUE 0x04
+#define ZS_DEVERR_TIMEOUT_DRAIN 0x08
+#define ZS_DEVERR_INDEX 0x10       /* an index input was out of range; the element was skipped */
+
+/* dtype codes */
+#define ZS_F32 0
+#define ZS_BF16 1
+#define ZS_F16 2
+
+/* ------------------------------------------------------------------ misc */
+int zs_version(void);
+const char* zs_error_string(int code);
+/* Synchronously read (stream-ordered) the device error word of the current device. */
+int zs_device_error_get(int* out, void* stream);
+/* Clear the device error word (stream-ordered). */
+int zs_device_error_clear(void* stream);
+
+/* ------------------------------------------------------------- routing (a1-a3) */
+
+/*
+ * MoEGate.forward after the router GEMM and sigmoid
+ * (modeling/moe_gate.py:29-34):
+ *   biased = gate_probs + expert_biases           (f32)
+ *   topk_idx = topk(biased, top_k, sorted=False)  (CUDA torch.topk order:
+ *              values above the k-th value in index order, then ties equal to
+ *              the k-th value in index order)
+ *   topk_weight = L1-normalise(gate_probs[topk_idx])  (F.normalize p=1, eps=1e-12)
+ * gate_probs: [num_tokens, num_experts] row-major, dtype probs_dtype.
+ * topk_idx: int64 [num_tokens, top_k]; topk_weight: probs_dtype [num_tokens, top_k].
+ * Limits: num_experts <= 1024, top_k <= 32, top_k <= num_experts.
+ */
+int zs_moe_gate_topk(const void* gate_probs, int probs_dtype, const float* expert_biases, int64_t num_tokens,
+                     int num_experts, int top_k, int64_t* topk_idx, void* topk_weight, void* stream);
+
+/*
+ * flatten_sort_count (scattermoe/parallel_experts.py:21-28): stable counting
+ * sort of the flat expert ids.
+ *   sorted_expert_idxs[i]    expert id of the i-th sorted slot
+ *   sorted_scattered_idxs[i] flat index (token * k + j) of that slot; ties keep
+ *                            ascending flat index
+ *   expert_offsets[e]        inclusive cumulative count (int64)
+ * expert_idxs values must lie in [0, num_experts); others raise ZS_DEVERR_INDEX
+ * and are dropped.  Workspace: zs_flatten_sort_count_workspace(n, num_experts) bytes.
+ */
+size_t zs_flatten_sort_count_workspace(int64_t n, int num_experts);
+int zs_flatten_sort_count(const int64_t* expert_idxs, int64_t n, int num_experts, int64_t* sorted_expert_idxs,
+                          int64_t* sorted_scattered_idxs, int64_t* expert_offsets, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* compileable_bincount (scattermoe/parallel_experts.py:6-15): int64 counts of
+ * x[0..n) over [0, minlength). */
+int zs_bincount(const int64_t* x, int64_t n, int minlength, int64_t* out, void* stream);
+
+/*
+ * auxillary_loss_free_update (main.py:161-175), split so that a data-parallel
+ * caller can all-reduce the counts between the two halves.
+ *   zs_expert_counts: counts[e] += #{(t, j) : valid[t] && topk_idx[t, j] == e}
+ *     (valid may be NULL = all tokens valid; counts is accumulated, not cleared)
+ *   zs_bias_sign_update: bias[e] += update_rate * sign(mean(counts) - counts[e]),
+ *     skipped entirely when sum(counts) == 0 (the reference's `numel() == 0`).
+ */
+int zs_expert_counts(const int64_t* topk_idx, const uint8_t* valid, int64_t num_tokens, int top_k,
+                     int num_experts, int64_t* counts, void* stream);
+int zs_bias_sign_update(const int64_t* counts, int num_experts, float update_rate, float* expert_biases,
+                        void* stream);
+
+/* ------------------------------------------------ grouped expert GEMMs (a5-a9) */
+
+/*
+ * scatter2scatter (scattermoe/kernels/ops.py:192-255, kernel :128-190):
+ *   for each sorted slot i with expert e = sorted_expert_idxs[i]:
+ *     in_row  = x_grouped ? i : sorted_scattered_idxs[i] / fan_out
+ *     out_row = y_grouped ? i : sorted_scattered_idxs[i]
+ *     out[out_row, :] = X[in_row, :] @ W[e] (+ b[e])
+ * W is addressed as W[e, k, n] = W + e*w_se + k*w_sk + n*w_sn and must have
+ * either w_sk == 1 (K contiguous, e.g. the reference's weight.permute(0,2,1))
+ * or w_sn == 1 (N contiguous); w_se must equal the packed expert size.
+ * X: [x_rows, K] with row stride x_sm; out: [n, N] with row stride out_sm.
+ * dtype: ZS_BF16 or ZS_F16 for X, W and out; bias same dtype or NULL.
+ * expert_offsets (inclusive cumsum) may be NULL, in which case expert
+ * boundaries are found from sorted_expert_idxs.
+ * Workspace: zs_scatter2scatter_workspace(n, K, dtype, x_grouped) bytes
+ * (the gathered input rows when x_grouped == 0).
+ */
+size_t zs_scatter2scatter_workspace(int64_t n, int64_t K, int dtype, int x_grouped);
+int zs_scatter2scatter(void* out, int64_t out_sm, const void* W, int64_t num_experts, int64_t K, int64_t N,
+                       int64_t w_se, int64_t w_sk, int64_t w_sn, const void* X, int64_t x_rows, int64_t x_sm,
+                       const void* bias, int64_t b_se, int64_t b_sn, int fan_out, const int64_t* sorted_expert_idxs,
+                       const int64_t* sorted_scattered_idxs, const int64_t* expert_offsets, int64_t n, int x_grouped,
+                       int y_grouped, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * groupXtY (scattermoe/kernels/ops.py:263-311, kernel :320-438):
+ *   for each expert e with sorted rows [start_e, end_e) (from expert_offsets,
+ *   inclusive cumsum):  DW[e] = X[start_e:end_e]^T @ DY[start_e:end_e]
+ *   and, when Db != NULL, Db[e] = column sums of DY[start_e:end_e].
+ * DW[e, k, n] = DW + e*dw_se + k*dw_sk + n*dw_sn, with dw_sk == 1 or dw_sn == 1.
+ * Experts with no rows get zeros.  X: [n, K], DY: [n, N], grouped (sorted) rows.
+ */
+int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db, int64_t db_se,
+                 int64_t db_sn, const void* DY, int64_t dy_sm, const void* X, int64_t x_sm, int64_t n, int64_t K,
+                 int64_t N, const int64_t* expert_offsets, int dtype, void* stream);
+
+/*
+ * group (scattermoe/kernels/ops.py:449-482, kernel :490-529):
+ *   Y[i, :] = A[sorted_scattered_idxs[i] / fan_out, :] (* coeff[sorted_scattered_idxs[i]])
+ * A: [n / fan_out, K] row stride a_sm; Y: [n, K] row stride y_sm; coeff may be NULL.
+ */
+int zs_group(const void* A, int64_t a_sm, int64_t K, void* Y, int64_t y_sm, int64_t n, const void* coeff,
+             int coeff_dtype, int fan_out, const int64_t* sorted_scattered_idxs, int dtype, void* stream);
+
+/*
+ * rowwise_sum_product (scattermoe/kernels/ops.py:9-46, kernel :50-80):
+ *   out[t, f] = sum_h A[t, f, h] * B[t, h]   (f32 accumulation)
+ * Strides in elements.
+ */
+int zs_rowwise_sum_product(void* out, int out_dtype, int64_t o_s0, int64_t o_s1, const void* A, int a_dtype,
+                           int64_t a_s0, int64_t a_s1, int64_t a_s2, const void* B, int b_dtype, int64_t b_s0,
+                           int64_t b_s1, int64_t T, int64_t F, int64_t H, void* stream);
+
+/*
+ * k-way row combine that closes the expert layer:
+ *   out[t, c] = sum_j w[t, j] * in[t*k + j, c]
+ * With weights it is the gate-weighted sum `gates.unsqueeze(1) @ output_expanded`
+ * (scattermoe/parallel_experts.py:50-52); with weights == NULL it is the
+ * `.view(T, k, d).sum(-2)` of the input gradient (parallel_experts.py:122-125).
+ * f32 accumulation; in/out dtype ZS_BF16 or ZS_F16, weights any dtype code.
+ */
+int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, const void* weights, int w_dtype,
+                        int64_t T, int k, int64_t C, int dtype, void* stream);
+
+/*
+ * GLUMLP up projection with the SwiGLU activation fused into the GEMM
+ * epilogue (scattermoe/mlp.py:80-87: experts(...) then chunk(2) into
+ * h = first half, gates = second half, then silu(gates) * h):
+ *   hfull[i, :] = Xg[i, :] @ W1[e_i]^T          ([n, 2F]; written when hfull != NULL)
+ *   act[i, c]   = silu(hfull[i, F + c]) * hfull[i, c]   ([n, F])
+ * W1: the experts.weight tensor [E, 2F, K], contiguous.  Xg: grouped rows
+ * [n, K] with row stride xg_sm.  act/hfull contiguous.  Intermediates are
+ * rounded to the storage dtype exactly where the reference stores them.
+ */
+int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64_t num_experts, int64_t K, int64_t F,
+                        const void* Xg, int64_t xg_sm, const int64_t* sorted_expert_idxs, const int64_t* expert_offsets,
+                        int64_t n, int dtype, void* stream);
+
+/*
+ * Backward of act = silu(g) * h (autograd of scattermoe/mlp.py:87):
+ *   dhfull[:, :F] = dact * silu(g);  dhfull[:, F:] = (dact * h) * silu'(g)
+ * with hfull = [h | g] rows [n, 2F]; all contiguous, one dtype.
+ */
+int zs_swiglu_backward(void* dhfull, const void* dact, const void* hfull, int64_t n, int64_t F, int dtype,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZS_H_ */

@@ -1,0 +1,159 @@
+"""Generate golden fixtures by running the reference implementation itself.
+
+Run once in a container that has the reference checked out (read-only) at
+$ZS_REFERENCE (default /root/reference):
+
+    python tests/golden/gen_golden.py
+
+The reference's Triton kernels (scattermoe/kernels/ops.py) run on the CPU
+through Triton's interpreter (TRITON_INTERPRET=1); MoEGate and
+flatten_sort_count run as plain CPU PyTorch.  Outputs are small .npz files next
+to this script; the tests read only those files and never the reference.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np
+import torch
+
+REF = os.environ.get("ZS_REFERENCE", "/root/reference")
+OUT = Path(__file__).resolve().parent
+
+
+def _import_reference():
+    sys.path.insert(0, REF)
+    from scattermoe.kernels import ops  # noqa: F401
+    from scattermoe import parallel_experts, mlp  # noqa: F401
+    from modeling import moe_gate  # noqa: F401
+    return ops, parallel_experts, mlp, moe_gate
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy() if t.is_floating_point() else t.detach().cpu().numpy()
+
+
+def gen_gate(moe_gate):
+    cases = {}
+    for name, (T, d, E, k, bias_std, seed) in {
+        "gate_e8_k2": (64, 32, 8, 2, 0.0, 11),
+        "gate_e64_k8": (300, 48, 64, 8, 0.1, 12),
+        "gate_e128_k8": (97, 40, 128, 8, 0.1, 13),
+    }.items():
+        g = torch.Generator().manual_seed(seed)
+        cfg = types.SimpleNamespace(n_experts_per_token=k, n_routed_experts=E, hidden_size=d, initializer_range=0.2)
+        gate = moe_gate.MoEGate(cfg)
+        with torch.no_grad():
+            gate.weight.copy_(torch.randn(E, d, generator=g) * 0.2)
+            gate.expert_biases.copy_(torch.randn(E, generator=g) * bias_std)
+        hidden = torch.randn(1, T, d, generator=g)
+        with torch.no_grad():
+            idx, w = gate(hidden)
+            probs = torch.sigmoid(torch.nn.functional.linear(hidden.view(-1, d), gate.weight))
+        cases[name] = dict(hidden=_np(hidden.view(T, d)), weight=_np(gate.weight), bias=_np(gate.expert_biases),
+                           probs=_np(probs), topk_idx=_np(idx.view(T, k)), topk_weight=_np(w.view(T, k)), k=k)
+    return cases
+
+
+def gen_fsc(parallel_experts):
+    cases = {}
+    for name, (T, k, E, seed) in {"fsc_small": (37, 2, 8, 21), "fsc_e64": (1500, 8, 64, 22),
+                                  "fsc_skew": (700, 6, 64, 23)}.items():
+        g = torch.Generator().manual_seed(seed)
+        if name == "fsc_skew":
+            probs = torch.softmax(torch.randn(E, generator=g) * 3, 0)
+            idx = torch.multinomial(probs.expand(T, E), k, replacement=False, generator=g)
+        else:
+            idx = torch.randint(0, E, (T, k), generator=g)
+        sei, ssi, off = parallel_experts.flatten_sort_count(idx, num_experts=E)
+        cases[name] = dict(expert_idxs=_np(idx), sorted_expert_idxs=_np(sei), sorted_scattered_idxs=_np(ssi),
+                           expert_offsets=_np(off), num_experts=E)
+    return cases
+
+
+def _routing(T, k, E, g):
+    scores = torch.rand(T, E, generator=g)
+    idx = torch.topk(scores, k, dim=-1).indices
+    p = torch.softmax(torch.randn(T, k, generator=g), -1)
+    return idx, p
+
+
+def gen_ops(ops, parallel_experts):
+    cases = {}
+    T, d, E, k, N = 45, 64, 6, 3, 80
+    g = torch.Generator().manual_seed(31)
+    X = torch.randn(T, d, generator=g)
+    Wt = torch.randn(E, N, d, generator=g) * 0.1          # weight [E, out, in]
+    idx, p = _routing(T, k, E, g)
+    sei, ssi, off = parallel_experts.flatten_sort_count(idx, num_experts=E)
+    base = dict(X=_np(X), Wt=_np(Wt), expert_idxs=_np(idx), p=_np(p), sorted_expert_idxs=_np(sei),
+                sorted_scattered_idxs=_np(ssi), expert_offsets=_np(off), k=k)
+    # scatter2scatter, x ungrouped -> y grouped and y scattered
+    base["s2s_xg0_yg1"] = _np(ops.scatter2scatter(X, Wt.permute(0, 2, 1), sei, ssi, k, x_grouped=False, y_grouped=True))
+    base["s2s_xg0_yg0"] = _np(ops.scatter2scatter(X, Wt.permute(0, 2, 1), sei, ssi, k, x_grouped=False, y_grouped=False))
+    Xg = torch.randn(T * k, d, generator=g)
+    base["Xg"] = _np(Xg)
+    base["s2s_xg1_yg1"] = _np(ops.scatter2scatter(Xg, Wt.permute(0, 2, 1), sei, ssi, 1, x_grouped=True, y_grouped=True))
+    base["s2s_xg1_yg0"] = _np(ops.scatter2scatter(Xg, Wt.permute(0, 2, 1), sei, ssi, 1, x_grouped=True, y_grouped=False))
+    # the transposed weight as used for input gradients (N contiguous)
+    DYg = torch.randn(T * k, N, generator=g)
+    base["DYg"] = _np(DYg)
+    base["s2s_wT"] = _np(ops.scatter2scatter(DYg, Wt, sei, ssi, 1, x_grouped=True, y_grouped=False))
+    bias = torch.randn(E, N, generator=g)
+    base["bias"] = _np(bias)
+    base["s2s_bias"] = _np(ops.scatter2scatter(X, Wt.permute(0, 2, 1), sei, ssi, k, b=bias, x_grouped=False,
+                                               y_grouped=True))
+    dw, db = ops.group_bwd_W(DYg, Xg, off, E, has_bias=True)
+    base["xty_dw"] = _np(dw)
+    base["xty_db"] = _np(db)
+    base["group"] = _np(ops.group(X, ssi, fan_out=k))
+    base["group_coeff"] = _np(ops.group(X, ssi, fan_out=k, coeff=p.flatten()))
+    A3 = torch.randn(T, k, d, generator=g)
+    B2 = torch.randn(T, d, generator=g)
+    base["A3"] = _np(A3)
+    base["B2"] = _np(B2)
+    base["rsp"] = _np(ops.rowwise_sum_product(A3, B2))
+    cases["ops_f32"] = base
+    return cases
+
+
+def gen_glu(mlp):
+    cases = {}
+    for name, (T, d, E, k, f, seed) in {"glu_small": (33, 64, 4, 2, 32, 41), "glu_e8": (70, 96, 8, 3, 48, 42)}.items():
+        g = torch.Generator().manual_seed(seed)
+        torch.manual_seed(seed)
+        m = mlp.GLUMLP(d, f, E, k)
+        with torch.no_grad():
+            m.experts.weight.copy_(torch.randn(E, 2 * f, d, generator=g) * 0.1)
+            m.output_experts.weight.copy_(torch.randn(E, d, f, generator=g) * 0.1)
+        x = torch.randn(T, d, generator=g, requires_grad=True)
+        idx, p = _routing(T, k, E, g)
+        p = p.clone().requires_grad_(True)
+        y = m(x, p, idx)
+        dy = torch.randn(T, d, generator=g)
+        y.backward(dy)
+        cases[name] = dict(x=_np(x), expert_p=_np(p), expert_idxs=_np(idx), W1=_np(m.experts.weight),
+                           W2=_np(m.output_experts.weight), y=_np(y), dy=_np(dy), dx=_np(x.grad), dp=_np(p.grad),
+                           dW1=_np(m.experts.weight.grad), dW2=_np(m.output_experts.weight.grad), k=k)
+    return cases
+
+
+def main():
+    ops, parallel_experts, mlp, moe_gate = _import_reference()
+    all_cases = {}
+    all_cases.update(gen_gate(moe_gate))
+    all_cases.update(gen_fsc(parallel_experts))
+    all_cases.update(gen_ops(ops, parallel_experts))
+    all_cases.update(gen_glu(mlp))
+    for name, arrs in all_cases.items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name, sorted(arrs.keys()))
+
+
+if __name__ == "__main__":
+    main()
