@@ -8,11 +8,12 @@
 //   MODE_XTY   out_e = A[rows of e]^T @ B[rows of e]
 //              (groupXtY, scattermoe/kernels/ops.py:320-438; weight gradients)
 //
-// Warp roles (192 threads, one CTA per SM):
+// Warp roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected lane) + TMEM allocator
 //   warp 1      MMA issuer (lane 0 issues tcgen05.mma, whole warp zero-fills
 //               reduction tails in MODE_XTY)
-//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> global
+//   warps 2..9  epilogue: tcgen05.ld TMEM -> registers -> per-warp shared
+//               memory transpose -> 64-byte row-segment global stores
 // Pipelines: STAGES shared-memory stages (full/empty mbarriers) between the
 // producer and the MMA warp; two TMEM accumulator buffers (tfull/tempty)
 // between the MMA warp and the epilogue, so the epilogue of tile i overlaps
@@ -35,7 +36,7 @@ constexpr int BK = 64;
 constexpr int MAX_EXPERTS_GEMM = 1024;
 
 enum { MODE_ROWS = 0, MODE_XTY = 1 };
-enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
+enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_DSWIGLU = 2 };
 
 struct GemmArgs {
   int mode;
@@ -59,7 +60,10 @@ struct GemmArgs {
   int64_t bias_se, bias_sn;
   int out_dtype;                       // ZS_F32 / ZS_BF16 / ZS_F16
   int b_rows_per_expert;               // rows of B's 2-D view per expert
-  int swiglu_half;                     // EPI_SWIGLU: B-row offset of the gate half
+  int swiglu_half;                     // EPI_SWIGLU: B-row offset of the gate half; EPI_DSWIGLU: column
+                                       // offset of the gate half in aux/out
+  const char* aux;                     // EPI_DSWIGLU: saved pre-activation rows [h | g]
+  int64_t ld_aux;
   int vec_ok;                          // 16-byte vector stores allowed for row-contiguous output
 };
 
@@ -75,7 +79,8 @@ struct Smem {
   static constexpr int OFF_MISC = OFF_BARS + NUM_BARS * 8;  // tmem addr, abort flag
   static constexpr int OFF_TPREFIX = OFF_MISC + 16;
   static constexpr int OFF_RSTART = OFF_TPREFIX + (MAX_EXPERTS_GEMM + 1) * 4;
-  static constexpr int TOTAL = OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4;
+  static constexpr int OFF_STG = ((OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4 + 15) / 16) * 16;
+  static constexpr int TOTAL = OFF_STG + 8 * 32 * 80;
   static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
 };
 
@@ -143,12 +148,34 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, int dtype) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-// Store 32 consecutive columns [col0, col0 + 32) of one output row.
-// Element (m, n) lives at out[row_off + n * ldn].
-__device__ __forceinline__ void store_chunk(char* out, int64_t row_off, int64_t ldn, int col0, int ncols,
-                                            const float (&v)[32], int dtype, bool vec_ok) {
-  if (ldn == 1 && vec_ok && ncols >= 32 && dtype != ZS_F32) {
-    uint4* dst = reinterpret_cast<uint4*>(out + (row_off + col0) * 2);
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == ZS_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == ZS_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+// Fast sigmoid / silu in f32 (ex2.approx-based exp and approximate divide);
+// the result is rounded to the storage dtype by the caller, which hides the
+// few-ulp f32 difference from torch's x / (1 + exp(-x)).
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_fast(float x) { return x * sigmoid_fast(x); }
+
+// Per-warp staging buffer for coalesced row stores: 32 rows x 64 bytes with
+// an 80-byte pitch (conflict-free 16-byte writes and reads).
+constexpr int STG_PITCH = 80;
+constexpr int STG_BYTES = 32 * STG_PITCH;
+constexpr int NUM_EPI_WARPS = 8;
+
+// Write 32 consecutive columns [col0, col0 + ncols) of this lane's output row
+// (element (row, n) at out[row_off + n]).  When the chunk is full and 16-bit,
+// the warp transposes its 32 rows through shared memory so that each store
+// instruction writes 64 contiguous bytes of 8 rows; otherwise scalar stores.
+// Must be called by all 32 lanes with warp-uniform col0/ncols.
+__device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0, int ncols, bool valid,
+                                           const float (&v)[32], int dtype, bool vec, uint8_t* stg) {
+  const int lane = threadIdx.x & 31;
+  if (vec && ncols == 32) {
+    uint4* my = reinterpret_cast<uint4*>(stg + lane * STG_PITCH);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint4 w;
@@ -156,31 +183,74 @@ __device__ __forceinline__ void store_chunk(char* out, int64_t row_off, int64_t 
       w.y = pack2(v[q * 8 + 2], v[q * 8 + 3], dtype);
       w.z = pack2(v[q * 8 + 4], v[q * 8 + 5], dtype);
       w.w = pack2(v[q * 8 + 6], v[q * 8 + 7], dtype);
-      dst[q] = w;
+      my[q] = w;
     }
-  } else if (ldn == 1 && vec_ok && ncols >= 32 && dtype == ZS_F32) {
-    float4* dst = reinterpret_cast<float4*>(out + (row_off + col0) * 4);
+    __syncwarp();
+    const unsigned long long my_ptr =
+        valid ? reinterpret_cast<unsigned long long>(out + (row_off + col0) * 2) : 0ull;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-  } else {
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2);
+      const int qq = lane & 3;
+      const uint4 w = *reinterpret_cast<const uint4*>(stg + r * STG_PITCH + qq * 16);
+      const unsigned long long p = __shfl_sync(0xffffffffu, my_ptr, r);
+      if (p != 0ull) reinterpret_cast<uint4*>(p)[qq] = w;
+    }
+    __syncwarp();
+  } else if (valid) {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (j < ncols) store_val(out, row_off + (int64_t)(col0 + j) * ldn, dtype, v[j]);
+      if (j < ncols) store_val(out, row_off + col0 + j, dtype, v[j]);
   }
 }
 
-__device__ __forceinline__ float round_to(float v, int dtype) {
-  if (dtype == ZS_BF16) return __bfloat162float(__float2bfloat16_rn(v));
-  if (dtype == ZS_F16) return __half2float(__float2half_rn(v));
-  return v;
+// Read 32 consecutive 16-bit columns of this lane's row as f32.
+__device__ __forceinline__ void load_chunk(const char* src, int64_t row_off, int col0, int ncols, bool valid,
+                                           float (&v)[32], int dtype, bool vec) {
+  if (!valid) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    return;
+  }
+  if (vec && ncols == 32) {
+    const uint4* p = reinterpret_cast<const uint4*>(src + (row_off + col0) * 2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = __ldg(p + q);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        if (dtype == ZS_F16) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[h]));
+          v[q * 8 + 2 * h] = f.x;
+          v[q * 8 + 2 * h + 1] = f.y;
+        } else {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[h]));
+          v[q * 8 + 2 * h] = f.x;
+          v[q * 8 + 2 * h + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float x = 0.f;
+      if (j < ncols) {
+        const int64_t i = row_off + col0 + j;
+        if (dtype == ZS_BF16)
+          x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[i]);
+        else if (dtype == ZS_F16)
+          x = __half2float(reinterpret_cast<const __half*>(src)[i]);
+        else
+          x = reinterpret_cast<const float*>(src)[i];
+      }
+      v[j] = x;
+    }
+  }
 }
 
-// silu as torch computes it for a reduced-precision tensor: x / (1 + exp(-x))
-// in f32, rounded to the storage dtype.
-__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
-
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
   using L = Smem<BN, STAGES>;
@@ -210,7 +280,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 32 * NUM_EPI_WARPS);
     }
     mbar_init(done, 1);
     *s_abort = 0;
@@ -408,25 +478,28 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    // 8 warps: warp w reads TMEM lane quarter (w % 4) (rows 32q..32q+31 of
+    // the tile) and one half of the tile's columns, h = (w - 2) / 4.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t* stg = smem + L::OFF_STG + (warp - 2) * STG_BYTES;
+    const bool vec = args.vec_ok && args.out_dtype != ZS_F32;
     uint32_t acc_iter = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
       if (args.mode == MODE_XTY && ti.nkb == 0) {
         // Expert without rows: its weight gradient is zero.
         const int m = ti.mt * BM + row_in_tile;
-        if (m < args.M_xty) {
-          float z[32];
+        float z[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) z[j] = 0.f;
-          for (int c = 0; c < BN / 32; ++c) {
-            const int col0 = ti.nt * BN + c * 32;
-            const int ncols = min(32, args.N_out - col0);
-            if (ncols <= 0) break;
-            store_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, args.ldo_n, col0, ncols, z,
-                        args.out_dtype, args.vec_ok);
-          }
+        for (int j = 0; j < 32; ++j) z[j] = 0.f;
+        for (int c = 0; c < BN / 64; ++c) {
+          const int col0 = ti.nt * BN + half * (BN / 2) + c * 32;
+          const int ncols = min(32, args.N_out - col0);
+          if (ncols <= 0) break;
+          const int64_t roff = ti.e * args.out_se + (int64_t)m * args.ldo_m;
+          emit_chunk(args.out, roff, col0, ncols, m < args.M_xty, z, args.out_dtype, vec, stg);
         }
         continue;
       }
@@ -448,81 +521,111 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         if (EPI == EPI_SWIGLU) {
-          // D columns [0, BN/2) hold the "up" half, [BN/2, BN) the "gate" half.
+          // D columns [0, BN/2) hold the "up" half, [BN/2, BN) the "gate"
+          // half; this warp produces activation columns [h*BN/4, (h+1)*BN/4).
+#pragma unroll 1
+          for (int c = 0; c < BN / 128; ++c) {
+            const int lc = half * (BN / 4) + c * 32;
+            uint32_t ru[32], rg[32];
+            tmem_ld_32x32b_x32(t_row + lc, ru);
+            tmem_ld_32x32b_x32(t_row + BN / 2 + lc, rg);
+            tc_wait_ld();
+            const int col0 = ti.nt * (BN / 2) + lc;
+            const int ncols = min(32, args.N_out - col0);
+            if (ncols <= 0) continue;
+            float u[32], g[32], h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              u[j] = round_to(__uint_as_float(ru[j]), args.out_dtype);
+              g[j] = round_to(__uint_as_float(rg[j]), args.out_dtype);
+              h[j] = round_to(silu_fast(g[j]), args.out_dtype) * u[j];
+            }
+            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, h, args.out_dtype, vec, stg);
+            if (args.out2 != nullptr) {
+              emit_chunk(args.out2, out_row * args.ldo2, col0, ncols, valid, u, args.out_dtype, vec, stg);
+              emit_chunk(args.out2, out_row * args.ldo2, args.swiglu_half + col0, ncols, valid, g,
+                         args.out_dtype, vec, stg);
+            }
+          }
+        } else if (EPI == EPI_DSWIGLU) {
+          // The accumulator is d(act) for activation columns; combine it with
+          // the saved pre-activation [h | g] into d[h | g].
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
-            uint32_t ru[32], rg[32];
-            tmem_ld_32x32b_x32(t_row + c * 32, ru);
-            tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
+            const int lc = half * (BN / 2) + c * 32;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + lc, r);
             tc_wait_ld();
-            const int col0 = ti.nt * (BN / 2) + c * 32;
+            const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
-            if (valid && ncols > 0) {
-              float u[32], g[32], h[32];
+            if (ncols <= 0) continue;
+            float hv[32], gv[32];
+            load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, args.out_dtype, vec);
+            load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, args.out_dtype,
+                       vec);
+            float dh[32], dg[32];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                u[j] = round_to(__uint_as_float(ru[j]), args.out_dtype);
-                g[j] = round_to(__uint_as_float(rg[j]), args.out_dtype);
-                const float s = round_to(silu_f32(g[j]), args.out_dtype);
-                h[j] = s * u[j];
-              }
-              store_chunk(args.out, out_row * args.ldo_m, 1, col0, ncols, h, args.out_dtype, args.vec_ok);
-              if (args.out2 != nullptr) {
-                store_chunk(args.out2, out_row * args.ldo2, 1, col0, ncols, u, args.out_dtype, args.vec_ok);
-                store_chunk(args.out2, out_row * args.ldo2, 1, args.swiglu_half + col0, ncols, g, args.out_dtype,
-                            args.vec_ok);
-              }
+            for (int j = 0; j < 32; ++j) {
+              const float da = round_to(__uint_as_float(r[j]), args.out_dtype);
+              const float sig = sigmoid_fast(gv[j]);
+              const float sl = round_to(gv[j] * sig, args.out_dtype);
+              dh[j] = da * sl;
+              const float tt = round_to(da * hv[j], args.out_dtype);
+              dg[j] = tt * (sig * (1.0f + gv[j] * (1.0f - sig)));
             }
+            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, dh, args.out_dtype, vec, stg);
+            emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, dg, args.out_dtype,
+                       vec, stg);
           }
         } else {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = 0; c < BN / 64; ++c) {
+            const int lc = half * (BN / 2) + c * 32;
             uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + c * 32, r);
+            tmem_ld_32x32b_x32(t_row + lc, r);
             tc_wait_ld();
-            const int col0 = ti.nt * BN + c * 32;
+            const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
-            if (valid && ncols > 0) {
-              float v[32];
+            if (ncols <= 0) continue;
+            float v[32];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-              if (args.bias != nullptr) {
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (args.bias != nullptr && valid) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  if (j < ncols) {
-                    const int64_t bi = ti.e * args.bias_se + (int64_t)(col0 + j) * args.bias_sn;
-                    float b;
-                    if (args.out_dtype == ZS_BF16)
-                      b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi]);
-                    else if (args.out_dtype == ZS_F16)
-                      b = __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
-                    else
-                      b = reinterpret_cast<const float*>(args.bias)[bi];
-                    v[j] += b;
-                  }
+              for (int j = 0; j < 32; ++j) {
+                if (j < ncols) {
+                  const int64_t bi = ti.e * args.bias_se + (int64_t)(col0 + j) * args.bias_sn;
+                  float b;
+                  if (args.out_dtype == ZS_BF16)
+                    b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi]);
+                  else if (args.out_dtype == ZS_F16)
+                    b = __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
+                  else
+                    b = reinterpret_cast<const float*>(args.bias)[bi];
+                  v[j] += b;
                 }
               }
-              store_chunk(args.out, out_row * args.ldo_m, args.ldo_n, col0, ncols, v, args.out_dtype, args.vec_ok);
             }
+            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, v, args.out_dtype, vec, stg);
           }
         }
       } else {
         const int m = ti.mt * BM + row_in_tile;
         const bool valid = m < args.M_xty;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < BN / 64; ++c) {
+          const int lc = half * (BN / 2) + c * 32;
           uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_32x32b_x32(t_row + lc, r);
           tc_wait_ld();
-          const int col0 = ti.nt * BN + c * 32;
+          const int col0 = ti.nt * BN + lc;
           const int ncols = min(32, args.N_out - col0);
-          if (valid && ncols > 0) {
-            float v[32];
+          if (ncols <= 0) continue;
+          float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, args.ldo_n, col0, ncols, v,
-                        args.out_dtype, args.vec_ok);
-          }
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          emit_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, valid, v, args.out_dtype,
+                     vec, stg);
         }
       }
       tc_fence_before();
@@ -595,7 +698,7 @@ static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
   int64_t grid = num_sms();
   if (max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, 192, L::ALLOC, stream>>>(tmA, tmB, args);
+  kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, args);
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
 }
@@ -813,4 +916,48 @@ extern "C" int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64
              ((F * es) % 16 == 0);
   const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
   return launch_gemm<BN, 4, false, false, EPI_SWIGLU>(tmA, tmB, a, max_tiles, stream);
+}
+
+extern "C" int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const void* W2, int64_t num_experts, int64_t K,
+                                      int64_t F, const void* dyg, int64_t dyg_sm, const int64_t* sorted_expert_idxs,
+                                      const int64_t* expert_offsets, int64_t n, int dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(dhfull && hfull && W2 && dyg && (sorted_expert_idxs || expert_offsets), ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && F >= 1 && n >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && F < (int64_t)1 << 23, ZS_ERR_SHAPE);
+  ZS_REQUIRE(num_experts * K < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  if (n == 0) return ZS_OK;
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, dyg, dtype, (uint64_t)K, (uint64_t)n, (uint64_t)dyg_sm * es, 64, 128);
+  if (rc != ZS_OK) return rc;
+  // W2 [E, K, F] viewed as [E*K rows, F cols]: MN-major B (F contiguous)
+  rc = make_tmap(&tmB, W2, dtype, (uint64_t)F, (uint64_t)(num_experts * K), (uint64_t)F * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+  GemmArgs a{};
+  a.mode = MODE_ROWS;
+  a.num_experts = (int)num_experts;
+  a.n_tiles = (int)((F + BN - 1) / BN);
+  a.kb_rows = (int)((K + BK - 1) / BK);
+  a.N_out = (int)F;
+  a.ab_fmt = dtype == ZS_BF16 ? 1 : 0;
+  a.n_rows = n;
+  a.out_rows = n;
+  a.expert_offsets = expert_offsets;
+  a.sorted_expert_idxs = sorted_expert_idxs;
+  a.out = reinterpret_cast<char*>(dhfull);
+  a.ldo_m = 2 * F;
+  a.ldo_n = 1;
+  a.aux = reinterpret_cast<const char*>(hfull);
+  a.ld_aux = 2 * F;
+  a.swiglu_half = (int)F;
+  a.out_dtype = dtype;
+  a.b_rows_per_expert = (int)K;
+  a.vec_ok = ((reinterpret_cast<uintptr_t>(dhfull) | reinterpret_cast<uintptr_t>(hfull)) % 16 == 0) &&
+             ((F * es) % 16 == 0);
+  const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
+  return launch_gemm<BN, 4, false, true, EPI_DSWIGLU>(tmA, tmB, a, max_tiles, stream);
 }

@@ -180,23 +180,42 @@ __global__ void fsc_hist_kernel(const int64_t* __restrict__ ids, int64_t n, int 
 }
 
 // Phase B (one block): turn hist[blk][b] into the global start of bucket b's
-// slice for block blk, and write the inclusive expert offsets.
-__global__ void fsc_scan_kernel(int* __restrict__ hist, int nblk, int E, int64_t* __restrict__ offsets) {
-  extern __shared__ int sh[];  // totals[B], then scan scratch
+// slice for block blk, and write the inclusive expert offsets.  The histogram
+// is staged in shared memory when it fits (coalesced load, no dependent
+// global-memory chains).
+__global__ void fsc_scan_kernel(int* __restrict__ hist, int nblk, int E, int64_t* __restrict__ offsets,
+                                int staged) {
+  extern __shared__ int sh[];  // totals[B] (+ staged hist[nblk][B])
   const int B = E + 1;
+  int* h = staged ? sh + B : hist;
+  if (staged) {
+    for (int i = threadIdx.x; i < nblk * B; i += blockDim.x) h[i] = hist[i];
+    __syncthreads();
+  }
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     int run = 0;
     for (int blk = 0; blk < nblk; ++blk) {
-      const int c = hist[(int64_t)blk * B + b];
-      hist[(int64_t)blk * B + b] = run;
+      const int c = h[blk * B + b];
+      h[blk * B + b] = run;
       run += c;
     }
     sh[b] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int b = 0; b < B; ++b) {
+  // exclusive scan of the bucket totals (one warp; B <= 4097)
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int per = (B + 31) / 32;
+    const int beg = lane * per, end = min(beg + per, B);
+    int local = 0;
+    for (int b = beg; b < end; ++b) local += sh[b];
+    int incl = local;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int run = incl - local;
+    for (int b = beg; b < end; ++b) {
       const int c = sh[b];
       sh[b] = run;
       run += c;
@@ -204,10 +223,7 @@ __global__ void fsc_scan_kernel(int* __restrict__ hist, int nblk, int E, int64_t
     }
   }
   __syncthreads();
-  for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const int base = sh[b];
-    for (int blk = 0; blk < nblk; ++blk) hist[(int64_t)blk * B + b] += base;
-  }
+  for (int i = threadIdx.x; i < nblk * B; i += blockDim.x) hist[i] = h[i] + sh[i % B];
 }
 
 // Phase C: stable scatter.  Each block walks its chunk in order, 256 ids per
@@ -353,7 +369,13 @@ extern "C" int zs_flatten_sort_count(const int64_t* expert_idxs, int64_t n, int 
   int* hist = reinterpret_cast<int*>(workspace);
   fsc_hist_kernel<<<nblk, FSC_THREADS, B * sizeof(int), stream>>>(expert_idxs, n, num_experts, hist);
   ZS_CUDA_TRY(cudaGetLastError());
-  fsc_scan_kernel<<<1, 1024, B * sizeof(int), stream>>>(hist, nblk, num_experts, expert_offsets);
+  const size_t scan_sh = (size_t)B * sizeof(int) * (1 + nblk);
+  const int staged = scan_sh <= 96 * 1024;
+  if (staged && scan_sh > 48 * 1024) {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(fsc_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_sh));
+  }
+  fsc_scan_kernel<<<1, 1024, staged ? scan_sh : B * sizeof(int), stream>>>(hist, nblk, num_experts, expert_offsets,
+                                                                           staged);
   ZS_CUDA_TRY(cudaGetLastError());
   const size_t sh = (size_t)B * sizeof(int) * (1 + FSC_THREADS / 32);
   if (sh > 48 * 1024) {

@@ -76,7 +76,8 @@ def scatter2scatter(X, W, sorted_expert_idxs, sorted_scattered_idxs, k, b=None, 
     return output
 
 
-def _launch_scatter2scatter(output, W, X, k, sei, ssi, b, x_grouped, y_grouped, expert_offsets=None):
+def _launch_scatter2scatter(output, W, X, k, sei, ssi, b, x_grouped, y_grouped, expert_offsets=None,
+                            tag="scatter2scatter"):
     Z.require_cuda(output, W, X, sei, ssi, b)
     mdt = _mma_dtype(X)
     Xc = _as(X, mdt)
@@ -96,7 +97,7 @@ def _launch_scatter2scatter(output, W, X, k, sei, ssi, b, x_grouped, y_grouped, 
     ws_bytes = Z.lib().zs_scatter2scatter_workspace(n, K, code, int(bool(x_grouped)))
     ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=X.device)
     Z.count(1 if x_grouped else 2)
-    with Z.timed("scatter2scatter"):
+    with Z.timed(tag):
       Z.check(Z.lib().zs_scatter2scatter(
         out.data_ptr(), out.stride(0), Wc.data_ptr(), E, K, N, Wc.stride(0), Wc.stride(1), Wc.stride(2),
         Xc.data_ptr(), Xc.size(0), Xc.stride(0),
@@ -121,11 +122,14 @@ def _(output, W, X, k, sorted_expert_idxs, sorted_scattered_idxs, b, x_grouped, 
 
 # ------------------------------------------------------------------------ groupXtY
 
-def group_bwd_W(DY, X, expert_offsets, E, has_bias=False):
-    DWt = torch.zeros((E, DY.size(-1), X.size(-1)), device=DY.device, dtype=DY.dtype)
+def group_bwd_W(DY, X, expert_offsets, E, has_bias=False, tag="groupXtY"):
+    # The kernel writes every element (zeros for experts without rows), so
+    # the outputs need no zero fill.
+    DWt = torch.empty((E, DY.size(-1), X.size(-1)), device=DY.device, dtype=DY.dtype)
     DW = DWt.permute(0, 2, 1)
-    Db = torch.zeros((E, DY.size(-1)), device=DY.device, dtype=DY.dtype) if has_bias else None
-    groupXtY_compileable(E, DW, Db, DY, X, expert_offsets)
+    Db = torch.empty((E, DY.size(-1)), device=DY.device, dtype=DY.dtype) if has_bias else None
+    with Z.timed(tag):
+        groupXtY_compileable(E, DW, Db, DY, X, expert_offsets)
     return DW, Db
 
 
@@ -149,8 +153,7 @@ def groupXtY_compileable(E: int, DW: torch.Tensor, Db: Optional[torch.Tensor], D
     n, K = Xc.shape
     N = DYc.size(1)
     Z.count(1 if Dbo is None else 2)
-    with Z.timed("groupXtY"):
-      Z.check(Z.lib().zs_group_xty(
+    Z.check(Z.lib().zs_group_xty(
         int(E), DWo.data_ptr(), DWo.stride(0), DWo.stride(1), DWo.stride(2),
         Z.ptr(Dbo), Dbo.stride(0) if Dbo is not None else 0, Dbo.stride(1) if Dbo is not None else 0,
         DYc.data_ptr(), DYc.stride(0), Xc.data_ptr(), Xc.stride(0), n, K, N, offs.data_ptr(),

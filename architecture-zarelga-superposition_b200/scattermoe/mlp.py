@@ -9,7 +9,8 @@ GLUMLP.forward runs one autograd function whose forward is
   sort -> gather -> grouped GEMM with SwiGLU fused in its epilogue ->
   grouped GEMM scattered to (token, slot) rows -> gate-weighted combine
 and whose backward is the reference's ParallelLinear backward for both
-projections with the SwiGLU backward in between.
+projections, with the SwiGLU backward fused into the epilogue of the
+down-projection's input-gradient GEMM.
 """
 from __future__ import annotations
 
@@ -53,6 +54,21 @@ def up_swiglu(xg, W1, sorted_expert_idxs, expert_offsets):
     return act, hfull
 
 
+def down_dswiglu(dyg, W2, hfull, sorted_expert_idxs, expert_offsets):
+    """d[h | g] [n, 2f] of the SwiGLU input from the gate-scaled grouped output
+    gradient, in one grouped GEMM whose epilogue applies the SwiGLU backward."""
+    n, d = dyg.shape
+    E, _, f = W2.shape
+    dh = torch.empty((n, 2 * f), dtype=dyg.dtype, device=dyg.device)
+    Z.count(1)
+    with Z.timed("down_dx"):
+        Z.check(Z.lib().zs_expert_down_dswiglu(dh.data_ptr(), hfull.data_ptr(), W2.data_ptr(), E, d, f,
+                                               dyg.data_ptr(), dyg.stride(0), sorted_expert_idxs.data_ptr(),
+                                               expert_offsets.data_ptr(), n, Z.dtype_code(dyg.dtype),
+                                               Z.stream_of(dyg)), "zs_expert_down_dswiglu")
+    return dh
+
+
 def swiglu_backward(dact, hfull):
     n, f = dact.shape
     dh = torch.empty((n, 2 * f), dtype=dact.dtype, device=dact.device)
@@ -77,7 +93,7 @@ class GLUExpertsFunction(torch.autograd.Function):
         act, hfull = up_swiglu(xg, W1c, sei, offs)
         y_rows = torch.empty((T * k, W2c.size(1)), dtype=cdt, device=x.device)
         ops._launch_scatter2scatter(y_rows, W2c.permute(0, 2, 1), act, 1, sei, ssi, None, True, False,
-                                    expert_offsets=offs)
+                                    expert_offsets=offs, tag="down_fwd")
         y = weighted_row_sum(y_rows, pc, T, k)
         ctx.save_for_backward(xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c)
         ctx.meta = (x.dtype, expert_p.dtype, W1.dtype, W2.dtype, num_experts, k, T)
@@ -92,13 +108,12 @@ class GLUExpertsFunction(torch.autograd.Function):
         d = dyc.size(1)
         d_p = ops.rowwise_sum_product(y_rows.view(T, k, d), dyc, dtype=p_dt)
         dyg = ops.group(dyc, ssi, fan_out=k, coeff=pc.flatten())
-        dact = torch.empty_like(act)
-        ops._launch_scatter2scatter(dact, W2c, dyg, 1, sei, ssi, None, True, True, expert_offsets=offs)
-        dW2, _ = ops.group_bwd_W(dyg, act, offs, E)             # [E, f, d] view of [E, d, f]
-        dhfull = swiglu_backward(dact, hfull)
-        dW1, _ = ops.group_bwd_W(dhfull, xg, offs, E)           # [E, d, 2f] view of [E, 2f, d]
+        dhfull = down_dswiglu(dyg, W2c, hfull, sei, offs)
+        dW2, _ = ops.group_bwd_W(dyg, act, offs, E, tag="down_dw")   # [E, f, d] view of [E, d, f]
+        dW1, _ = ops.group_bwd_W(dhfull, xg, offs, E, tag="up_dw")   # [E, d, 2f] view of [E, 2f, d]
         dx_rows = torch.empty((T * k, xg.size(1)), dtype=cdt, device=dy.device)
-        ops._launch_scatter2scatter(dx_rows, W1c, dhfull, 1, sei, ssi, None, True, False, expert_offsets=offs)
+        ops._launch_scatter2scatter(dx_rows, W1c, dhfull, 1, sei, ssi, None, True, False, expert_offsets=offs,
+                                    tag="up_dx")
         dx = weighted_row_sum(dx_rows, None, T, k)
         return (dx.to(x_dt), d_p, None, dW1.permute(0, 2, 1).to(w1_dt), dW2.permute(0, 2, 1).to(w2_dt), None,
                 None)

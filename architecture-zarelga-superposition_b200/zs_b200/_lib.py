@@ -43,6 +43,7 @@ _SIGNATURES = {
     "zs_weighted_row_sum": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i64, _i32, _vp]),
     "zs_expert_up_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
     "zs_swiglu_backward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
+    "zs_expert_down_dswiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
 }
 
 

@@ -154,7 +154,7 @@ def run_reference(args):
 # ---------------------------------------------------------------- GPU arm
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -168,12 +168,13 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
+        """Summarise the samples taken between host times t0 and t1."""
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -188,10 +189,14 @@ class ClockSampler:
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk, cmax = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
+            if t0 is not None and not (t0 <= ts <= t1):
+                continue
+            sm.append(clk)
+            mx = max(mx, cmax)
             for nm, v in zip(names, parts[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
@@ -217,7 +222,9 @@ def run_gpu(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
-    c = CFG
+    c = dict(CFG)
+    if args.tokens:
+        c["T"] = args.tokens
     T, d, E, k, f = c["T"], c["d"], c["E"], c["k"], c["f"]
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     bf = torch.bfloat16
@@ -258,7 +265,7 @@ def run_gpu(args):
 
     sampler = ClockSampler(local)
     sampler.start()
-    time.sleep(0.3)
+    time.sleep(0.5)  # let nvidia-smi start sampling
     Z.INSTR.events = {}
     Z.INSTR.timing = True
     launches0 = Z.INSTR.launches
@@ -267,15 +274,17 @@ def run_gpu(args):
     t_end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier()
+    host_t0 = time.time()
     t_start.record(stream)
     for _ in range(args.steps):
         step(x.detach(), logits.detach(), dy)
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
+    host_t1 = time.time()
     Z.INSTR.timing = False
     launches = Z.INSTR.launches - launches0
-    clocks = sampler.stop()
+    clocks = sampler.stop(host_t0, host_t1)
     ms = t_start.elapsed_time(t_end)
     if world > 1:
         tt = torch.tensor([ms], device=dev)
@@ -297,7 +306,7 @@ def run_gpu(args):
     xd = torch.empty_like(x)
     ld = torch.empty_like(logits)
     dyd = torch.empty_like(dy)
-    e_steps = max(1, args.steps)
+    e_steps = 0 if args.no_e2e else max(1, args.steps)
     torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -311,7 +320,7 @@ def run_gpu(args):
         dxh.copy_(dx, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
+    e_ms = max(e0.elapsed_time(e1), 1e-9)
     if world > 1:
         tt = torch.tensor([e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -346,13 +355,15 @@ def run_gpu(args):
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside the step loop)",
                          "kernels": kern},
             "cpu_baseline": None,
-            "e2e": {"value": world * T * e_steps / (e_ms * 1e-3), "unit": UNIT,
+            "e2e": None if not e_steps else {"value": world * T * e_steps / (e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": xh.numel() * 2 + lh.numel() * 2 + dyh.numel() * 2,
                     "d2h_bytes_per_step": dxh.numel() * 2},
             "gpu_launches": launches,
             "clocks": clocks,
             "device_error": err,
         }
+        if args.tokens and args.tokens != CFG["T"]:
+            line["config"]["workload"] = WORKLOAD.replace("T=16384", f"T={T} (reduced)")
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -364,10 +375,12 @@ def run_gpu(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="zs", choices=["zs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: config 2's 16384)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -194,6 +194,20 @@ int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64_t num_expe
 int zs_swiglu_backward(void* dhfull, const void* dact, const void* hfull, int64_t n, int64_t F, int dtype,
                        void* stream);
 
+/*
+ * GLUMLP down-projection input gradient with the SwiGLU backward fused into
+ * the GEMM epilogue (ParallelLinear.backward's grouped scatter2scatter with
+ * the transposed weight, scattermoe/parallel_experts.py:112-120, followed by
+ * the autograd of scattermoe/mlp.py:87):
+ *   dact[i, :]  = dyg[i, :] @ W2[e_i]                 (never stored)
+ *   dhfull[i,:] = zs_swiglu_backward(dact, hfull) rows
+ * W2: output_experts.weight [E, K, F] contiguous (K = d_model); dyg: grouped
+ * gate-scaled output gradient [n, K], row stride dyg_sm; hfull/dhfull [n, 2F].
+ */
+int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const void* W2, int64_t num_experts, int64_t K, int64_t F,
+                           const void* dyg, int64_t dyg_sm, const int64_t* sorted_expert_idxs,
+                           const int64_t* expert_offsets, int64_t n, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

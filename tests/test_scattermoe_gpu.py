@@ -203,8 +203,8 @@ def test_glumlp_config2_full_size():
     m, x, p, idx, dy = _glu_case(T, d, E, k, f, seed=2, skew=0.5)
     y = m(x, p, idx)
     y.backward(dy)
-    W1 = m.experts.weight.float()
-    W2 = m.output_experts.weight.float()
+    W1 = m.experts.weight.detach().float()
+    W2 = m.output_experts.weight.detach().float()
     xf, pf, dyf = x.detach().float(), p.detach().float(), dy.float()
     # f32 reference with autograd
     xr = xf.clone().requires_grad_(True)
@@ -228,5 +228,45 @@ def test_glumlp_config2_full_size():
     assert cosine(p.grad, pr.grad) > 0.999
     assert cosine(m.experts.weight.grad, W1r.grad) > 0.999
     assert cosine(m.output_experts.weight.grad, W2r.grad) > 0.999
+    from zs_b200 import device_error
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize("n_per,E,d,f", [(50, 6, 64, 48), (700, 8, 256, 192), (2000, 64, 1024, 512)])
+def test_up_swiglu_and_down_dswiglu_kernels(n_per, E, d, f):
+    """The fused-epilogue GEMMs against the oracle's SwiGLU forward/backward."""
+    from scattermoe.mlp import down_dswiglu, up_swiglu
+
+    g = torch.Generator(device="cuda").manual_seed(n_per + f)
+    counts = torch.randint(0, 2 * n_per, (E,), device="cuda", generator=g)
+    counts[1] = 0
+    off = counts.cumsum(0)
+    n = int(off[-1])
+    sei = torch.repeat_interleave(torch.arange(E, device="cuda"), counts)
+    xg = torch.randn(n, d, device="cuda", generator=g).to(BF)
+    W1 = (torch.randn(E, 2 * f, d, device="cuda", generator=g) * 0.05).to(BF)
+    W2 = (torch.randn(E, d, f, device="cuda", generator=g) * 0.05).to(BF)
+    act, hfull = up_swiglu(xg, W1, sei, off)
+    hf_ref = np.zeros((n, 2 * f))
+    sei_np = sei.cpu().numpy()
+    xg_np, W1_np, W2_np = bf16_exact(xg), bf16_exact(W1), bf16_exact(W2)
+    for e in range(E):
+        m = sei_np == e
+        hf_ref[m] = xg_np[m].astype(np.float64) @ W1_np[e].T.astype(np.float64)
+    assert rel_err(hfull, hf_ref) < TOL
+    hf = hfull.float().cpu().numpy().astype(np.float64)
+    h, gt = hf[:, :f], hf[:, f:]
+    act_ref = h * gt / (1 + np.exp(-gt))
+    assert rel_err(act, act_ref) < TOL
+    dyg = torch.randn(n, d, device="cuda", generator=g).to(BF)
+    dh = down_dswiglu(dyg, W2, hfull, sei, off)
+    dyg_np = bf16_exact(dyg).astype(np.float64)
+    dact = np.zeros((n, f))
+    for e in range(E):
+        m = sei_np == e
+        dact[m] = dyg_np[m] @ W2_np[e].astype(np.float64)
+    sg = 1 / (1 + np.exp(-gt))
+    ref = np.concatenate([dact * gt * sg, dact * h * sg * (1 + gt * (1 - sg))], axis=1)
+    assert rel_err(dh, ref) < TOL
     from zs_b200 import device_error
     assert device_error() == 0
