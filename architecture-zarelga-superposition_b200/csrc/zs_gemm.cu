@@ -79,7 +79,8 @@ struct Smem {
   static constexpr int OFF_MISC = OFF_BARS + NUM_BARS * 8;  // tmem addr, abort flag
   static constexpr int OFF_TPREFIX = OFF_MISC + 16;
   static constexpr int OFF_RSTART = OFF_TPREFIX + (MAX_EXPERTS_GEMM + 1) * 4;
-  static constexpr int OFF_STG = ((OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4 + 15) / 16) * 16;
+  static constexpr int OFF_ORDER = OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4;
+  static constexpr int OFF_STG = ((OFF_ORDER + (MAX_EXPERTS_GEMM + 1) * 4 + 15) / 16) * 16;
   static constexpr int TOTAL = OFF_STG + 8 * 32 * 80;
   static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
 };
@@ -103,8 +104,11 @@ __device__ __forceinline__ int64_t lower_bound_i64(const int64_t* a, int64_t n, 
   return lo;
 }
 
+// Tiles are numbered expert by expert in the order order[0..E); tprefix[p] is
+// the first tile of the expert at position p.
 template <int BN>
-__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const int* tprefix, const int* rstart) {
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const int* tprefix, const int* rstart,
+                                                const int* order) {
   TileInfo ti;
   int lo = 0, hi = a.num_experts;
   while (hi - lo > 1) {
@@ -114,8 +118,9 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const 
     else
       hi = mid;
   }
+  const int local = t - tprefix[lo];
+  lo = order[lo];
   ti.e = lo;
-  int local = t - tprefix[lo];
   ti.mt = local / a.n_tiles;
   ti.nt = local - ti.mt * a.n_tiles;
   if (a.mode == MODE_ROWS) {
@@ -204,6 +209,42 @@ __device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0,
   }
 }
 
+// The gate half [swiglu_half + col0, +32) of this lane's saved row, raw.
+__device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&w)[4]) {
+  ok = ok && col0 + 32 <= a.N_out;
+  const uint4* p = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + a.swiglu_half + col0) * 2);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
+}
+
+// Element j (compile-time after unrolling) of 32 packed 16-bit values, as f32.
+__device__ __forceinline__ float elem16(const uint4 (&w)[4], int j, int dtype) {
+  const uint4& q = w[j >> 3];
+  const int k = (j & 7) >> 1;
+  const uint32_t u = k == 0 ? q.x : (k == 1 ? q.y : (k == 2 ? q.z : q.w));
+  const uint16_t b = (j & 1) ? (uint16_t)(u >> 16) : (uint16_t)(u & 0xffffu);
+  if (dtype == ZS_F16) return __half2float(__ushort_as_half(b));
+  return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// 4 x 16 bytes of 16-bit values -> 32 f32.
+__device__ __forceinline__ void unpack32(const uint4 (&w)[4], float (&v)[32], int dtype) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t u[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float2 f;
+      if (dtype == ZS_F16)
+        f = __half22float2(*reinterpret_cast<const __half2*>(&u[h]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[h]));
+      v[q * 8 + 2 * h] = f.x;
+      v[q * 8 + 2 * h + 1] = f.y;
+    }
+  }
+}
+
 // Read 32 consecutive 16-bit columns of this lane's row as f32.
 __device__ __forceinline__ void load_chunk(const char* src, int64_t row_off, int col0, int ncols, bool valid,
                                            float (&v)[32], int dtype, bool vec) {
@@ -266,6 +307,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   int* s_tprefix = reinterpret_cast<int*>(smem + L::OFF_TPREFIX);
   int* s_rstart = reinterpret_cast<int*>(smem + L::OFF_RSTART);
+  int* s_order = reinterpret_cast<int*>(smem + L::OFF_ORDER);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -306,12 +348,32 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     s_rstart[e] = (int)s;
   }
   __syncthreads();
+  // Expert order.  MODE_XTY tiles cost in proportion to their expert's rows
+  // and the loads are skewed, so the weight-gradient tiles go largest expert
+  // first (greedy longest-first over the persistent CTAs); MODE_ROWS tiles
+  // all cost the same and keep expert order.
+  const bool lpt = args.mode == MODE_XTY && E <= 256;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    if (lpt) {
+      const int ce = max(s_rstart[e + 1] - s_rstart[e], 0);
+      int rank = 0;
+      for (int j = 0; j < E; ++j) {
+        const int cj = max(s_rstart[j + 1] - s_rstart[j], 0);
+        rank += (cj > ce) || (cj == ce && j < e);
+      }
+      s_order[rank] = e;
+    } else {
+      s_order[e] = e;
+    }
+  }
+  __syncthreads();
   if (warp == 0) {
     const int per = (E + 31) / 32;
     const int beg = lane * per;
     const int end = min(beg + per, E);
     int local = 0;
-    for (int e = beg; e < end; ++e) {
+    for (int p = beg; p < end; ++p) {
+      const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
       local += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
     }
@@ -322,8 +384,9 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       if (lane >= off) incl += v;
     }
     int run = incl - local;
-    for (int e = beg; e < end; ++e) {
-      s_tprefix[e] = run;
+    for (int p = beg; p < end; ++p) {
+      s_tprefix[p] = run;
+      const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
       run += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
     }
@@ -348,7 +411,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       uint32_t issued_parity = 0;     // parity of the last load per stage
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+        const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
         for (int kb = 0; kb < ti.nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -404,7 +467,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     const uint32_t idesc = args.ab_fmt ? IDESC_BF16 : IDESC_F16;
     bool issued_any = false;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
       if (ti.nkb == 0) continue;
       const uint32_t buf = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
@@ -487,7 +550,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     const bool vec = args.vec_ok && args.out_dtype != ZS_F32;
     uint32_t acc_iter = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart);
+      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
       if (args.mode == MODE_XTY && ti.nkb == 0) {
         // Expert without rows: its weight gradient is zero.
         const int m = ti.mt * BM + row_in_tile;
@@ -505,21 +568,25 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       }
       const uint32_t buf = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      // Row bookkeeping and (EPI_DSWIGLU) the saved-activation loads do not
+      // depend on the accumulator: issue them before waiting for the MMA.
+      const int row = ti.r0 + row_in_tile;
+      int64_t out_row = row;
+      bool valid = args.mode == MODE_ROWS && row < ti.r1;
+      if (valid && args.row_map != nullptr) {
+        out_row = __ldg(args.row_map + row);
+        if (out_row < 0 || out_row >= args.out_rows) {
+          record_error(ZS_DEVERR_INDEX);
+          valid = false;
+        }
+      }
+      uint4 gcur[4];
+      if (EPI == EPI_DSWIGLU) prefetch_chunk(args, out_row, ti.nt * BN + half * (BN / 2), valid && vec, gcur);
       if (!warp_wait(&tfull[buf], acc_phase, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
 
       if (args.mode == MODE_ROWS) {
-        const int row = ti.r0 + row_in_tile;
-        int64_t out_row = row;
-        bool valid = row < ti.r1;
-        if (valid && args.row_map != nullptr) {
-          out_row = __ldg(args.row_map + row);
-          if (out_row < 0 || out_row >= args.out_rows) {
-            record_error(ZS_DEVERR_INDEX);
-            valid = false;
-          }
-        }
         if (EPI == EPI_SWIGLU) {
           // D columns [0, BN/2) hold the "up" half, [BN/2, BN) the "gate"
           // half; this warp produces activation columns [h*BN/4, (h+1)*BN/4).
@@ -549,33 +616,63 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           }
         } else if (EPI == EPI_DSWIGLU) {
           // The accumulator is d(act) for activation columns; combine it with
-          // the saved pre-activation [h | g] into d[h | g].
+          // the saved pre-activation [h | g] into d[h | g].  The gate half of
+          // the next chunk is fetched while this one is processed.
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
             const int lc = half * (BN / 2) + c * 32;
+            uint4 gnext[4];
+            prefetch_chunk(args, out_row, ti.nt * BN + lc + 32, valid && vec && c + 1 < BN / 64, gnext);
             uint32_t r[32];
             tmem_ld_32x32b_x32(t_row + lc, r);
             tc_wait_ld();
             const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
             if (ncols <= 0) continue;
-            float hv[32], gv[32];
-            load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, args.out_dtype, vec);
-            load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, args.out_dtype,
-                       vec);
-            float dh[32], dg[32];
+            float o[32];
+#define ZS_DV(j) round_to(__uint_as_float(r[j]), args.out_dtype)
+            if (vec && ncols == 32) {
+              // h is read now; its latency overlaps the d(h) half below.
+              uint4 hraw[4];
+              const uint4* ph = reinterpret_cast<const uint4*>(args.aux + (out_row * args.ld_aux + col0) * 2);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float da = round_to(__uint_as_float(r[j]), args.out_dtype);
-              const float sig = sigmoid_fast(gv[j]);
-              const float sl = round_to(gv[j] * sig, args.out_dtype);
-              dh[j] = da * sl;
-              const float tt = round_to(da * hv[j], args.out_dtype);
-              dg[j] = tt * (sig * (1.0f + gv[j] * (1.0f - sig)));
+              for (int q = 0; q < 4; ++q) hraw[q] = valid ? __ldg(ph + q) : make_uint4(0, 0, 0, 0);
+              // d(h) = d(act) * silu(g)
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float gj = elem16(gcur, j, args.out_dtype);
+                o[j] = ZS_DV(j) * round_to(gj * sigmoid_fast(gj), args.out_dtype);
+              }
+              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, args.out_dtype, vec, stg);
+              // d(g) = (d(act) * h) * silu'(g)
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float gj = elem16(gcur, j, args.out_dtype);
+                const float hj = elem16(hraw, j, args.out_dtype);
+                const float sig = sigmoid_fast(gj);
+                o[j] = round_to(ZS_DV(j) * hj, args.out_dtype) * (sig * (1.0f + gj * (1.0f - sig)));
+              }
+              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, args.out_dtype,
+                         vec, stg);
+            } else {
+              float hv[32], gv[32];
+              load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, args.out_dtype, vec);
+              load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, args.out_dtype,
+                         vec);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] = ZS_DV(j) * round_to(gv[j] * sigmoid_fast(gv[j]), args.out_dtype);
+              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, args.out_dtype, vec, stg);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float sig = sigmoid_fast(gv[j]);
+                o[j] = round_to(ZS_DV(j) * hv[j], args.out_dtype) * (sig * (1.0f + gv[j] * (1.0f - sig)));
+              }
+              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, args.out_dtype,
+                         vec, stg);
             }
-            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, dh, args.out_dtype, vec, stg);
-            emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, dg, args.out_dtype,
-                       vec, stg);
+#undef ZS_DV
+#pragma unroll
+            for (int q = 0; q < 4; ++q) gcur[q] = gnext[q];
           }
         } else {
 #pragma unroll 1

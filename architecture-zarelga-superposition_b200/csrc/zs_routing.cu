@@ -424,3 +424,77 @@ extern "C" int zs_bias_sign_update(const int64_t* counts, int num_experts, float
                                                                              expert_biases);
   return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
 }
+
+namespace zs {
+// Gradient of topk_weight = L1-normalise(gate_probs[topk_idx]) with respect to
+// gate_probs (the differentiable half of modeling/moe_gate.py:33-34):
+//   s = sum_j |p_j|, D = max(s, eps)
+//   dp_j = g_j / D - [s > eps] * sign(p_j) * (sum_i g_i p_i) / D^2
+// scattered into a zero row of grad_probs [T, E].  One warp per token, f32.
+template <typename T, typename G>
+__global__ void gate_topk_backward_kernel(const T* __restrict__ probs, const int64_t* __restrict__ idx,
+                                          const G* __restrict__ grad_w, T* __restrict__ grad_probs, int64_t num_tokens,
+                                          int E, int k) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tokens; t += warps) {
+    int e = -1;
+    float p = 0.f, g = 0.f;
+    if (lane < k) {
+      e = (int)idx[t * k + lane];
+      if (e < 0 || e >= E) {
+        record_error(ZS_DEVERR_INDEX);
+        e = -1;
+      } else {
+        p = to_f32<T>(probs[t * E + e]);
+        g = to_f32<G>(grad_w[t * k + lane]);
+      }
+    }
+    float s = fabsf(p), dot = g * p;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      s += __shfl_xor_sync(0xffffffffu, s, off);
+      dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    }
+    const float eps = 1e-12f;
+    const float D = fmaxf(s, eps);
+    const float sg = p > 0.f ? 1.f : (p < 0.f ? -1.f : 0.f);
+    const float dp = g / D - (s > eps ? sg * dot / (D * D) : 0.f);
+    for (int c = lane; c < E; c += 32) {
+      float v = 0.f;
+      for (int j = 0; j < k; ++j) {
+        const int ej = __shfl_sync(0xffffffffu, e, j);
+        const float dj = __shfl_sync(0xffffffffu, dp, j);
+        if (ej == c) v += dj;
+      }
+      grad_probs[t * E + c] = from_f32<T>(v);
+    }
+  }
+}
+}  // namespace zs
+
+extern "C" int zs_moe_gate_topk_backward(const void* gate_probs, int probs_dtype, const int64_t* topk_idx,
+                                         const void* grad_weight, int grad_dtype, int64_t num_tokens, int num_experts,
+                                         int top_k, void* grad_probs, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(gate_probs && topk_idx && grad_weight && grad_probs, ZS_ERR_ARG);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= 1024 && top_k >= 1 && top_k <= 32 && num_tokens >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(grad_dtype == probs_dtype, ZS_ERR_DTYPE);
+  if (num_tokens == 0) return ZS_OK;
+  int64_t blocks = (num_tokens + 7) / 8;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+#define ZS_GB(T)                                                                                                   \
+  gate_topk_backward_kernel<T, T><<<(unsigned)blocks, 256, 0, stream>>>(                                           \
+      reinterpret_cast<const T*>(gate_probs), topk_idx, reinterpret_cast<const T*>(grad_weight),                   \
+      reinterpret_cast<T*>(grad_probs), num_tokens, num_experts, top_k)
+  if (probs_dtype == ZS_F32)
+    ZS_GB(float);
+  else if (probs_dtype == ZS_BF16)
+    ZS_GB(__nv_bfloat16);
+  else if (probs_dtype == ZS_F16)
+    ZS_GB(__half);
+  else
+    return ZS_ERR_DTYPE;
+#undef ZS_GB
+  return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
+}

@@ -38,7 +38,7 @@ class GateTopK(torch.autograd.Function):
     @staticmethod
     def forward(ctx, gate_probs, expert_biases, top_k):
         idx, w = gate_topk(gate_probs, expert_biases, top_k)
-        ctx.save_for_backward(gate_probs, idx)
+        ctx.save_for_backward(gate_probs.contiguous(), idx)
         ctx.mark_non_differentiable(idx)
         return idx, w
 
@@ -47,16 +47,15 @@ class GateTopK(torch.autograd.Function):
         probs, idx = ctx.saved_tensors
         if grad_w is None:
             return None, None, None
-        p = probs.gather(-1, idx).float()
-        g = grad_w.float()
-        s = p.abs().sum(-1, keepdim=True)
-        eps = 1e-12
-        denom = s.clamp_min(eps)
-        # d(p / max(||p||_1, eps)) / dp
-        gp = g / denom - torch.where(s > eps, (g * p).sum(-1, keepdim=True) / denom.pow(2), torch.zeros_like(s)) \
-            * torch.sign(p)
-        grad = torch.zeros_like(probs, dtype=torch.float32).scatter_(-1, idx, gp)
-        return grad.to(probs.dtype), None, None
+        T, E = probs.shape
+        k = idx.size(1)
+        g = grad_w.to(probs.dtype).contiguous()
+        grad = torch.empty_like(probs)
+        Z.count(1)
+        Z.check(Z.lib().zs_moe_gate_topk_backward(probs.data_ptr(), Z.dtype_code(probs.dtype), idx.data_ptr(),
+                                                  g.data_ptr(), Z.dtype_code(g.dtype), T, E, k, grad.data_ptr(),
+                                                  Z.stream_of(probs)), "zs_moe_gate_topk_backward")
+        return grad, None, None
 
 
 class MoEGate(nn.Module):

@@ -27,6 +27,7 @@ _SIGNATURES = {
     "zs_device_error_get": (_i32, [ctypes.POINTER(_i32), _vp]),
     "zs_device_error_clear": (_i32, [_vp]),
     "zs_moe_gate_topk": (_i32, [_vp, _i32, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "zs_moe_gate_topk_backward": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp]),
     "zs_flatten_sort_count_workspace": (_sz, [_i64, _i32]),
     "zs_flatten_sort_count": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "zs_bincount": (_i32, [_vp, _i64, _i32, _vp, _vp]),

@@ -76,6 +76,17 @@ int zs_moe_gate_topk(const void* gate_probs, int probs_dtype, const float* exper
                      int num_experts, int top_k, int64_t* topk_idx, void* topk_weight, void* stream);
 
 /*
+ * Backward of the differentiable part of MoEGate.forward
+ * (modeling/moe_gate.py:33-34: gather of gate_probs at topk_idx, then
+ * F.normalize(p=1, eps=1e-12)): grad_probs [T, E] (fully written, zeros off
+ * the selected experts) from grad_weight [T, k].  f32 arithmetic; grad and
+ * probs share one dtype.
+ */
+int zs_moe_gate_topk_backward(const void* gate_probs, int probs_dtype, const int64_t* topk_idx,
+                              const void* grad_weight, int grad_dtype, int64_t num_tokens, int num_experts, int top_k,
+                              void* grad_probs, void* stream);
+
+/*
  * flatten_sort_count (scattermoe/parallel_experts.py:21-28): stable counting
  * sort of the flat expert ids.
  *   sorted_expert_idxs[i]    expert id of the i-th sorted slot
