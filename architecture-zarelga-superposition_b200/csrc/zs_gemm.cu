@@ -290,7 +290,7 @@ __device__ __forceinline__ void load_chunk(const char* src, int64_t row_off, int
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT>
 __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     uint32_t phase = 0;
     uint32_t acc_iter = 0;
     bool ok = true;
-    const uint32_t idesc = args.ab_fmt ? IDESC_BF16 : IDESC_F16;
+    const uint32_t idesc = DT == ZS_BF16 ? IDESC_BF16 : IDESC_F16;
     bool issued_any = false;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     uint8_t* stg = smem + L::OFF_STG + (warp - 2) * STG_BYTES;
-    const bool vec = args.vec_ok && args.out_dtype != ZS_F32;
+    const bool vec = args.vec_ok;
     uint32_t acc_iter = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           const int ncols = min(32, args.N_out - col0);
           if (ncols <= 0) break;
           const int64_t roff = ti.e * args.out_se + (int64_t)m * args.ldo_m;
-          emit_chunk(args.out, roff, col0, ncols, m < args.M_xty, z, args.out_dtype, vec, stg);
+          emit_chunk(args.out, roff, col0, ncols, m < args.M_xty, z, DT, vec, stg);
         }
         continue;
       }
@@ -603,15 +603,15 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             float u[32], g[32], h[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              u[j] = round_to(__uint_as_float(ru[j]), args.out_dtype);
-              g[j] = round_to(__uint_as_float(rg[j]), args.out_dtype);
-              h[j] = round_to(silu_fast(g[j]), args.out_dtype) * u[j];
+              u[j] = round_to(__uint_as_float(ru[j]), DT);
+              g[j] = round_to(__uint_as_float(rg[j]), DT);
+              h[j] = round_to(silu_fast(g[j]), DT) * u[j];
             }
-            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, h, args.out_dtype, vec, stg);
+            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, h, DT, vec, stg);
             if (args.out2 != nullptr) {
-              emit_chunk(args.out2, out_row * args.ldo2, col0, ncols, valid, u, args.out_dtype, vec, stg);
+              emit_chunk(args.out2, out_row * args.ldo2, col0, ncols, valid, u, DT, vec, stg);
               emit_chunk(args.out2, out_row * args.ldo2, args.swiglu_half + col0, ncols, valid, g,
-                         args.out_dtype, vec, stg);
+                         DT, vec, stg);
             }
           }
         } else if (EPI == EPI_DSWIGLU) {
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             const int ncols = min(32, args.N_out - col0);
             if (ncols <= 0) continue;
             float o[32];
-#define ZS_DV(j) round_to(__uint_as_float(r[j]), args.out_dtype)
+#define ZS_DV(j) round_to(__uint_as_float(r[j]), DT)
             if (vec && ncols == 32) {
               // h is read now; its latency overlaps the d(h) half below.
               uint4 hraw[4];
@@ -640,34 +640,34 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
               // d(h) = d(act) * silu(g)
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const float gj = elem16(gcur, j, args.out_dtype);
-                o[j] = ZS_DV(j) * round_to(gj * sigmoid_fast(gj), args.out_dtype);
+                const float gj = elem16(gcur, j, DT);
+                o[j] = ZS_DV(j) * round_to(gj * sigmoid_fast(gj), DT);
               }
-              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, args.out_dtype, vec, stg);
+              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, DT, vec, stg);
               // d(g) = (d(act) * h) * silu'(g)
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const float gj = elem16(gcur, j, args.out_dtype);
-                const float hj = elem16(hraw, j, args.out_dtype);
+                const float gj = elem16(gcur, j, DT);
+                const float hj = elem16(hraw, j, DT);
                 const float sig = sigmoid_fast(gj);
-                o[j] = round_to(ZS_DV(j) * hj, args.out_dtype) * (sig * (1.0f + gj * (1.0f - sig)));
+                o[j] = round_to(ZS_DV(j) * hj, DT) * (sig * (1.0f + gj * (1.0f - sig)));
               }
-              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, args.out_dtype,
+              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, DT,
                          vec, stg);
             } else {
               float hv[32], gv[32];
-              load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, args.out_dtype, vec);
-              load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, args.out_dtype,
+              load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, DT, vec);
+              load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, DT,
                          vec);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) o[j] = ZS_DV(j) * round_to(gv[j] * sigmoid_fast(gv[j]), args.out_dtype);
-              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, args.out_dtype, vec, stg);
+              for (int j = 0; j < 32; ++j) o[j] = ZS_DV(j) * round_to(gv[j] * sigmoid_fast(gv[j]), DT);
+              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, DT, vec, stg);
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const float sig = sigmoid_fast(gv[j]);
-                o[j] = round_to(ZS_DV(j) * hv[j], args.out_dtype) * (sig * (1.0f + gv[j] * (1.0f - sig)));
+                o[j] = round_to(ZS_DV(j) * hv[j], DT) * (sig * (1.0f + gv[j] * (1.0f - sig)));
               }
-              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, args.out_dtype,
+              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, DT,
                          vec, stg);
             }
 #undef ZS_DV
@@ -693,9 +693,9 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                 if (j < ncols) {
                   const int64_t bi = ti.e * args.bias_se + (int64_t)(col0 + j) * args.bias_sn;
                   float b;
-                  if (args.out_dtype == ZS_BF16)
+                  if (DT == ZS_BF16)
                     b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi]);
-                  else if (args.out_dtype == ZS_F16)
+                  else if (DT == ZS_F16)
                     b = __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
                   else
                     b = reinterpret_cast<const float*>(args.bias)[bi];
@@ -703,7 +703,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                 }
               }
             }
-            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, v, args.out_dtype, vec, stg);
+            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, v, DT, vec, stg);
           }
         }
       } else {
@@ -721,7 +721,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          emit_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, valid, v, args.out_dtype,
+          emit_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, valid, v, DT,
                      vec, stg);
         }
       }
@@ -790,7 +790,8 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
                        cudaStream_t stream) {
   using L = Smem<BN, STAGES>;
-  auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  auto kern = args.out_dtype == ZS_F16 ? grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_F16>
+                                       : grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_BF16>;
   ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   int64_t grid = num_sms();
   if (max_tiles < grid) grid = max_tiles;
