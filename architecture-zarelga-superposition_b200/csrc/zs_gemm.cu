@@ -171,25 +171,20 @@ constexpr int STG_PITCH = 80;
 constexpr int STG_BYTES = 32 * STG_PITCH;
 constexpr int NUM_EPI_WARPS = 8;
 
-// Write 32 consecutive columns [col0, col0 + ncols) of this lane's output row
-// (element (row, n) at out[row_off + n]).  When the chunk is full and 16-bit,
-// the warp transposes its 32 rows through shared memory so that each store
-// instruction writes 64 contiguous bytes of 8 rows; otherwise scalar stores.
-// Must be called by all 32 lanes with warp-uniform col0/ncols.
-__device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0, int ncols, bool valid,
-                                           const float (&v)[32], int dtype, bool vec, uint8_t* stg) {
+// Write 32 consecutive 16-bit columns [col0, col0 + ncols) of this lane's
+// output row (element (row, n) at out[row_off + n]), given as 16 packed pairs.
+// When the chunk is full and aligned, the warp transposes its 32 rows through
+// shared memory so that each store instruction writes 64 contiguous bytes of
+// 8 rows; otherwise scalar stores.  Must be called by all 32 lanes with
+// warp-uniform col0/ncols.
+template <int DT>
+__device__ __forceinline__ void emit_packed(char* out, int64_t row_off, int col0, int ncols, bool valid,
+                                            const uint32_t (&p)[16], bool vec, uint8_t* stg) {
   const int lane = threadIdx.x & 31;
   if (vec && ncols == 32) {
     uint4* my = reinterpret_cast<uint4*>(stg + lane * STG_PITCH);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack2(v[q * 8 + 0], v[q * 8 + 1], dtype);
-      w.y = pack2(v[q * 8 + 2], v[q * 8 + 3], dtype);
-      w.z = pack2(v[q * 8 + 4], v[q * 8 + 5], dtype);
-      w.w = pack2(v[q * 8 + 6], v[q * 8 + 7], dtype);
-      my[q] = w;
-    }
+    for (int q = 0; q < 4; ++q) my[q] = make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
     __syncwarp();
     const unsigned long long my_ptr =
         valid ? reinterpret_cast<unsigned long long>(out + (row_off + col0) * 2) : 0ull;
@@ -198,51 +193,25 @@ __device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0,
       const int r = 8 * i + (lane >> 2);
       const int qq = lane & 3;
       const uint4 w = *reinterpret_cast<const uint4*>(stg + r * STG_PITCH + qq * 16);
-      const unsigned long long p = __shfl_sync(0xffffffffu, my_ptr, r);
-      if (p != 0ull) reinterpret_cast<uint4*>(p)[qq] = w;
+      const unsigned long long ptr = __shfl_sync(0xffffffffu, my_ptr, r);
+      if (ptr != 0ull) reinterpret_cast<uint4*>(ptr)[qq] = w;
     }
     __syncwarp();
   } else if (valid) {
+    uint16_t* o = reinterpret_cast<uint16_t*>(out) + row_off + col0;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (j < ncols) store_val(out, row_off + col0 + j, dtype, v[j]);
+      if (j < ncols) o[j] = (j & 1) ? (uint16_t)(p[j >> 1] >> 16) : (uint16_t)(p[j >> 1] & 0xffffu);
   }
 }
 
-// The gate half [swiglu_half + col0, +32) of this lane's saved row, raw.
-__device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&w)[4]) {
-  ok = ok && col0 + 32 <= a.N_out;
-  const uint4* p = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + a.swiglu_half + col0) * 2);
+template <int DT>
+__device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0, int ncols, bool valid,
+                                           const float (&v)[32], bool vec, uint8_t* stg) {
+  uint32_t p[16];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
-}
-
-// Element j (compile-time after unrolling) of 32 packed 16-bit values, as f32.
-__device__ __forceinline__ float elem16(const uint4 (&w)[4], int j, int dtype) {
-  const uint4& q = w[j >> 3];
-  const int k = (j & 7) >> 1;
-  const uint32_t u = k == 0 ? q.x : (k == 1 ? q.y : (k == 2 ? q.z : q.w));
-  const uint16_t b = (j & 1) ? (uint16_t)(u >> 16) : (uint16_t)(u & 0xffffu);
-  if (dtype == ZS_F16) return __half2float(__ushort_as_half(b));
-  return __bfloat162float(__ushort_as_bfloat16(b));
-}
-
-// 4 x 16 bytes of 16-bit values -> 32 f32.
-__device__ __forceinline__ void unpack32(const uint4 (&w)[4], float (&v)[32], int dtype) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t u[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      float2 f;
-      if (dtype == ZS_F16)
-        f = __half22float2(*reinterpret_cast<const __half2*>(&u[h]));
-      else
-        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[h]));
-      v[q * 8 + 2 * h] = f.x;
-      v[q * 8 + 2 * h + 1] = f.y;
-    }
-  }
+  for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], DT);
+  emit_packed<DT>(out, row_off, col0, ncols, valid, p, vec, stg);
 }
 
 // Read 32 consecutive 16-bit columns of this lane's row as f32.
@@ -280,14 +249,43 @@ __device__ __forceinline__ void load_chunk(const char* src, int64_t row_off, int
         const int64_t i = row_off + col0 + j;
         if (dtype == ZS_BF16)
           x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[i]);
-        else if (dtype == ZS_F16)
-          x = __half2float(reinterpret_cast<const __half*>(src)[i]);
         else
-          x = reinterpret_cast<const float*>(src)[i];
+          x = __half2float(reinterpret_cast<const __half*>(src)[i]);
       }
       v[j] = x;
     }
   }
+}
+
+// Two 16-bit lanes of a packed word <-> f32 pair; and the product of two
+// packed pairs rounded once to the 16-bit type (exact f32 product of two
+// 16-bit values, then round-to-nearest: the reference's `a * b` on tensors).
+template <int DT>
+__device__ __forceinline__ float2 unpk(uint32_t u) {
+  if (DT == ZS_F16) return __half22float2(*reinterpret_cast<const __half2*>(&u));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+template <int DT>
+__device__ __forceinline__ uint32_t pk(float a, float b) {
+  return pack2(a, b, DT);
+}
+template <int DT>
+__device__ __forceinline__ uint32_t mul_rn(uint32_t a, uint32_t b) {
+  const float2 x = unpk<DT>(a), y = unpk<DT>(b);
+  return pack2(x.x * y.x, x.y * y.y, DT);
+}
+__device__ __forceinline__ uint32_t word_of(const uint4 (&w)[4], int jj) {
+  const uint4& q = w[jj >> 2];
+  const int k = jj & 3;
+  return k == 0 ? q.x : (k == 1 ? q.y : (k == 2 ? q.z : q.w));
+}
+
+// The gate half [swiglu_half + col0, +32) of this lane's saved row, raw.
+__device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&w)[4]) {
+  ok = ok && col0 + 32 <= a.N_out;
+  const uint4* p = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + a.swiglu_half + col0) * 2);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT>
@@ -562,7 +560,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           const int ncols = min(32, args.N_out - col0);
           if (ncols <= 0) break;
           const int64_t roff = ti.e * args.out_se + (int64_t)m * args.ldo_m;
-          emit_chunk(args.out, roff, col0, ncols, m < args.M_xty, z, DT, vec, stg);
+          emit_chunk<DT>(args.out, roff, col0, ncols, m < args.M_xty, z, vec, stg);
         }
         continue;
       }
@@ -600,77 +598,75 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             const int col0 = ti.nt * (BN / 2) + lc;
             const int ncols = min(32, args.N_out - col0);
             if (ncols <= 0) continue;
-            float u[32], g[32], h[32];
+            // u, g as stored (rounded), act = round(round(silu(g)) * u)
+            uint32_t pu[16], pg[16], pa[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              u[j] = round_to(__uint_as_float(ru[j]), DT);
-              g[j] = round_to(__uint_as_float(rg[j]), DT);
-              h[j] = round_to(silu_fast(g[j]), DT) * u[j];
+            for (int jj = 0; jj < 16; ++jj) {
+              pu[jj] = pk<DT>(__uint_as_float(ru[2 * jj]), __uint_as_float(ru[2 * jj + 1]));
+              pg[jj] = pk<DT>(__uint_as_float(rg[2 * jj]), __uint_as_float(rg[2 * jj + 1]));
+              const float2 g2 = unpk<DT>(pg[jj]);
+              pa[jj] = mul_rn<DT>(pk<DT>(silu_fast(g2.x), silu_fast(g2.y)), pu[jj]);
             }
-            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, h, DT, vec, stg);
+            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pa, vec, stg);
             if (args.out2 != nullptr) {
-              emit_chunk(args.out2, out_row * args.ldo2, col0, ncols, valid, u, DT, vec, stg);
-              emit_chunk(args.out2, out_row * args.ldo2, args.swiglu_half + col0, ncols, valid, g,
-                         DT, vec, stg);
+              emit_packed<DT>(args.out2, out_row * args.ldo2, col0, ncols, valid, pu, vec, stg);
+              emit_packed<DT>(args.out2, out_row * args.ldo2, args.swiglu_half + col0, ncols, valid, pg, vec, stg);
             }
           }
         } else if (EPI == EPI_DSWIGLU) {
           // The accumulator is d(act) for activation columns; combine it with
-          // the saved pre-activation [h | g] into d[h | g].  The gate half of
-          // the next chunk is fetched while this one is processed.
+          // the saved pre-activation [h | g] into d[h | g] in one pass, with
+          // the reference's rounding points:
+          //   dh = round(da * round(silu(g))),  dg = round(round(da * h) * silu'(g))
+          // The gate half of the next chunk is fetched during this one.
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
             const int lc = half * (BN / 2) + c * 32;
             uint4 gnext[4];
             prefetch_chunk(args, out_row, ti.nt * BN + lc + 32, valid && vec && c + 1 < BN / 64, gnext);
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + lc, r);
-            tc_wait_ld();
             const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
-            if (ncols <= 0) continue;
-            float o[32];
-#define ZS_DV(j) round_to(__uint_as_float(r[j]), DT)
-            if (vec && ncols == 32) {
-              // h is read now; its latency overlaps the d(h) half below.
-              uint4 hraw[4];
+            uint4 hraw[4];
+            const bool fast = vec && ncols == 32;
+            if (fast) {
               const uint4* ph = reinterpret_cast<const uint4*>(args.aux + (out_row * args.ld_aux + col0) * 2);
 #pragma unroll
               for (int q = 0; q < 4; ++q) hraw[q] = valid ? __ldg(ph + q) : make_uint4(0, 0, 0, 0);
-              // d(h) = d(act) * silu(g)
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float gj = elem16(gcur, j, DT);
-                o[j] = ZS_DV(j) * round_to(gj * sigmoid_fast(gj), DT);
-              }
-              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, DT, vec, stg);
-              // d(g) = (d(act) * h) * silu'(g)
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float gj = elem16(gcur, j, DT);
-                const float hj = elem16(hraw, j, DT);
-                const float sig = sigmoid_fast(gj);
-                o[j] = round_to(ZS_DV(j) * hj, DT) * (sig * (1.0f + gj * (1.0f - sig)));
-              }
-              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, DT,
-                         vec, stg);
-            } else {
+            }
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + lc, r);
+            tc_wait_ld();
+            if (ncols <= 0) continue;
+            if (!fast) {
+              // ragged edge: plain loads
               float hv[32], gv[32];
               load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, hv, DT, vec);
-              load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, DT,
-                         vec);
+              load_chunk(args.aux, out_row * args.ld_aux, args.swiglu_half + col0, ncols, valid, gv, DT, vec);
+              uint32_t ph[16], pgv[16];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) o[j] = ZS_DV(j) * round_to(gv[j] * sigmoid_fast(gv[j]), DT);
-              emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, o, DT, vec, stg);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float sig = sigmoid_fast(gv[j]);
-                o[j] = round_to(ZS_DV(j) * hv[j], DT) * (sig * (1.0f + gv[j] * (1.0f - sig)));
+              for (int jj = 0; jj < 16; ++jj) {
+                ph[jj] = pk<DT>(hv[2 * jj], hv[2 * jj + 1]);
+                pgv[jj] = pk<DT>(gv[2 * jj], gv[2 * jj + 1]);
               }
-              emit_chunk(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, o, DT,
-                         vec, stg);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                hraw[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
+                gcur[q] = make_uint4(pgv[4 * q], pgv[4 * q + 1], pgv[4 * q + 2], pgv[4 * q + 3]);
+              }
             }
-#undef ZS_DV
+            uint32_t odh[16], odg[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const uint32_t da = pk<DT>(__uint_as_float(r[2 * jj]), __uint_as_float(r[2 * jj + 1]));
+              const uint32_t gw = word_of(gcur, jj);
+              const float2 g2 = unpk<DT>(gw);
+              const float s0 = sigmoid_fast(g2.x), s1 = sigmoid_fast(g2.y);
+              odh[jj] = mul_rn<DT>(da, pk<DT>(g2.x * s0, g2.y * s1));
+              const float2 t2 = unpk<DT>(mul_rn<DT>(da, word_of(hraw, jj)));
+              odg[jj] = pk<DT>(t2.x * (s0 * (1.0f + g2.x * (1.0f - s0))), t2.y * (s1 * (1.0f + g2.y * (1.0f - s1))));
+            }
+            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, odh, vec, stg);
+            emit_packed<DT>(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, odg, vec, stg);
 #pragma unroll
             for (int q = 0; q < 4; ++q) gcur[q] = gnext[q];
           }
@@ -692,23 +688,17 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
               for (int j = 0; j < 32; ++j) {
                 if (j < ncols) {
                   const int64_t bi = ti.e * args.bias_se + (int64_t)(col0 + j) * args.bias_sn;
-                  float b;
-                  if (DT == ZS_BF16)
-                    b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi]);
-                  else if (DT == ZS_F16)
-                    b = __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
-                  else
-                    b = reinterpret_cast<const float*>(args.bias)[bi];
-                  v[j] += b;
+                  v[j] += DT == ZS_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[bi])
+                                        : __half2float(reinterpret_cast<const __half*>(args.bias)[bi]);
                 }
               }
             }
-            emit_chunk(args.out, out_row * args.ldo_m, col0, ncols, valid, v, DT, vec, stg);
+            emit_chunk<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, v, vec, stg);
           }
         }
       } else {
         const int m = ti.mt * BM + row_in_tile;
-        const bool valid = m < args.M_xty;
+        const bool mvalid = m < args.M_xty;
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           const int lc = half * (BN / 2) + c * 32;
@@ -721,8 +711,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          emit_chunk(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, valid, v, DT,
-                     vec, stg);
+          emit_chunk<DT>(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, mvalid, v, vec, stg);
         }
       }
       tc_fence_before();
