@@ -13,6 +13,7 @@ extern "C" const char* zs_error_string(int code) {
     case ZS_ERR_CUDA: return "CUDA runtime or driver call failed";
     case ZS_ERR_WORKSPACE: return "workspace missing or too small";
     case ZS_ERR_LAYOUT: return "stride pattern not supported";
+    case ZS_ERR_SCRATCH_LIMIT: return "problem larger than the fixed scratch of the allocation-free entry point";
   }
   return "unknown zs error";
 }

@@ -9,6 +9,8 @@
 //     (scattermoe/parallel_experts.py:6-15, main.py:161-175).
 #include "zs_common.cuh"
 
+#include <mutex>
+
 namespace zs {
 
 // Total order on f32 used by CUDA torch.topk's radix select: flip so that
@@ -497,4 +499,55 @@ extern "C" int zs_moe_gate_topk_backward(const void* gate_probs, int probs_dtype
     return ZS_ERR_DTYPE;
 #undef ZS_GB
   return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
+}
+
+// ----------------------------------------------- allocation-free variant --
+//
+// Some callers cannot allocate device memory at the point where they route
+// tokens: code running inside a CUDA stream capture that must not add
+// allocation nodes, runtimes that own a fixed memory pool and forbid
+// cudaMalloc after start-up, or plain C callers without an allocator.  For
+// them zs_flatten_sort_count_noalloc keeps its scratch (the per-chunk expert
+// histograms) in the fixed device array below instead of a caller workspace.
+//
+// The array is 1 MiB (ZS_FSC_NOALLOC_MAX_INTS ints) and exists on every GPU
+// that loads this library until the process exits.  Host code cannot use the
+// array's name as a device address (it names a host-side shadow), so the
+// device address is looked up once per device with cudaGetSymbolAddress, with
+// that device current, on the first call made on that device.
+constexpr int64_t ZS_FSC_NOALLOC_MAX_INTS = (int64_t)1 << 18;
+static __device__ __align__(256) int zs_fsc_noalloc_scratch[ZS_FSC_NOALLOC_MAX_INTS];
+
+static int fsc_noalloc_scratch_ptr(void** out) {
+  constexpr int MAX_DEVICES = 64;
+  static std::mutex mu;
+  static void* ptrs[MAX_DEVICES] = {};
+  int dev = 0;
+  ZS_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= MAX_DEVICES) return ZS_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    ZS_CUDA_TRY(cudaGetSymbolAddress(&p, zs_fsc_noalloc_scratch));
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return ZS_OK;
+}
+
+extern "C" int64_t zs_flatten_sort_count_noalloc_max_scratch_ints(void) { return ZS_FSC_NOALLOC_MAX_INTS; }
+
+extern "C" int zs_flatten_sort_count_noalloc(const int64_t* expert_idxs, int64_t n, int num_experts,
+                                             int64_t* sorted_expert_idxs, int64_t* sorted_scattered_idxs,
+                                             int64_t* expert_offsets, void* stream) {
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= 4096 && n >= 0 && n < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  const size_t need = zs_flatten_sort_count_workspace(n, num_experts);
+  if ((int64_t)(need / sizeof(int)) > ZS_FSC_NOALLOC_MAX_INTS) return ZS_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int rc = fsc_noalloc_scratch_ptr(&scratch);
+  if (rc != ZS_OK) return rc;
+  // Every histogram slot the sort reads is written by its first kernel in the
+  // same call, so leftovers from an earlier call need no clearing.
+  return zs_flatten_sort_count(expert_idxs, n, num_experts, sorted_expert_idxs, sorted_scattered_idxs, expert_offsets,
+                               scratch, (size_t)ZS_FSC_NOALLOC_MAX_INTS * sizeof(int), stream);
 }

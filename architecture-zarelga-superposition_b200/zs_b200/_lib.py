@@ -30,6 +30,8 @@ _SIGNATURES = {
     "zs_moe_gate_topk_backward": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp]),
     "zs_flatten_sort_count_workspace": (_sz, [_i64, _i32]),
     "zs_flatten_sort_count": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "zs_flatten_sort_count_noalloc_max_scratch_ints": (_i64, []),
+    "zs_flatten_sort_count_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "zs_bincount": (_i32, [_vp, _i64, _i32, _vp, _vp]),
     "zs_expert_counts": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "zs_bias_sign_update": (_i32, [_vp, _i32, _f32, _vp, _vp]),

@@ -37,6 +37,7 @@ extern "C" {
 #define ZS_ERR_CUDA 5        /* a CUDA runtime/driver call failed */
 #define ZS_ERR_WORKSPACE 6   /* workspace missing or too small */
 #define ZS_ERR_LAYOUT 7      /* stride pattern not supported by the kernel */
+#define ZS_ERR_SCRATCH_LIMIT 8 /* problem larger than the fixed scratch of an allocation-free entry point */
 
 /* device error bits (zs_device_error_get) */
 #define ZS_DEVERR_TIMEOUT_PRODUCER 0x01
@@ -100,6 +101,28 @@ size_t zs_flatten_sort_count_workspace(int64_t n, int num_experts);
 int zs_flatten_sort_count(const int64_t* expert_idxs, int64_t n, int num_experts, int64_t* sorted_expert_idxs,
                           int64_t* sorted_scattered_idxs, int64_t* expert_offsets, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/*
+ * Allocation-free variant of zs_flatten_sort_count.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they route tokens (inside a CUDA stream capture that must not add
+ * allocation nodes, runtimes with a fixed memory pool, C callers without an
+ * allocator).  Same inputs, outputs and results as zs_flatten_sort_count; the
+ * scratch lives in a fixed 1 MiB device array inside the library (held on
+ * every GPU that loads the library until the process exits), so the problem
+ * must satisfy ceil(n / 4096) * (num_experts + 1) <= 262144 (the value of
+ * zs_flatten_sort_count_noalloc_max_scratch_ints()); larger problems return
+ * ZS_ERR_SCRATCH_LIMIT without launching anything.  It allocates nothing.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  All calls on a device share the array, so calls
+ * whose kernels overlap on the GPU (different streams without ordering) race;
+ * serialise them.
+ */
+int64_t zs_flatten_sort_count_noalloc_max_scratch_ints(void);
+int zs_flatten_sort_count_noalloc(const int64_t* expert_idxs, int64_t n, int num_experts,
+                                  int64_t* sorted_expert_idxs, int64_t* sorted_scattered_idxs,
+                                  int64_t* expert_offsets, void* stream);
 
 /* compileable_bincount (scattermoe/parallel_experts.py:6-15): int64 counts of
  * x[0..n) over [0, minlength). */
