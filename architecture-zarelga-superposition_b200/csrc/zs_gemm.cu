@@ -36,7 +36,7 @@ constexpr int BK = 64;
 constexpr int MAX_EXPERTS_GEMM = 1024;
 
 enum { MODE_ROWS = 0, MODE_XTY = 1 };
-enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_DSWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_DSWIGLU = 2, EPI_LSE = 3, EPI_XENT_GRAD = 4, EPI_F32 = 5 };
 
 struct GemmArgs {
   int mode;
@@ -65,6 +65,20 @@ struct GemmArgs {
   const char* aux;                     // EPI_DSWIGLU: saved pre-activation rows [h | g]
   int64_t ld_aux;
   int vec_ok;                          // 16-byte vector stores allowed for row-contiguous output
+  int64_t b_row_offset;                // added to B's row coordinate (dense GEMMs over a slice of B)
+  // cross-entropy epilogues (EPI_LSE, EPI_XENT_GRAD); columns are vocabulary entries
+  const int64_t* labels;               // [rows, s_max]
+  const int* s_count;                  // [rows] active labels per row (0 = row ignored)
+  int s_max;
+  int64_t col_offset;                  // vocabulary index of this launch's column 0
+  float* part_max;                     // EPI_LSE: [rows, part_ld] running max / sum partials
+  float* part_sum;
+  int64_t part_ld;
+  float* target_sum;                   // EPI_LSE: [rows] += target logits (atomic)
+  const float* lse;                    // EPI_XENT_GRAD: [rows]
+  const float* grad_loss;              // EPI_XENT_GRAD: device scalar dL/dloss
+  const float* denom;                  // EPI_XENT_GRAD: device scalar N (total active labels)
+  int accumulate;                      // EPI_F32: out += acc instead of out = acc
 };
 
 template <int BN, int STAGES>
@@ -280,6 +294,31 @@ __device__ __forceinline__ uint32_t word_of(const uint4 (&w)[4], int jj) {
   return k == 0 ? q.x : (k == 1 ? q.y : (k == 2 ? q.z : q.w));
 }
 
+// 32 f32 accumulator columns of this lane's row to f32 memory (optionally
+// added to what is there).  vec: 16-byte aligned row segments.
+__device__ __forceinline__ void store_f32_chunk(float* o, const uint32_t (&r)[32], int ncols, bool acc, bool vec) {
+  if (vec && ncols == 32) {
+    float4* p = reinterpret_cast<float4*>(o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                             __uint_as_float(r[4 * q + 3]));
+      if (acc) {
+        const float4 w = p[q];
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+      }
+      p[q] = v;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols) o[j] = (acc ? o[j] : 0.f) + __uint_as_float(r[j]);
+  }
+}
+
 // The gate half [swiglu_half + col0, +32) of this lane's saved row, raw.
 __device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&w)[4]) {
   ok = ok && col0 + 32 <= a.N_out;
@@ -338,6 +377,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     int64_t s;
     if (e == 0)
       s = 0;
+    else if (args.expert_offsets == nullptr && args.sorted_expert_idxs == nullptr)
+      s = args.n_rows;  // dense GEMM: one group holding every row
     else if (args.expert_offsets != nullptr)
       s = __ldg(args.expert_offsets + (e - 1));
     else
@@ -421,7 +462,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           if (args.mode == MODE_ROWS) {
             if (!A_MN) tma_load_2d(sA, &tmA, &full[stage], kb * BK, ti.r0);
             if (!B_MN) {
-              const int brow = ti.e * args.b_rows_per_expert;
+              const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset;
               if (EPI == EPI_SWIGLU) {
                 tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * (BN / 2));
                 tma_load_2d(sB + (BN / 2) * 128, &tmB, &full[stage], kb * BK,
@@ -430,7 +471,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                 tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * BN);
               }
             } else {
-              const int brow = ti.e * args.b_rows_per_expert + kb * BK;
+              const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset + kb * BK;
 #pragma unroll
               for (int j = 0; j < BN / 64; ++j)
                 tma_load_2d(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + j * 64, brow);
@@ -560,7 +601,15 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           const int ncols = min(32, args.N_out - col0);
           if (ncols <= 0) break;
           const int64_t roff = ti.e * args.out_se + (int64_t)m * args.ldo_m;
-          emit_chunk<DT>(args.out, roff, col0, ncols, m < args.M_xty, z, vec, stg);
+          if (EPI == EPI_F32) {
+            uint32_t zr[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) zr[j] = 0u;
+            if (m < args.M_xty)
+              store_f32_chunk(reinterpret_cast<float*>(args.out) + roff + col0, zr, ncols, args.accumulate != 0, vec);
+          } else {
+            emit_chunk<DT>(args.out, roff, col0, ncols, m < args.M_xty, z, vec, stg);
+          }
         }
         continue;
       }
@@ -670,6 +719,93 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) gcur[q] = gnext[q];
           }
+        } else if (EPI == EPI_LSE || EPI == EPI_XENT_GRAD) {
+          // Columns are vocabulary entries col_offset + col.  Labels of this
+          // row, relative to this warp's first column, found by range test.
+          int si = 0;
+          int64_t lab[8];
+          const int64_t wcol = args.col_offset + ti.nt * BN + half * (BN / 2);
+          if (valid) {
+            si = min(__ldg(args.s_count + row), args.s_max);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) lab[j] = (j < si) ? __ldg(args.labels + (int64_t)row * args.s_max + j) - wcol : -1;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) lab[j] = -1;
+          }
+          float run_m = -INFINITY, run_s = 0.f, tgt = 0.f;
+          float alpha = 0.f, scale = 0.f, lrow = 0.f;
+          if (EPI == EPI_XENT_GRAD) {
+            scale = __ldg(args.grad_loss) / __ldg(args.denom);
+            alpha = scale * (float)si;
+            lrow = valid ? __ldg(args.lse + row) : 0.f;
+          }
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            const int lc = half * (BN / 2) + c * 32;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + lc, r);
+            tc_wait_ld();
+            const int col0 = ti.nt * BN + lc;
+            const int ncols = min(32, args.N_out - col0);
+            if (ncols <= 0) continue;
+            if (EPI == EPI_LSE) {
+              float cm = -INFINITY;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) cm = fmaxf(cm, __uint_as_float(r[j]));
+              const float nm = fmaxf(run_m, cm);
+              float acc = run_s * __expf(run_m - nm);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) acc += __expf(__uint_as_float(r[j]) - nm);
+              run_m = nm;
+              run_s = acc;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int64_t off = lab[j] - c * 32;
+                if (off >= 0 && off < ncols) {
+                  float z = 0.f;
+#pragma unroll
+                  for (int q = 0; q < 32; ++q) z = (q == (int)off) ? __uint_as_float(r[q]) : z;
+                  tgt += z;
+                }
+              }
+            } else {
+              float g[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) g[j] = alpha * __expf(__uint_as_float(r[j]) - lrow);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int64_t off = lab[j] - c * 32;
+                if (off >= 0 && off < ncols) {
+#pragma unroll
+                  for (int q = 0; q < 32; ++q)
+                    if (q == (int)off) g[q] -= scale;
+                }
+              }
+              emit_chunk<DT>(args.out, (int64_t)row * args.ldo_m, col0, ncols, valid, g, vec, stg);
+            }
+          }
+          if (EPI == EPI_LSE && valid) {
+            const int64_t slot = (int64_t)row * args.part_ld + (int64_t)ti.nt * 2 + half;
+            args.part_max[slot] = run_m;
+            args.part_sum[slot] = run_s;
+            if (tgt != 0.f) atomicAdd(args.target_sum + row, tgt);
+          }
+        } else if (EPI == EPI_F32) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            const int lc = half * (BN / 2) + c * 32;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + lc, r);
+            tc_wait_ld();
+            const int col0 = ti.nt * BN + lc;
+            const int ncols = min(32, args.N_out - col0);
+            if (ncols <= 0 || !valid) continue;
+            float* o = reinterpret_cast<float*>(args.out) + out_row * args.ldo_m + col0;
+            store_f32_chunk(o, r, ncols, args.accumulate != 0, vec);
+          }
         } else {
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
@@ -708,6 +844,13 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           const int col0 = ti.nt * BN + lc;
           const int ncols = min(32, args.N_out - col0);
           if (ncols <= 0) continue;
+          if (EPI == EPI_F32) {
+            if (mvalid) {
+              float* o = reinterpret_cast<float*>(args.out) + ti.e * args.out_se + (int64_t)m * args.ldo_m + col0;
+              store_f32_chunk(o, r, ncols, args.accumulate != 0, vec);
+            }
+            continue;
+          }
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -1047,4 +1190,237 @@ extern "C" int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const voi
              ((F * es) % 16 == 0);
   const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
   return launch_gemm<BN, 4, false, true, EPI_DSWIGLU>(tmA, tmB, a, max_tiles, stream);
+}
+
+// ------------------------------------------------------------ cross entropy
+
+namespace zs {
+
+// lse[t] from the (max, sum) partials; row loss s_t * lse_t - target_t.
+__global__ void xent_finalize_kernel(const float* __restrict__ part_max, const float* __restrict__ part_sum,
+                                     int64_t part_ld, int nparts, const float* __restrict__ target_sum,
+                                     const int* __restrict__ s_count, int s_max, int64_t T, float* __restrict__ lse,
+                                     float* __restrict__ row_loss) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+    float m = -INFINITY;
+    for (int p = lane; p < nparts; p += 32) m = fmaxf(m, part_max[t * part_ld + p]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sum = 0.f;
+    for (int p = lane; p < nparts; p += 32) {
+      const float pm = part_max[t * part_ld + p];
+      if (pm != -INFINITY) sum += part_sum[t * part_ld + p] * expf(pm - m);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) {
+      const float l = m + logf(sum);
+      lse[t] = l;
+      const int si = min(s_count[t], s_max);
+      row_loss[t] = si > 0 ? (float)si * l - target_sum[t] : 0.f;
+    }
+  }
+}
+
+// loss = sum(row_loss) / sum(s); one block, fixed reduction order.
+__global__ void xent_reduce_kernel(const float* __restrict__ row_loss, const int* __restrict__ s_count, int s_max,
+                                   int64_t T, float* __restrict__ loss, float* __restrict__ denom) {
+  __shared__ double sh_l[32];
+  __shared__ long long sh_n[32];
+  double l = 0.0;
+  long long n = 0;
+  for (int64_t t = threadIdx.x; t < T; t += blockDim.x) {
+    l += (double)row_loss[t];
+    n += min(s_count[t], s_max);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    l += __shfl_xor_sync(0xffffffffu, l, off);
+    n += __shfl_xor_sync(0xffffffffu, n, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sh_l[threadIdx.x >> 5] = l;
+    sh_n[threadIdx.x >> 5] = n;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double L = 0.0;
+    long long N = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      L += sh_l[w];
+      N += sh_n[w];
+    }
+    denom[0] = (float)N;
+    loss[0] = N > 0 ? (float)(L / (double)N) : 0.f;
+  }
+}
+
+}  // namespace zs
+
+extern "C" size_t zs_xent_forward_workspace(int64_t T, int64_t V) {
+  const int64_t nparts = 2 * ((V + 255) / 256);
+  return (size_t)(T * nparts * 2 + T) * sizeof(float) + 256;
+}
+
+extern "C" int zs_xent_forward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, const void* classifier,
+                               int64_t V, int64_t c_sm, const int64_t* labels, int s_max, const int* s_count,
+                               float* lse, float* row_loss, float* loss, float* denom, void* workspace,
+                               size_t workspace_bytes, int dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(hidden && classifier && labels && s_count && lse && row_loss && loss && denom, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(T >= 1 && D >= 1 && V >= 1 && s_max >= 1 && s_max <= 8, ZS_ERR_SHAPE);
+  ZS_REQUIRE(T < ((int64_t)1 << 31) && V < ((int64_t)1 << 31) && D < ((int64_t)1 << 24), ZS_ERR_SHAPE);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_xent_forward_workspace(T, V), ZS_ERR_WORKSPACE);
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+  const int64_t n_vt = (V + BN - 1) / BN;
+  float* ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  float* part_max = ws;
+  float* part_sum = ws + T * 2 * n_vt;
+  float* target_sum = part_sum + T * 2 * n_vt;
+  ZS_CUDA_TRY(cudaMemsetAsync(target_sum, 0, sizeof(float) * T, stream));
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 128);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmB, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN);
+  if (rc != ZS_OK) return rc;
+  GemmArgs a{};
+  a.mode = MODE_ROWS;
+  a.num_experts = 1;
+  a.n_tiles = (int)n_vt;
+  a.kb_rows = (int)((D + BK - 1) / BK);
+  a.N_out = (int)V;
+  a.n_rows = T;
+  a.out_rows = T;
+  a.out_dtype = dtype;
+  a.b_rows_per_expert = 0;
+  a.labels = labels;
+  a.s_count = s_count;
+  a.s_max = s_max;
+  a.col_offset = 0;
+  a.part_max = part_max;
+  a.part_sum = part_sum;
+  a.part_ld = 2 * n_vt;
+  a.target_sum = target_sum;
+  rc = launch_gemm<BN, 4, false, false, EPI_LSE>(tmA, tmB, a, ((T + BM - 1) / BM) * n_vt, stream);
+  if (rc != ZS_OK) return rc;
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  xent_finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part_max, part_sum, 2 * n_vt, (int)(2 * n_vt), target_sum,
+                                                            s_count, s_max, T, lse, row_loss);
+  ZS_CUDA_TRY(cudaGetLastError());
+  xent_reduce_kernel<<<1, 1024, 0, stream>>>(row_loss, s_count, s_max, T, loss, denom);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" size_t zs_xent_backward_workspace(int64_t T, int64_t v_chunk, int dtype) {
+  const int64_t pitch = ((v_chunk * elem_size(dtype) + 15) / 16) * 16;
+  return (size_t)(T * pitch + 256);
+}
+
+extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, const void* classifier,
+                                int64_t V, int64_t c_sm, const int64_t* labels, int s_max, const int* s_count,
+                                const float* lse, const float* grad_loss, const float* denom, float* d_hidden,
+                                float* d_classifier, int64_t v_chunk, void* workspace, size_t workspace_bytes,
+                                int dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(hidden && classifier && labels && s_count && lse && grad_loss && denom, ZS_ERR_ARG);
+  ZS_REQUIRE(d_hidden || d_classifier, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(T >= 1 && D >= 1 && V >= 1 && s_max >= 1 && s_max <= 8, ZS_ERR_SHAPE);
+  ZS_REQUIRE(T < ((int64_t)1 << 31) && V < ((int64_t)1 << 31) && D < ((int64_t)1 << 24), ZS_ERR_SHAPE);
+  ZS_REQUIRE(v_chunk >= 256 && v_chunk % 256 == 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_xent_backward_workspace(T, v_chunk, dtype), ZS_ERR_WORKSPACE);
+  ZS_REQUIRE((D * 4) % 16 == 0, ZS_ERR_ALIGN);
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+  const int64_t pitch = ((v_chunk * es + 15) / 16) * 16 / es;
+  char* G = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  CUtensorMap tmH_k, tmC_k, tmC_mn, tmH_mn;
+  int rc = make_tmap(&tmH_k, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 128);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmC_k, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmC_mn, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+  rc = make_tmap(&tmH_mn, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 64);
+  if (rc != ZS_OK) return rc;
+  for (int64_t v0 = 0; v0 < V; v0 += v_chunk) {
+    const int64_t vc = (V - v0 < v_chunk) ? (V - v0) : v_chunk;
+    // (1) recompute the logits of this vocabulary slice; epilogue writes the
+    //     logit gradient G = scale * (s * softmax - counts) in the input dtype
+    GemmArgs g{};
+    g.mode = MODE_ROWS;
+    g.num_experts = 1;
+    g.n_tiles = (int)((vc + BN - 1) / BN);
+    g.kb_rows = (int)((D + BK - 1) / BK);
+    g.N_out = (int)vc;
+    g.n_rows = T;
+    g.out_rows = T;
+    g.out_dtype = dtype;
+    g.out = G;
+    g.ldo_m = pitch;
+    g.ldo_n = 1;
+    g.vec_ok = (pitch * es) % 16 == 0;
+    g.b_row_offset = v0;
+    g.labels = labels;
+    g.s_count = s_count;
+    g.s_max = s_max;
+    g.col_offset = v0;
+    g.lse = lse;
+    g.grad_loss = grad_loss;
+    g.denom = denom;
+    rc = launch_gemm<BN, 4, false, false, EPI_XENT_GRAD>(tmH_k, tmC_k, g, ((T + BM - 1) / BM) * g.n_tiles, stream);
+    if (rc != ZS_OK) return rc;
+    CUtensorMap tmG_k, tmG_mn;
+    rc = make_tmap(&tmG_k, G, dtype, (uint64_t)vc, (uint64_t)T, (uint64_t)pitch * es, 64, 128);
+    if (rc != ZS_OK) return rc;
+    rc = make_tmap(&tmG_mn, G, dtype, (uint64_t)vc, (uint64_t)T, (uint64_t)pitch * es, 64, 64);
+    if (rc != ZS_OK) return rc;
+    // (2) d_hidden (+)= G @ classifier[v0:v0+vc]
+    if (d_hidden) {
+      GemmArgs h{};
+      h.mode = MODE_ROWS;
+      h.num_experts = 1;
+      h.n_tiles = (int)((D + BN - 1) / BN);
+      h.kb_rows = (int)((vc + BK - 1) / BK);
+      h.N_out = (int)D;
+      h.n_rows = T;
+      h.out_rows = T;
+      h.out_dtype = dtype;
+      h.out = reinterpret_cast<char*>(d_hidden);
+      h.ldo_m = D;
+      h.ldo_n = 1;
+      h.vec_ok = (reinterpret_cast<uintptr_t>(d_hidden) % 16) == 0;
+      h.b_row_offset = v0;
+      h.accumulate = v0 > 0;
+      rc = launch_gemm<BN, 4, false, true, EPI_F32>(tmG_k, tmC_mn, h, ((T + BM - 1) / BM) * h.n_tiles, stream);
+      if (rc != ZS_OK) return rc;
+    }
+    // (3) d_classifier[v0:v0+vc] = G^T @ hidden
+    if (d_classifier) {
+      GemmArgs w{};
+      w.mode = MODE_XTY;
+      w.num_experts = 1;
+      w.n_tiles = (int)((D + BN - 1) / BN);
+      w.m_tiles_xty = (int)((vc + BM - 1) / BM);
+      w.M_xty = (int)vc;
+      w.N_out = (int)D;
+      w.n_rows = T;
+      w.out_dtype = dtype;
+      w.out = reinterpret_cast<char*>(d_classifier + v0 * D);
+      w.ldo_m = D;
+      w.ldo_n = 1;
+      w.out_se = 0;
+      w.vec_ok = (reinterpret_cast<uintptr_t>(d_classifier) % 16) == 0;
+      w.accumulate = 0;
+      rc = launch_gemm<BN, 4, true, true, EPI_F32>(tmG_mn, tmH_mn, w, (int64_t)w.m_tiles_xty * w.n_tiles, stream);
+      if (rc != ZS_OK) return rc;
+    }
+  }
+  return ZS_OK;
 }

@@ -242,6 +242,41 @@ int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const void* W2, int6
                            const void* dyg, int64_t dyg_sm, const int64_t* sorted_expert_idxs,
                            const int64_t* expert_offsets, int64_t n, int dtype, void* stream);
 
+/* ------------------------------------------------ cross entropy (a16-a18) */
+
+/*
+ * Multi-target cut cross entropy, raw-token mean (modeling/mcce_fast.py:21-31,
+ * mcce_fast_v2.py:329-408) and, with s_max = 1 and s = 0 on ignored rows, the
+ * standard next-token CE of linear_cross_entropy(e, c, targets,
+ * ignore_index) as main.py:761 calls it:
+ *   lse_t  = logsumexp_v(hidden[t] . classifier[v])
+ *   loss   = (sum_t s_t * lse_t - sum_t sum_{j<s_t} z[t, labels[t, j]]) / sum_t s_t
+ * The logits are never stored: one tensor-core GEMM pass keeps per-tile
+ * (max, sum exp) partials and the target logits (workspace:
+ * zs_xent_forward_workspace(T, V) bytes).  hidden [T, D], classifier [V, D]
+ * (row strides h_sm / c_sm), labels int64 [T, s_max] (s_max <= 8; only the
+ * first s_t of a row are read), s_count int32 [T].  Outputs (f32, device):
+ * lse [T], row_loss [T], loss [1], denom [1] = sum_t s_t.
+ */
+size_t zs_xent_forward_workspace(int64_t T, int64_t V);
+int zs_xent_forward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, const void* classifier, int64_t V,
+                    int64_t c_sm, const int64_t* labels, int s_max, const int* s_count, float* lse, float* row_loss,
+                    float* loss, float* denom, void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * Backward of zs_xent_forward: dz[t, v] = (grad_loss / denom) * (s_t * softmax_t[v] - count_t(v))
+ * recomputed per vocabulary slice of v_chunk columns (a multiple of 256); the
+ * slice's dz lives only in the workspace (zs_xent_backward_workspace bytes):
+ *   d_hidden     (f32 [T, D])  = dz @ classifier   (either output may be NULL)
+ *   d_classifier (f32 [V, D])  = dz^T @ hidden
+ * grad_loss and denom are device scalars (f32).
+ */
+size_t zs_xent_backward_workspace(int64_t T, int64_t v_chunk, int dtype);
+int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, const void* classifier, int64_t V,
+                     int64_t c_sm, const int64_t* labels, int s_max, const int* s_count, const float* lse,
+                     const float* grad_loss, const float* denom, float* d_hidden, float* d_classifier, int64_t v_chunk,
+                     void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

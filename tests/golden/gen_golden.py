@@ -150,10 +150,68 @@ def main():
     all_cases.update(gen_fsc(parallel_experts))
     all_cases.update(gen_ops(ops, parallel_experts))
     all_cases.update(gen_glu(mlp))
+    all_cases.update(gen_mcce())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
 
 
-if __name__ == "__main__":
+
+
+def gen_mcce():
+    """MCCE fixtures from the reference's own CPU paths: the naive formulation
+    (modeling/mcce_fast.py:117-139) for the loss and autograd gradients, and
+    the chunked exact path (:147-249) as a second opinion."""
+    from modeling import mcce_fast
+
+    cases = {}
+    shapes = {"mcce_selftest": (17, 64, 1009, 4, 123), "mcce_t1": (1, 16, 33, 1, 5), "mcce_t7": (7, 32, 127, 2, 6),
+              "mcce_t33": (33, 64, 2099, 8, 7)}
+    for name, (T, D, V, S_MAX, seed) in shapes.items():
+        g = torch.Generator().manual_seed(seed)
+        hidden = torch.randn(T, D, generator=g) / D ** 0.5
+        emb = torch.randn(V, D, generator=g) / D ** 0.5 * (3.0 if name == "mcce_selftest" else 1.0)
+        s = torch.randint(1, S_MAX + 1, (T,), generator=g, dtype=torch.int32)
+        labels = torch.randint(0, V, (T, S_MAX), generator=g, dtype=torch.int64)
+        if S_MAX >= 2:
+            labels[:, 1] = labels[:, 0]                       # duplicate labels count twice
+        cols = torch.arange(S_MAX)[None, :]
+        labels = torch.where(cols < s[:, None].long(), labels, torch.full_like(labels, V + 777))  # never read
+        h1 = hidden.clone().requires_grad_(True)
+        e1 = emb.clone().requires_grad_(True)
+        loss = mcce_fast.naive_mcce_raw_token_mean(h1, e1, labels, s)
+        loss.backward()
+        h2 = hidden.clone().requires_grad_(True)
+        e2 = emb.clone().requires_grad_(True)
+        loss2 = mcce_fast.mcce_raw_token_mean(h2, e2, labels, s, use_triton=False, v_chunk_size=128)
+        loss2.backward()
+        # the reference's two CPU paths agree with each other
+        assert torch.allclose(loss, loss2, rtol=1e-5, atol=1e-6)
+        assert torch.allclose(h1.grad, h2.grad, rtol=1e-4, atol=1e-6)
+        assert torch.allclose(e1.grad, e2.grad, rtol=1e-4, atol=1e-6)
+        cases[name] = dict(hidden=_np(hidden), emb=_np(emb), labels=_np(labels), s=_np(s), loss=_np(loss),
+                           dH=_np(h1.grad), dE=_np(e1.grad))
+    # standard CE with ignore_index, as F.cross_entropy defines it
+    g = torch.Generator().manual_seed(9)
+    T, D, V = 50, 48, 777
+    e = torch.randn(T, D, generator=g) / D ** 0.5
+    c = torch.randn(V, D, generator=g)
+    t = torch.randint(0, V, (T,), generator=g)
+    t[::7] = -100
+    e1 = e.clone().requires_grad_(True)
+    c1 = c.clone().requires_grad_(True)
+    loss = torch.nn.functional.cross_entropy(e1 @ c1.T, t, ignore_index=-100)
+    loss.backward()
+    cases["cce_ignore"] = dict(e=_np(e), c=_np(c), targets=_np(t), loss=_np(loss), de=_np(e1.grad), dc=_np(c1.grad))
+    return cases
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "mcce":
+    sys.path.insert(0, REF)
+    for name, arrs in gen_mcce().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name)
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") != "mcce":
     main()
