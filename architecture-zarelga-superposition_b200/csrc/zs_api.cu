@@ -33,3 +33,5 @@ extern "C" int zs_device_error_clear(void* stream) {
   ZS_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
   return ZS_OK;
 }
+
+extern "C" int zs_last_cuda_error(void) { return zs_last_cuda_error_ref(); }

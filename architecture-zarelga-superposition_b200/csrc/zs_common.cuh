@@ -233,8 +233,46 @@ __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2hal
     if (!(cond)) return (code); \
   } while (0)
 
+// Last CUDA runtime / driver error seen by an entry point (host side, for
+// zs_last_cuda_error()).
+inline int& zs_last_cuda_error_ref() {
+  static thread_local int v = 0;
+  return v;
+}
+
 #define ZS_CUDA_TRY(expr)                          \
   do {                                             \
     cudaError_t e_ = (expr);                       \
-    if (e_ != cudaSuccess) return ZS_ERR_CUDA;     \
+    if (e_ != cudaSuccess) {                       \
+      zs_last_cuda_error_ref() = (int)e_;          \
+      return ZS_ERR_CUDA;                          \
+    }                                              \
+  } while (0)
+
+// Make the primary context of the device that owns `p` current on the calling
+// thread.  Entry points may be called from threads where no context is
+// current yet (autograd runs backward passes on its own worker threads), and
+// this library links its own CUDA runtime, whose notion of the current device
+// is independent of the caller's.  A host pointer is rejected.
+inline int zs_bind_device(const void* p) {
+  if (p == nullptr) return ZS_OK;
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, p);
+  if (e != cudaSuccess) {
+    zs_last_cuda_error_ref() = (int)e;
+    return ZS_ERR_CUDA;
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return ZS_ERR_ARG;
+  e = cudaSetDevice(a.device);
+  if (e != cudaSuccess) {
+    zs_last_cuda_error_ref() = (int)e;
+    return ZS_ERR_CUDA;
+  }
+  return ZS_OK;
+}
+
+#define ZS_BIND(ptr)                       \
+  do {                                     \
+    const int rc_ = zs_bind_device(ptr);   \
+    if (rc_ != ZS_OK) return rc_;          \
   } while (0)

@@ -903,7 +903,11 @@ static int make_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t inner
   CUresult r = fn(m, dtype == ZS_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                   const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? ZS_OK : ZS_ERR_CUDA;
+  if (r != CUDA_SUCCESS) {
+    zs_last_cuda_error_ref() = 100000 + (int)r;  // driver result codes, offset
+    return ZS_ERR_CUDA;
+  }
+  return ZS_OK;
 }
 
 int num_sms() {
@@ -965,6 +969,7 @@ extern "C" int zs_scatter2scatter(void* out, int64_t out_sm, const void* W, int6
   ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0 && fan_out >= 1, ZS_ERR_SHAPE);
   ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
   ZS_REQUIRE(x_grouped ? (x_rows == n) : (x_rows * fan_out == n), ZS_ERR_SHAPE);
+  ZS_BIND(X);
   if (n == 0) return ZS_OK;
   const int es = elem_size(dtype);
 
@@ -1047,6 +1052,7 @@ extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw
   ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
   ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
+  ZS_BIND(DY);
   const int es = elem_size(dtype);
   constexpr int BN = 256;
 
@@ -1114,6 +1120,7 @@ extern "C" int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64
   ZS_REQUIRE(K >= 1 && F >= 1 && n >= 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && F < (int64_t)1 << 23, ZS_ERR_SHAPE);
   ZS_REQUIRE(num_experts * 2 * F < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_BIND(Xg);
   if (n == 0) return ZS_OK;
   const int es = elem_size(dtype);
   constexpr int BN = 256;
@@ -1158,6 +1165,7 @@ extern "C" int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const voi
   ZS_REQUIRE(K >= 1 && F >= 1 && n >= 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && F < (int64_t)1 << 23, ZS_ERR_SHAPE);
   ZS_REQUIRE(num_experts * K < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_BIND(dyg);
   if (n == 0) return ZS_OK;
   const int es = elem_size(dtype);
   constexpr int BN = 256;
@@ -1274,6 +1282,7 @@ extern "C" int zs_xent_forward(const void* hidden, int64_t T, int64_t D, int64_t
   ZS_REQUIRE(T >= 1 && D >= 1 && V >= 1 && s_max >= 1 && s_max <= 8, ZS_ERR_SHAPE);
   ZS_REQUIRE(T < ((int64_t)1 << 31) && V < ((int64_t)1 << 31) && D < ((int64_t)1 << 24), ZS_ERR_SHAPE);
   ZS_REQUIRE(workspace && workspace_bytes >= zs_xent_forward_workspace(T, V), ZS_ERR_WORKSPACE);
+  ZS_BIND(hidden);
   const int es = elem_size(dtype);
   constexpr int BN = 256;
   const int64_t n_vt = (V + BN - 1) / BN;
@@ -1336,6 +1345,7 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
   ZS_REQUIRE(v_chunk >= 256 && v_chunk % 256 == 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(workspace && workspace_bytes >= zs_xent_backward_workspace(T, v_chunk, dtype), ZS_ERR_WORKSPACE);
   ZS_REQUIRE((D * 4) % 16 == 0, ZS_ERR_ALIGN);
+  ZS_BIND(hidden);
   const int es = elem_size(dtype);
   constexpr int BN = 256;
   const int64_t pitch = ((v_chunk * es + 15) / 16) * 16 / es;

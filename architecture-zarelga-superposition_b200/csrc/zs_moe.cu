@@ -208,6 +208,7 @@ extern "C" int zs_group(const void* A, int64_t a_sm, int64_t K, void* Y, int64_t
   ZS_REQUIRE(A && Y && sorted_scattered_idxs, ZS_ERR_ARG);
   ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16 || dtype == ZS_F32, ZS_ERR_DTYPE);
   ZS_REQUIRE(coeff == nullptr || coeff_dtype == ZS_BF16 || coeff_dtype == ZS_F16 || coeff_dtype == ZS_F32,
+  ZS_BIND(A);
              ZS_ERR_DTYPE);
   ZS_REQUIRE(K >= 0 && n >= 0 && fan_out >= 1, ZS_ERR_SHAPE);
   return launch_group(A, a_sm, K, Y, y_sm, n, coeff, coeff_dtype, fan_out, sorted_scattered_idxs, dtype,
@@ -220,6 +221,7 @@ extern "C" int zs_rowwise_sum_product(void* out, int out_dtype, int64_t o_s0, in
                                       void* stream) {
   ZS_REQUIRE(out && A && B, ZS_ERR_ARG);
   ZS_REQUIRE(T >= 0 && F >= 0 && H >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(A);
   if (T * F == 0) return ZS_OK;
   const int vec = a_dtype != ZS_F32 && b_dtype != ZS_F32 && a_s2 == 1 && b_s1 == 1 && H % 8 == 0 &&
                   (a_s0 % 8 == 0) && (a_s1 % 8 == 0) && (b_s0 % 8 == 0) &&
@@ -237,6 +239,7 @@ extern "C" int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int6
   ZS_REQUIRE(out && in, ZS_ERR_ARG);
   ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
   ZS_REQUIRE(T >= 0 && k >= 1 && k <= 32 && C >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(in);
   if (T == 0 || C == 0) return ZS_OK;
   const int vec = C % 8 == 0 && o_sm % 8 == 0 && i_sm % 8 == 0 &&
                   ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(in)) % 16 == 0);
@@ -274,6 +277,7 @@ extern "C" int zs_swiglu_backward(void* dhfull, const void* dact, const void* hf
                                   void* stream) {
   ZS_REQUIRE(dhfull && dact && hfull, ZS_ERR_ARG);
   ZS_REQUIRE(n >= 0 && F >= 1, ZS_ERR_SHAPE);
+  ZS_BIND(dact);
   if (n == 0) return ZS_OK;
   int64_t blocks = (n * F + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;

@@ -332,6 +332,7 @@ extern "C" int zs_moe_gate_topk(const void* gate_probs, int probs_dtype, const f
   ZS_REQUIRE(num_experts >= 1 && num_experts <= 1024, ZS_ERR_SHAPE);
   ZS_REQUIRE(top_k >= 1 && top_k <= 32 && top_k <= num_experts, ZS_ERR_SHAPE);
   ZS_REQUIRE(num_tokens >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(gate_probs);
   if (num_tokens == 0) return ZS_OK;
   switch (probs_dtype) {
     case ZS_F32:
@@ -360,6 +361,7 @@ extern "C" int zs_flatten_sort_count(const int64_t* expert_idxs, int64_t n, int 
   ZS_REQUIRE(n == 0 || (expert_idxs && sorted_expert_idxs && sorted_scattered_idxs), ZS_ERR_ARG);
   ZS_REQUIRE(num_experts >= 1 && num_experts <= 4096, ZS_ERR_SHAPE);
   ZS_REQUIRE(n >= 0 && n < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_BIND(expert_offsets);
   if (n == 0) {
     ZS_CUDA_TRY(cudaMemsetAsync(expert_offsets, 0, sizeof(int64_t) * num_experts, stream));
     return ZS_OK;
@@ -406,6 +408,7 @@ extern "C" int zs_bincount(const int64_t* x, int64_t n, int minlength, int64_t* 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(out && (n == 0 || x), ZS_ERR_ARG);
   ZS_REQUIRE(minlength >= 1 && minlength <= 49152 && n >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(out);
   ZS_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(int64_t) * minlength, stream));
   return launch_count(x, nullptr, n, 1, minlength, out, stream);
 }
@@ -415,6 +418,7 @@ extern "C" int zs_expert_counts(const int64_t* topk_idx, const uint8_t* valid, i
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(counts && (num_tokens == 0 || topk_idx), ZS_ERR_ARG);
   ZS_REQUIRE(num_experts >= 1 && num_experts <= 49152 && top_k >= 1 && num_tokens >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(counts);
   return launch_count(topk_idx, valid, num_tokens * top_k, top_k, num_experts, counts, stream);
 }
 
@@ -422,6 +426,7 @@ extern "C" int zs_bias_sign_update(const int64_t* counts, int num_experts, float
                                    void* stream_) {
   ZS_REQUIRE(counts && expert_biases, ZS_ERR_ARG);
   ZS_REQUIRE(num_experts >= 1, ZS_ERR_SHAPE);
+  ZS_BIND(counts);
   bias_sign_update_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream_)>>>(counts, num_experts, update_rate,
                                                                              expert_biases);
   return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
@@ -482,6 +487,7 @@ extern "C" int zs_moe_gate_topk_backward(const void* gate_probs, int probs_dtype
   ZS_REQUIRE(gate_probs && topk_idx && grad_weight && grad_probs, ZS_ERR_ARG);
   ZS_REQUIRE(num_experts >= 1 && num_experts <= 1024 && top_k >= 1 && top_k <= 32 && num_tokens >= 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(grad_dtype == probs_dtype, ZS_ERR_DTYPE);
+  ZS_BIND(gate_probs);
   if (num_tokens == 0) return ZS_OK;
   int64_t blocks = (num_tokens + 7) / 8;
   if (blocks > 148 * 32) blocks = 148 * 32;
@@ -541,6 +547,7 @@ extern "C" int zs_flatten_sort_count_noalloc(const int64_t* expert_idxs, int64_t
                                              int64_t* sorted_expert_idxs, int64_t* sorted_scattered_idxs,
                                              int64_t* expert_offsets, void* stream) {
   ZS_REQUIRE(num_experts >= 1 && num_experts <= 4096 && n >= 0 && n < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_BIND(expert_offsets);
   const size_t need = zs_flatten_sort_count_workspace(n, num_experts);
   if ((int64_t)(need / sizeof(int)) > ZS_FSC_NOALLOC_MAX_INTS) return ZS_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;

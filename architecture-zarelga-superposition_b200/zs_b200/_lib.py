@@ -26,6 +26,7 @@ _SIGNATURES = {
     "zs_error_string": (ctypes.c_char_p, [_i32]),
     "zs_device_error_get": (_i32, [ctypes.POINTER(_i32), _vp]),
     "zs_device_error_clear": (_i32, [_vp]),
+    "zs_last_cuda_error": (_i32, []),
     "zs_moe_gate_topk": (_i32, [_vp, _i32, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
     "zs_moe_gate_topk_backward": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp]),
     "zs_flatten_sort_count_workspace": (_sz, [_i64, _i32]),
@@ -85,7 +86,10 @@ def exported_symbols():
 def check(rc: int, what: str) -> None:
     if rc != 0:
         msg = lib().zs_error_string(rc).decode()
-        raise ZsError(f"{what} failed: {msg} (zs code {rc})")
+        extra = ""
+        if rc == 5:
+            extra = f", CUDA error {lib().zs_last_cuda_error()}"
+        raise ZsError(f"{what} failed: {msg} (zs code {rc}{extra})")
 
 
 def dtype_code(dt: torch.dtype) -> int:

@@ -58,6 +58,9 @@ const char* zs_error_string(int code);
 int zs_device_error_get(int* out, void* stream);
 /* Clear the device error word (stream-ordered). */
 int zs_device_error_clear(void* stream);
+/* The cudaError_t of the last failed CUDA runtime call behind a ZS_ERR_CUDA
+ * return on this host thread (driver CUresult codes are reported + 100000). */
+int zs_last_cuda_error(void);
 
 /* ------------------------------------------------------------- routing (a1-a3) */
 
