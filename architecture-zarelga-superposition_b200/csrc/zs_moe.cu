@@ -208,9 +208,9 @@ extern "C" int zs_group(const void* A, int64_t a_sm, int64_t K, void* Y, int64_t
   ZS_REQUIRE(A && Y && sorted_scattered_idxs, ZS_ERR_ARG);
   ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16 || dtype == ZS_F32, ZS_ERR_DTYPE);
   ZS_REQUIRE(coeff == nullptr || coeff_dtype == ZS_BF16 || coeff_dtype == ZS_F16 || coeff_dtype == ZS_F32,
-  ZS_BIND(A);
              ZS_ERR_DTYPE);
   ZS_REQUIRE(K >= 0 && n >= 0 && fan_out >= 1, ZS_ERR_SHAPE);
+  ZS_BIND(A);
   return launch_group(A, a_sm, K, Y, y_sm, n, coeff, coeff_dtype, fan_out, sorted_scattered_idxs, dtype,
                       static_cast<cudaStream_t>(stream));
 }

@@ -372,6 +372,80 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_config3(args):
+    """cut cross entropy forward + backward, bf16, hidden
+    16384 x 2048 N(0,1), classifier 131072 x 2048 N(0,0.02), uniform targets
+    with 5 % ignore_index (CCE) or 4 targets per position (--mcce)."""
+    import torch
+
+    from zs_b200 import _lib as Z
+    from zs_b200.xent import fused_linear_cross_entropy
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    T, D, V = (args.tokens or 16384), 2048, 131072
+    g = torch.Generator(device=dev).manual_seed(3)
+    h = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    c = (torch.randn(V, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    if args.mcce:
+        labels = torch.randint(0, V, (T, 4), device=dev, generator=g)
+        s = torch.full((T,), 4, dtype=torch.int32, device=dev)
+    else:
+        labels = torch.randint(0, V, (T, 1), device=dev, generator=g)
+        s = (torch.rand(T, device=dev, generator=g) >= 0.05).to(torch.int32)
+
+    def step():
+        hh = h.detach().requires_grad_(True)
+        cc = c.detach().requires_grad_(True)
+        loss = fused_linear_cross_entropy(hh, cc, labels, s)
+        loss.backward()
+        return loss
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    Z.INSTR.events = {}
+    Z.INSTR.timing = True
+    l0 = Z.INSTR.launches
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.5)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ht0 = time.time()
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ht1 = time.time()
+    Z.INSTR.timing = False
+    clocks = sampler.stop(ht0, ht1)
+    ms = t0.elapsed_time(t1)
+    kern = {}
+    for name, evs in Z.INSTR.events.items():
+        durs = [a.elapsed_time(b) for a, b in evs]
+        kern[name] = {"launches": len(durs), "avg_ms": sum(durs) / len(durs)}
+    _, sustained, _, src = measured_peaks()
+    fl = 3 * 2 * T * V * D  # algorithmic: forward logits, dH, dW (the backward's logit recompute excluded)
+    executed = 4 * 2 * T * V * D
+    value = T * args.steps / (ms * 1e-3)
+    achieved = executed * args.steps / (ms * 1e-3) / 1e12
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": ("config3: MCCE 4 targets" if args.mcce else "config3: CCE 5% ignored")
+                       + f", fwd+bwd, T={T} D={D} V={V}, bf16",
+                       "algorithmic_tflop_per_step": fl / 1e12, "executed_tflop_per_step": executed / 1e12,
+                       "useful_tflops": fl * args.steps / (ms * 1e-3) / 1e12},
+            "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (classifier GEMMs: LSE forward, "
+                                                      "logit-gradient recompute, dH, dW)",
+                         "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                         "traffic": None, "peak_source": f"{src} bf16_tflops_sustained", "kernels": kern},
+            "gpu_launches": Z.INSTR.launches - l0, "clocks": clocks, "device_error": Z.device_error()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -381,9 +455,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: config 2's 16384)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3], help="BASELINE config (default 2)")
+    ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 3:
+        run_config3(args)
     else:
         run_gpu(args)
 
