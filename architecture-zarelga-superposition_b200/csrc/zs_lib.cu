@@ -4,4 +4,5 @@
 #include "zs_gemm.cu"
 #include "zs_moe.cu"
 #include "zs_routing.cu"
+#include "zs_norm.cu"
 #include "zs_api.cu"

@@ -1,0 +1,217 @@
+// Bandwidth-bound kernels around attention:
+//   * zero-centred RMSNorm forward/backward (modeling/zRMSNorm.py:4-20):
+//       y = x * rsqrt(mean(x^2) + eps) * (1 + w), computed in f32, stored in
+//       the input dtype; backward gives dx and the f32 weight gradient.
+//   * rotate-half RoPE with separate Q/K cos/sin tables, in place
+//     (modeling/liger_rope.py:20-119): pairs (i, i + hd/2) of every head are
+//     rotated by the row's angle; the backward rotates by the negative angle.
+#include "zs_common.cuh"
+
+namespace zs {
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) {
+  return to_f32<T>(*p);
+}
+
+// One warp per row; each lane keeps its slice of the row in registers when
+// d <= 32 * MAXV (else the row is re-read from L1/L2).
+template <typename T, typename W>
+__global__ void zrmsnorm_fwd_kernel(const T* __restrict__ x, const W* __restrict__ w, T* __restrict__ y,
+                                    float* __restrict__ rstd, int64_t rows, int d, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const T* xr = x + r * d;
+    float ss = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float v = ldf(xr + c);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    // torch: x.pow(2).mean(-1) + eps, then rsqrt, all f32
+    const float rs = rsqrtf(ss / (float)d + eps);
+    if (lane == 0 && rstd != nullptr) rstd[r] = rs;
+    T* yr = y + r * d;
+    for (int c = lane; c < d; c += 32) yr[c] = from_f32<T>((ldf(xr + c) * rs) * (1.0f + ldf(w + c)));
+  }
+}
+
+// dx = rs * (dn - n * mean(dn * n)),  dn = dy * (1 + w),  n = x * rs;
+// dw partial sums per block: part[blockIdx][c] = sum over this block's rows of dy * n.
+template <typename T, typename W>
+__global__ void zrmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const W* __restrict__ w,
+                                    const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw_part,
+                                    int64_t rows, int d) {
+  extern __shared__ float sdw[];  // [d] per block
+  for (int c = threadIdx.x; c < d; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const T* xr = x + r * d;
+    const T* dyr = dy + r * d;
+    const float rs = rstd[r];
+    float dot = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float n = ldf(xr + c) * rs;
+      const float g = ldf(dyr + c);
+      dot = fmaf(g * (1.0f + ldf(w + c)), n, dot);
+      atomicAdd(&sdw[c], g * n);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / (float)d;
+    T* dxr = dx + r * d;
+    for (int c = lane; c < d; c += 32) {
+      const float n = ldf(xr + c) * rs;
+      const float dn = ldf(dyr + c) * (1.0f + ldf(w + c));
+      dxr[c] = from_f32<T>(rs * (dn - n * mean));
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) dw_part[(int64_t)blockIdx.x * d + c] = sdw[c];
+}
+
+__global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int d, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= d) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * d + c];
+  out[c] = s;
+}
+
+// One block per (batch, position) row: all q heads then all k heads.
+template <typename T, typename C>
+__global__ void rope_kernel(T* __restrict__ q, int64_t q_row_stride, T* __restrict__ k, int64_t k_row_stride,
+                            const C* __restrict__ q_cos, const C* __restrict__ q_sin, const C* __restrict__ k_cos,
+                            const C* __restrict__ k_sin, int64_t cos_row_stride, int64_t rows, int seq_len,
+                            int cos_bs, int n_qh, int n_kh, int hd, int backward) {
+  const int half = hd / 2;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t b = r / seq_len, s = r % seq_len;
+    const int64_t crow = (cos_bs == 1 ? s : b * seq_len + s) * cos_row_stride;
+    const int total = (n_qh + n_kh) * half;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const bool isq = i < n_qh * half;
+      const int j = isq ? i : i - n_qh * half;
+      const int h = j / half, p = j - h * half;
+      T* base = isq ? q + r * q_row_stride + (int64_t)h * hd : k + r * k_row_stride + (int64_t)h * hd;
+      const float c = to_f32<C>((isq ? q_cos : k_cos)[crow + p]);
+      const float sn = to_f32<C>((isq ? q_sin : k_sin)[crow + p]);
+      const float x1 = to_f32<T>(base[p]);
+      const float x2 = to_f32<T>(base[p + half]);
+      if (!backward) {
+        base[p] = from_f32<T>(x1 * c - x2 * sn);
+        base[p + half] = from_f32<T>(x2 * c + x1 * sn);
+      } else {
+        base[p] = from_f32<T>(x1 * c + x2 * sn);
+        base[p + half] = from_f32<T>(x2 * c - x1 * sn);
+      }
+    }
+  }
+}
+
+}  // namespace zs
+
+using namespace zs;
+
+#define ZS_DISPATCH_XW(xdt, wdt, ...)                                               \
+  do {                                                                              \
+    if (xdt == ZS_BF16 && wdt == ZS_F32) {                                          \
+      using TX = __nv_bfloat16; using TW = float; __VA_ARGS__;                      \
+    } else if (xdt == ZS_F32 && wdt == ZS_F32) {                                    \
+      using TX = float; using TW = float; __VA_ARGS__;                              \
+    } else if (xdt == ZS_F16 && wdt == ZS_F32) {                                    \
+      using TX = __half; using TW = float; __VA_ARGS__;                             \
+    } else if (xdt == ZS_BF16 && wdt == ZS_BF16) {                                  \
+      using TX = __nv_bfloat16; using TW = __nv_bfloat16; __VA_ARGS__;              \
+    } else {                                                                        \
+      return ZS_ERR_DTYPE;                                                          \
+    }                                                                               \
+  } while (0)
+
+extern "C" int zs_zrmsnorm_forward(const void* x, const void* weight, void* y, float* rstd, int64_t rows, int d,
+                                   float eps, int x_dtype, int w_dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(x && weight && y, ZS_ERR_ARG);
+  ZS_REQUIRE(rows >= 0 && d >= 1, ZS_ERR_SHAPE);
+  ZS_BIND(x);
+  if (rows == 0) return ZS_OK;
+  int64_t blocks = (rows + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  ZS_DISPATCH_XW(x_dtype, w_dtype,
+                 zrmsnorm_fwd_kernel<TX, TW><<<(unsigned)blocks, 256, 0, stream>>>(
+                     reinterpret_cast<const TX*>(x), reinterpret_cast<const TW*>(weight), reinterpret_cast<TX*>(y),
+                     rstd, rows, d, eps));
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" size_t zs_zrmsnorm_backward_workspace(int64_t rows, int d) {
+  return (size_t)296 * d * sizeof(float);
+}
+
+extern "C" int zs_zrmsnorm_backward(const void* dy, const void* x, const void* weight, const float* rstd, void* dx,
+                                    float* dweight, int64_t rows, int d, int x_dtype, int w_dtype, void* workspace,
+                                    size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(dy && x && weight && rstd && dx && dweight, ZS_ERR_ARG);
+  ZS_REQUIRE(rows >= 0 && d >= 1 && d <= 12288, ZS_ERR_SHAPE);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_zrmsnorm_backward_workspace(rows, d), ZS_ERR_WORKSPACE);
+  ZS_BIND(x);
+  int64_t blocks = (rows + 7) / 8;
+  if (blocks > 296) blocks = 296;
+  if (blocks < 1) blocks = 1;
+  float* part = reinterpret_cast<float*>(workspace);
+  const size_t sh = (size_t)d * sizeof(float);
+  ZS_DISPATCH_XW(x_dtype, w_dtype, {
+    if (sh > 48 * 1024) {
+      ZS_CUDA_TRY(cudaFuncSetAttribute(zrmsnorm_bwd_kernel<TX, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sh));
+    }
+    zrmsnorm_bwd_kernel<TX, TW><<<(unsigned)blocks, 256, sh, stream>>>(
+        reinterpret_cast<const TX*>(dy), reinterpret_cast<const TX*>(x), reinterpret_cast<const TW*>(weight), rstd,
+        reinterpret_cast<TX*>(dx), part, rows, d);
+  });
+  ZS_CUDA_TRY(cudaGetLastError());
+  sum_rows_kernel<<<(d + 255) / 256, 256, 0, stream>>>(part, (int)blocks, d, dweight);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos,
+                       const void* q_sin, const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch,
+                       int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim, int dtype,
+                       int table_dtype, int backward, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(q && k && q_cos && q_sin && k_cos && k_sin, ZS_ERR_ARG);
+  ZS_REQUIRE(batch >= 0 && seq_len >= 1 && n_q_heads >= 1 && n_kv_heads >= 1 && head_dim >= 2 && head_dim % 2 == 0,
+             ZS_ERR_SHAPE);
+  ZS_REQUIRE(cos_batch == 1 || cos_batch == batch, ZS_ERR_SHAPE);
+  ZS_BIND(q);
+  const int64_t rows = (int64_t)batch * seq_len;
+  if (rows == 0) return ZS_OK;
+  int64_t blocks = rows < 148 * 32 ? rows : 148 * 32;
+  const int threads = 128;
+#define ZS_ROPE(T, C)                                                                                            \
+  rope_kernel<T, C><<<(unsigned)blocks, threads, 0, stream>>>(                                                 \
+      reinterpret_cast<T*>(q), q_row_stride, reinterpret_cast<T*>(k), k_row_stride,                            \
+      reinterpret_cast<const C*>(q_cos), reinterpret_cast<const C*>(q_sin), reinterpret_cast<const C*>(k_cos), \
+      reinterpret_cast<const C*>(k_sin), cos_row_stride, rows, seq_len, cos_batch, n_q_heads, n_kv_heads,      \
+      head_dim, backward)
+  if (dtype == ZS_BF16 && table_dtype == ZS_F32)
+    ZS_ROPE(__nv_bfloat16, float);
+  else if (dtype == ZS_BF16 && table_dtype == ZS_BF16)
+    ZS_ROPE(__nv_bfloat16, __nv_bfloat16);
+  else if (dtype == ZS_F32 && table_dtype == ZS_F32)
+    ZS_ROPE(float, float);
+  else if (dtype == ZS_F16 && table_dtype == ZS_F32)
+    ZS_ROPE(__half, float);
+  else
+    return ZS_ERR_DTYPE;
+#undef ZS_ROPE
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}

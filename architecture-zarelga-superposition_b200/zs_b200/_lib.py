@@ -48,6 +48,11 @@ _SIGNATURES = {
     "zs_expert_up_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
     "zs_swiglu_backward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "zs_expert_down_dswiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
+    "zs_zrmsnorm_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _i32, _i32, _vp]),
+    "zs_zrmsnorm_backward_workspace": (_sz, [_i64, _i32]),
+    "zs_zrmsnorm_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "zs_rope": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                       _i32, _vp]),
     "zs_xent_forward_workspace": (_sz, [_i64, _i64]),
     "zs_xent_forward": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                _i32, _vp]),

@@ -245,6 +245,41 @@ int zs_expert_down_dswiglu(void* dhfull, const void* hfull, const void* W2, int6
                            const void* dyg, int64_t dyg_sm, const int64_t* sorted_expert_idxs,
                            const int64_t* expert_offsets, int64_t n, int dtype, void* stream);
 
+/* ------------------------------------------------ norm and RoPE (a12, a14) */
+
+/*
+ * ZeroCenteredRMSNorm.forward (modeling/zRMSNorm.py:13-17), rows of length d:
+ *   y = x * rsqrt(mean(x^2) + eps) * (1 + w)   in f32, stored in x's dtype.
+ * rstd (f32 [rows], nullable) keeps rsqrt(...) for the backward.
+ * Dtypes: x/y ZS_BF16 | ZS_F16 | ZS_F32; weight ZS_F32 (or ZS_BF16 with bf16 x).
+ */
+int zs_zrmsnorm_forward(const void* x, const void* weight, void* y, float* rstd, int64_t rows, int d, float eps,
+                        int x_dtype, int w_dtype, void* stream);
+/*
+ * Backward of zs_zrmsnorm_forward (autograd of modeling/zRMSNorm.py:13-17):
+ *   dx = r * (dn - n * mean(dn * n)),  n = x * r,  dn = dy * (1 + w)   (x's dtype)
+ *   dweight = sum over rows of dy * n                                   (f32 [d])
+ * d <= 12288; workspace: zs_zrmsnorm_backward_workspace(rows, d) bytes.
+ */
+size_t zs_zrmsnorm_backward_workspace(int64_t rows, int d);
+int zs_zrmsnorm_backward(const void* dy, const void* x, const void* weight, const float* rstd, void* dx,
+                         float* dweight, int64_t rows, int d, int x_dtype, int w_dtype, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/*
+ * LigerRopeFunction forward / backward (modeling/liger_rope.py:20-119, 183-206),
+ * in place on q [batch, seq, n_q_heads, head_dim] and k [batch, seq,
+ * n_kv_heads, head_dim] (row strides q_row_stride / k_row_stride per
+ * (batch, position) row; heads contiguous).  Pair (i, i + head_dim/2) of each
+ * head is rotated by the angle whose cos/sin are the tables' row entry i;
+ * tables [cos_batch (1 or batch), seq, head_dim/2] with row stride
+ * cos_row_stride.  backward != 0 rotates by the negative angle (the
+ * gradient).  Arithmetic in f32.
+ */
+int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos, const void* q_sin,
+            const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch, int seq_len, int cos_batch,
+            int n_q_heads, int n_kv_heads, int head_dim, int dtype, int table_dtype, int backward, void* stream);
+
 /* ------------------------------------------------ cross entropy (a16-a18) */
 
 /*

@@ -151,6 +151,7 @@ def main():
     all_cases.update(gen_ops(ops, parallel_experts))
     all_cases.update(gen_glu(mlp))
     all_cases.update(gen_mcce())
+    all_cases.update(gen_norm_rope())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
@@ -213,5 +214,50 @@ if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "mcce":
         print("wrote", name)
 
 
-if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") != "mcce":
+
+
+def gen_norm_rope():
+    """zRMSNorm from the reference module (CPU autograd); Liger RoPE from the
+    reference's Triton kernel under the interpreter; RoPE tables from the
+    reference's own table builder."""
+    from modeling.zRMSNorm import ZeroCenteredRMSNorm
+    from modeling import liger_rope
+    from modeling.attention import GatedAttention
+
+    cases = {}
+    g = torch.Generator().manual_seed(51)
+    for name, (rows, d) in {"zrms_d64": (37, 64), "zrms_d256": (20, 256)}.items():
+        m = ZeroCenteredRMSNorm(d, eps=1e-6)
+        with torch.no_grad():
+            m.weight.copy_(torch.randn(d, generator=g) * 0.1)
+        x = (torch.randn(rows, d, generator=g) * 2).requires_grad_(True)
+        y = m(x)
+        dy = torch.randn(rows, d, generator=g)
+        y.backward(dy)
+        cases[name] = dict(x=_np(x), w=_np(m.weight), y=_np(y), dy=_np(dy), dx=_np(x.grad), dw=_np(m.weight.grad))
+    fake = types.SimpleNamespace(pos_rope_pairs=16, pos_rope_dims=32)
+    cos_t, sin_t = GatedAttention._build_pos_rope_tables(fake, 300, 64, 10000.0, torch.float32, "cpu")
+    B, S, Hq, Hk, hd = 2, 11, 4, 2, 64
+    pos = torch.randint(0, 300, (B, S), generator=g)
+    cos, sin = cos_t[pos], sin_t[pos]
+    q = torch.randn(B, S, Hq, hd, generator=g)
+    k = torch.randn(B, S, Hk, hd, generator=g)
+    q_out, k_out = liger_rope.LigerRopeFunction.apply(q.clone(), k.clone(), cos, sin, cos, sin)
+    dq = torch.randn(B, S, Hq, hd, generator=g)
+    dk = torch.randn(B, S, Hk, hd, generator=g)
+    dq_out, dk_out = liger_rope.rope_backward(dq.clone(), dk.clone(), cos, sin, cos, sin)
+    cases["rope"] = dict(cos_table=_np(cos_t), sin_table=_np(sin_t), pos=_np(pos), q=_np(q), k=_np(k),
+                         q_out=_np(q_out), k_out=_np(k_out), dq=_np(dq), dk=_np(dk), dq_out=_np(dq_out),
+                         dk_out=_np(dk_out))
+    return cases
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "norm_rope":
+    sys.path.insert(0, REF)
+    for name, arrs in gen_norm_rope().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name)
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") is None:
     main()
