@@ -36,7 +36,7 @@ constexpr int BK = 64;
 constexpr int MAX_EXPERTS_GEMM = 1024;
 
 enum { MODE_ROWS = 0, MODE_XTY = 1 };
-enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_DSWIGLU = 2, EPI_LSE = 3, EPI_XENT_GRAD = 4, EPI_F32 = 5 };
+enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_DSWIGLU = 2, EPI_LSE = 3, EPI_XENT_GRAD = 4, EPI_F32 = 5, EPI_AXPBY = 6 };
 
 struct GemmArgs {
   int mode;
@@ -79,6 +79,8 @@ struct GemmArgs {
   const float* grad_loss;              // EPI_XENT_GRAD: device scalar dL/dloss
   const float* denom;                  // EPI_XENT_GRAD: device scalar N (total active labels)
   int accumulate;                      // EPI_F32: out += acc instead of out = acc
+  int64_t group_rows;                  // > 0: uniform groups (batched GEMM), group e = rows [e*g, (e+1)*g)
+  float alpha, beta;                   // EPI_AXPBY: out = alpha * acc + beta * aux
 };
 
 template <int BN, int STAGES>
@@ -377,6 +379,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     int64_t s;
     if (e == 0)
       s = 0;
+    else if (args.group_rows > 0)
+      s = (int64_t)e * args.group_rows;  // batched GEMM with uniform groups
     else if (args.expert_offsets == nullptr && args.sorted_expert_idxs == nullptr)
       s = args.n_rows;  // dense GEMM: one group holding every row
     else if (args.expert_offsets != nullptr)
@@ -792,6 +796,23 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             args.part_max[slot] = run_m;
             args.part_sum[slot] = run_s;
             if (tgt != 0.f) atomicAdd(args.target_sum + row, tgt);
+          }
+        } else if (EPI == EPI_AXPBY) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            const int lc = half * (BN / 2) + c * 32;
+            const int col0 = ti.nt * BN + lc;
+            const int ncols = min(32, args.N_out - col0);
+            float av[32];
+            if (ncols > 0) load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, av, DT, vec);
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + lc, r);
+            tc_wait_ld();
+            if (ncols <= 0) continue;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(args.alpha, __uint_as_float(r[j]), args.beta * av[j]);
+            emit_chunk<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, v, vec, stg);
           }
         } else if (EPI == EPI_F32) {
 #pragma unroll 1
@@ -1432,5 +1453,131 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
       if (rc != ZS_OK) return rc;
     }
   }
+  return ZS_OK;
+}
+
+
+// ------------------------------------------------------------ Newton-Schulz
+
+namespace zs {
+// Per-matrix Frobenius normalisation in the storage dtype, as
+// X / (X.norm(dim=(-2,-1), keepdim=True) + 1e-7) evaluates it on a bf16 tensor:
+// the norm (f32 accumulation) is rounded to the dtype, the sum with 1e-7 and
+// the quotient each round once more.
+template <typename T>
+__global__ void ns_normalize_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t per) {
+  const int64_t e = blockIdx.x;
+  const T* xe = x + e * per;
+  T* ye = y + e * per;
+  float ss = 0.f;
+  for (int64_t i = threadIdx.x; i < per; i += blockDim.x) {
+    const float v = to_f32<T>(xe[i]);
+    ss = fmaf(v, v, ss);
+  }
+  __shared__ float sh[32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) sh[0] = v;
+  }
+  __syncthreads();
+  const float nrm = to_f32<T>(from_f32<T>(sqrtf(sh[0])));
+  const float den = to_f32<T>(from_f32<T>(nrm + 1e-7f));
+  for (int64_t i = threadIdx.x; i < per; i += blockDim.x) ye[i] = from_f32<T>(__fdiv_rn(to_f32<T>(xe[i]), den));
+}
+}  // namespace zs
+
+extern "C" size_t zs_newton_schulz5_workspace(int64_t batch, int64_t m, int64_t n, int dtype) {
+  const int es = elem_size(dtype);
+  return (size_t)(2 * batch * m * m + batch * m * n) * es + 3 * 256;
+}
+
+extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int64_t n, int steps, float a,
+                                 float b, float c, void* workspace, size_t workspace_bytes, int dtype, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(G && X_out, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(batch >= 1 && m >= 1 && n >= m && steps >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(batch * m < ((int64_t)1 << 31) && batch <= MAX_EXPERTS_GEMM && n < ((int64_t)1 << 24), ZS_ERR_SHAPE);
+  ZS_REQUIRE((m * elem_size(dtype)) % 16 == 0 && (n * elem_size(dtype)) % 16 == 0, ZS_ERR_ALIGN);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_newton_schulz5_workspace(batch, m, n, dtype), ZS_ERR_WORKSPACE);
+  ZS_BIND(G);
+  const int es = elem_size(dtype);
+  constexpr int BN = 256;
+  char* ws = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  char* Abuf = ws;
+  char* Bbuf = Abuf + ((batch * m * m * es + 255) / 256) * 256;
+  char* Xtmp = Bbuf + ((batch * m * m * es + 255) / 256) * 256;
+  // X0 = G / (||G|| + 1e-7) -> X_out; iterate X_out -> Xtmp -> X_out ...
+  if (dtype == ZS_BF16)
+    ns_normalize_kernel<__nv_bfloat16><<<(unsigned)batch, 1024, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(G), reinterpret_cast<__nv_bfloat16*>(X_out), m * n);
+  else
+    ns_normalize_kernel<__half><<<(unsigned)batch, 1024, 0, stream>>>(reinterpret_cast<const __half*>(G),
+                                                                      reinterpret_cast<__half*>(X_out), m * n);
+  ZS_CUDA_TRY(cudaGetLastError());
+  char* X = reinterpret_cast<char*>(X_out);
+  char* Xn = Xtmp;
+  for (int it = 0; it < steps; ++it) {
+    CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128;
+    int rc;
+    if ((rc = make_tmap(&tX_k128, X, dtype, n, batch * m, n * es, 64, 128)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tX_k256, X, dtype, n, batch * m, n * es, 64, BN)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tX_mn, X, dtype, n, batch * m, n * es, 64, 64)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tA_k128, Abuf, dtype, m, batch * m, m * es, 64, 128)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tA_k256, Abuf, dtype, m, batch * m, m * es, 64, BN)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tB_k128, Bbuf, dtype, m, batch * m, m * es, 64, 128)) != ZS_OK) return rc;
+    GemmArgs g{};
+    g.mode = MODE_ROWS;
+    g.num_experts = (int)batch;
+    g.group_rows = m;
+    g.n_rows = batch * m;
+    g.out_rows = batch * m;
+    g.out_dtype = dtype;
+    g.ldo_n = 1;
+    const int64_t mt = (m + BM - 1) / BM;
+    // A = X X^T  (per matrix: M = m, N = m, K = n; B operand = X rows of the same matrix)
+    g.n_tiles = (int)((m + BN - 1) / BN);
+    g.kb_rows = (int)((n + BK - 1) / BK);
+    g.N_out = (int)m;
+    g.out = Abuf;
+    g.ldo_m = m;
+    g.b_rows_per_expert = (int)m;
+    g.vec_ok = 1;
+    if ((rc = launch_gemm<BN, 4, false, false, EPI_STORE>(tX_k128, tX_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+      return rc;
+    // B = b A + c A A   (B operand = A^T = A)
+    g.kb_rows = (int)((m + BK - 1) / BK);
+    g.out = Bbuf;
+    g.aux = Abuf;
+    g.ld_aux = m;
+    g.alpha = c;
+    g.beta = b;
+    if ((rc = launch_gemm<BN, 4, false, false, EPI_AXPBY>(tA_k128, tA_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+      return rc;
+    // X' = a X + B X    (B operand = X^T: X is [K = m rows, N = n cols] per matrix, MN-major)
+    g.n_tiles = (int)((n + BN - 1) / BN);
+    g.kb_rows = (int)((m + BK - 1) / BK);
+    g.N_out = (int)n;
+    g.out = Xn;
+    g.ldo_m = n;
+    g.aux = X;
+    g.ld_aux = n;
+    g.alpha = 1.0f;
+    g.beta = a;
+    g.b_rows_per_expert = (int)m;
+    if ((rc = launch_gemm<BN, 4, false, true, EPI_AXPBY>(tB_k128, tX_mn, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+      return rc;
+    char* t = X;
+    X = Xn;
+    Xn = t;
+  }
+  if (X != reinterpret_cast<char*>(X_out))
+    ZS_CUDA_TRY(cudaMemcpyAsync(X_out, X, (size_t)batch * m * n * es, cudaMemcpyDeviceToDevice, stream));
   return ZS_OK;
 }

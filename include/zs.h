@@ -315,6 +315,21 @@ int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, con
                      const float* grad_loss, const float* denom, float* d_hidden, float* d_classifier, int64_t v_chunk,
                      void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
+/* ------------------------------------------------ Muon (a22) */
+
+/*
+ * zeropower_via_newtonschulz5 (optimizer/muon.py:6-32) on a batch of
+ * matrices already oriented with m <= n (the caller transposes taller ones):
+ *   X = G / (||G||_F + 1e-7);  repeat `steps` times:
+ *     A = X X^T;  B = b*A + c*A A;  X = a*X + B X
+ * G, X_out: [batch, m, n] contiguous, bf16 or f16 (m and n multiples of 8).
+ * Each product is a batched tcgen05 GEMM; the linear combinations are fused
+ * into the GEMM epilogues.  Workspace: zs_newton_schulz5_workspace bytes.
+ */
+size_t zs_newton_schulz5_workspace(int64_t batch, int64_t m, int64_t n, int dtype);
+int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int64_t n, int steps, float a, float b,
+                      float c, void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

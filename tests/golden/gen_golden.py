@@ -152,6 +152,7 @@ def main():
     all_cases.update(gen_glu(mlp))
     all_cases.update(gen_mcce())
     all_cases.update(gen_norm_rope())
+    all_cases.update(gen_muon())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
@@ -261,3 +262,39 @@ if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "norm_rope":
 
 if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") is None:
     main()
+
+
+def gen_muon():
+    """Newton-Schulz output and two MuonMD steps from the reference optimizer on CPU."""
+    from optimizer import muon
+
+    cases = {}
+    g = torch.Generator().manual_seed(61)
+    Gw = torch.randn(3, 64, 128, generator=g)
+    Gt = torch.randn(2, 96, 64, generator=g)
+    cases["ns5"] = dict(G_wide=_np(Gw), X_wide=_np(muon.zeropower_via_newtonschulz5(Gw, 5).float()),
+                        G_tall=_np(Gt), X_tall=_np(muon.zeropower_via_newtonschulz5(Gt, 5).float()))
+    for gain_mode, norm_axis, rescale in [("both", "frobenius", "balanced"), ("col", "row", "muon"),
+                                          ("scalar", "frobenius", "balanced"), ("none", "col", "balanced")]:
+        W0 = torch.randn(4, 64, 96, generator=g) * 0.05
+        p = W0.clone()
+        state = {}
+        grads = [torch.randn(4, 64, 96, generator=g) * 0.01 for _ in range(2)]
+        for gr in grads:
+            muon.md_decoupled_step(p, gr.clone(), state, lr=0.02, momentum=0.95, gain_lr=1e-3,
+                                   gain_betas=(0.9, 0.95), gain_eps=1e-10, gain_mode=gain_mode, norm_axis=norm_axis,
+                                   ns_steps=5, rescale_mode=rescale)
+        out = dict(W0=_np(W0), grad0=_np(grads[0]), grad1=_np(grads[1]), W2=_np(p),
+                   momentum=_np(state["momentum_buffer"]))
+        for key in ("g_scalar", "g_row", "g_col"):
+            if key in state:
+                out[key] = _np(state[key])
+        cases[f"md_{gain_mode}_{norm_axis}"] = out
+    return cases
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "muon":
+    sys.path.insert(0, REF)
+    for name, arrs in gen_muon().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name)
