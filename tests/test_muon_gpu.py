@@ -2,7 +2,7 @@
 the reference's CPU fixtures, the oracle, and the reference formula in torch
 bf16 on the GPU (cfg 4 expert-stack shapes).  bf16 tolerance (five chained bf16 iterations): relative error
 <= 5e-2 and cosine >= 0.999 on the orthogonalised update; parameters after a
-MuonMD step within 2e-3 relative (f32 state, bf16 update)."""
+MuonMD steps within 5e-3 relative, update direction cosine >= 0.998."""
 import numpy as np
 import pytest
 import torch
@@ -66,7 +66,11 @@ def test_md_decoupled_step_reference_fixture(golden, case, gain_mode, norm_axis,
         md_decoupled_step(p, torch.tensor(gd[key], device="cuda"), state, lr=0.02, momentum=0.95, gain_lr=1e-3,
                           gain_betas=(0.9, 0.95), gain_eps=1e-10, gain_mode=gain_mode, norm_axis=norm_axis,
                           ns_steps=5, rescale_mode=rescale)
-    assert rel_err(p, gd["W2"]) < 2e-3
+    # two steps of lr 0.02 with a bf16 orthogonalised update (~5e-2 relative
+    # apart from the reference's bf16 CPU run) move p by ~4e-2; 5e-3 bounds it
+    assert rel_err(p, gd["W2"]) < 5e-3
+    w0 = torch.tensor(gd["W0"], device="cuda")
+    assert cosine(p - w0, torch.tensor(gd["W2"], device="cuda") - w0) > 0.998
     assert rel_err(state["momentum_buffer"], gd["momentum"]) < 1e-5
     for key in ("g_scalar", "g_row", "g_col"):
         if key in gd:
