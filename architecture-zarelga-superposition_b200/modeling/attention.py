@@ -1,0 +1,114 @@
+"""GatedAttention (https://arxiv.org/abs/2505.06708) with the reference's
+interface (modeling/attention.py:14-226): q/k/v/o and head-gate projections,
+per-head QK zero-centred RMSNorm, partial position-RoPE on the first
+pos_rope_dims of each head, causal GQA attention with an optional sliding
+window, and a per-head sigmoid output gate.  An optional learned sink logit
+per head (the key-sink of modeling/hca.py:138-144, value 0) is off by default
+so the state dict matches the reference's.
+
+QK-norm and RoPE run in libzs.so; the projections are cuBLAS linears.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from zs_b200.attn import attention as attention_core
+
+from .liger_rope import LigerRopeFunction
+from .zRMSNorm import ZeroCenteredRMSNorm
+
+
+def _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len):
+    """Sequence id per (batch, position) for a packed batch; -1 on padding."""
+    total = int(cu_seqlens[-1])
+    ids = torch.repeat_interleave(torch.arange(cu_seqlens.numel() - 1, device=cu_seqlens.device),
+                                  cu_seqlens[1:] - cu_seqlens[:-1], output_size=total)
+    full = torch.full((bsz * seq_len,), -1, dtype=torch.long, device=cu_seqlens.device)
+    full[unpad_indices] = ids
+    return full.view(bsz, seq_len)
+
+
+class GatedAttention(nn.Module):
+    def __init__(self, config, window_size: Optional[int] = None, use_sink: bool = False):
+        super().__init__()
+        self.hidden_size = config.hidden_size
+        self.num_heads = config.n_attention_heads
+        self.num_key_value_heads = config.n_key_value_heads
+        self.num_key_value_groups = self.num_heads // self.num_key_value_heads
+        self.head_dim = config.hidden_size // config.n_attention_heads
+        self.max_position_embeddings = config.max_position_embeddings
+        self.rope_theta = config.rope_theta
+        self.do_rope = config.do_rope
+        self.initializer_range = config.initializer_range
+        self.window_size = window_size
+        self.window = (window_size - 1, 0) if window_size is not None else (-1, -1)
+        if self.head_dim * self.num_heads != self.hidden_size:
+            raise ValueError("hidden_size must be divisible by num_attention_heads")
+        self.q_proj = nn.Linear(self.hidden_size, self.num_heads * self.head_dim, bias=False)
+        self.k_proj = nn.Linear(self.hidden_size, self.num_key_value_heads * self.head_dim, bias=False)
+        self.v_proj = nn.Linear(self.hidden_size, self.num_key_value_heads * self.head_dim, bias=False)
+        self.o_proj = nn.Linear(self.num_heads * self.head_dim, self.hidden_size, bias=False)
+        self.head_gate_proj = nn.Linear(self.hidden_size, self.num_heads, bias=False)
+        self.use_qk_norm = config.use_qk_norm
+        if self.use_qk_norm:
+            self.q_norm = ZeroCenteredRMSNorm(self.head_dim, eps=config.rms_norm_eps)
+            self.k_norm = ZeroCenteredRMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        else:
+            self.q_norm = nn.Identity()
+            self.k_norm = nn.Identity()
+        self.k_sink = nn.Parameter(torch.empty(self.num_heads, self.head_dim)) if use_sink else None
+        self.reset_parameters()
+        self.pos_rope_dims = config.pos_rope_dims
+        self.pos_rope_pairs = config.pos_rope_dims // 2
+        if self.do_rope:
+            pos_cos, pos_sin = self._build_pos_rope_tables(self.max_position_embeddings, self.head_dim,
+                                                           self.rope_theta, dtype=torch.float32,
+                                                           device=self.q_proj.weight.device)
+        else:
+            pos_cos = pos_sin = None
+        self.register_buffer("pos_cos_cache", pos_cos, persistent=False)
+        self.register_buffer("pos_sin_cache", pos_sin, persistent=False)
+
+    def reset_parameters(self):
+        for lin in (self.q_proj, self.k_proj, self.v_proj, self.o_proj, self.head_gate_proj):
+            nn.init.normal_(lin.weight, mean=0.0, std=self.initializer_range)
+        if self.k_sink is not None:
+            nn.init.normal_(self.k_sink, mean=0.0, std=self.initializer_range)
+
+    def _build_pos_rope_tables(self, max_position_embeddings, head_dim, base, dtype, device):
+        """cos/sin [max_pos, head_dim/2]: rotation on the first pos_rope_dims/2 pairs, identity after."""
+        half = head_dim // 2
+        cos_table = torch.ones(max_position_embeddings, half, dtype=dtype, device=device)
+        sin_table = torch.zeros(max_position_embeddings, half, dtype=dtype, device=device)
+        if self.pos_rope_pairs == 0:
+            return cos_table, sin_table
+        inv_freq = 1.0 / (base ** (torch.arange(0, self.pos_rope_dims, 2, device=device, dtype=torch.float32)
+                                   / self.pos_rope_dims))
+        freqs = torch.outer(torch.arange(max_position_embeddings, device=device, dtype=torch.float32), inv_freq)
+        cos_table[:, : self.pos_rope_pairs] = freqs.cos().to(dtype)
+        sin_table[:, : self.pos_rope_pairs] = freqs.sin().to(dtype)
+        return cos_table, sin_table
+
+    def forward(self, hidden_states, position_ids=None, cu_seqlens=None, max_seqlen=None, unpad_indices=None):
+        bsz, seq_len, _ = hidden_states.shape
+        if self.do_rope and position_ids is None:
+            position_ids = torch.arange(seq_len, device=hidden_states.device).expand(bsz, seq_len)
+        q = self.q_proj(hidden_states).view(bsz, seq_len, self.num_heads, self.head_dim)
+        k = self.k_proj(hidden_states).view(bsz, seq_len, self.num_key_value_heads, self.head_dim)
+        v = self.v_proj(hidden_states).view(bsz, seq_len, self.num_key_value_heads, self.head_dim)
+        q = self.q_norm(q)
+        k = self.k_norm(k)
+        if self.do_rope:
+            cos = self.pos_cos_cache[position_ids]
+            sin = self.pos_sin_cache[position_ids]
+            q, k = LigerRopeFunction.apply(q, k, cos, sin, cos, sin)
+        seq_ids = None
+        if cu_seqlens is not None:
+            seq_ids = _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len)
+        attn = attention_core(q, k, v, window=self.window_size, seq_ids=seq_ids, k_sink=self.k_sink)
+        gate = torch.sigmoid(self.head_gate_proj(hidden_states))
+        attn = attn * gate.unsqueeze(-1)
+        return self.o_proj(attn.reshape(bsz, seq_len, self.num_heads * self.head_dim))

@@ -1,0 +1,26 @@
+"""ExpertMLP (the shared expert): down(silu(gate(x)) * up(x)) with bias-free
+linears named gate_proj / up_proj / down_proj (modeling/expert_layer.py:6-24)."""
+from __future__ import annotations
+
+import torch.nn as nn
+
+
+class ExpertMLP(nn.Module):
+    def __init__(self, config, intermediate_size=None):
+        super().__init__()
+        self.config = config
+        self.hidden_size = config.hidden_size
+        self.intermediate_size = intermediate_size or config.intermediate_size
+        self.initializer_range = config.initializer_range
+        self.gate_proj = nn.Linear(self.hidden_size, self.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(self.hidden_size, self.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(self.intermediate_size, self.hidden_size, bias=False)
+        self.act_fn = nn.SiLU()
+        self.reset_parameters()
+
+    def reset_parameters(self):
+        for lin in (self.gate_proj, self.up_proj, self.down_proj):
+            nn.init.normal_(lin.weight, mean=0.0, std=self.initializer_range)
+
+    def forward(self, x):
+        return self.down_proj(self.act_fn(self.gate_proj(x)) * self.up_proj(x))

@@ -1,0 +1,48 @@
+"""MoELayer: router + shared expert + routed GLU experts (modeling/moe_layer.py:11-58).
+Parameter names match the reference (gate, shared_experts, routed_experts)."""
+from __future__ import annotations
+
+import torch.nn as nn
+
+from scattermoe.mlp import GLUMLP
+
+from .expert_layer import ExpertMLP
+from .moe_gate import MoEGate
+
+
+class MoELayer(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.config = config
+        self.n_experts_per_token = config.n_experts_per_token
+        self.gate = MoEGate(config)
+        self.shared_experts = ExpertMLP(config, intermediate_size=config.intermediate_size * config.n_shared_experts)
+        self.routed_experts = GLUMLP(input_size=config.hidden_size, hidden_size=config.intermediate_size,
+                                     num_experts=config.n_routed_experts, top_k=config.n_experts_per_token,
+                                     activation=nn.SiLU())
+        self.reset_routed_expert_parameters()
+
+    def reset_routed_expert_parameters(self):
+        std = self.config.initializer_range
+        nn.init.normal_(self.routed_experts.experts.weight, mean=0.0, std=std)
+        nn.init.normal_(self.routed_experts.output_experts.weight, mean=0.0, std=std)
+
+    def forward(self, hidden_states, unpad_indices=None):
+        if unpad_indices is not None:
+            bsz, seq_len, d = hidden_states.shape
+            x = hidden_states.reshape(bsz * seq_len, d).index_select(0, unpad_indices).unsqueeze(0)
+        else:
+            x = hidden_states
+        topk_idx, topk_weight = self.gate(x)
+        shared = self.shared_experts(x)
+        k = self.n_experts_per_token
+        routed = self.routed_experts(x, topk_weight.reshape(-1, k), topk_idx.reshape(-1, k))
+        out = shared + routed
+        if unpad_indices is not None:
+            full = out.new_zeros(bsz * seq_len, out.size(-1))
+            full.index_copy_(0, unpad_indices, out.squeeze(0))
+            out = full.view(bsz, seq_len, -1)
+            idx_full = topk_idx.new_zeros(bsz * seq_len, k)
+            idx_full.index_copy_(0, unpad_indices, topk_idx.reshape(-1, k))
+            topk_idx = idx_full.view(bsz, seq_len, k)
+        return out, topk_idx

@@ -446,6 +446,126 @@ def run_config3(args):
     print(json.dumps(line), flush=True)
 
 
+def config4_model_config(layers=16):
+    from modeling.model_config import ModelConfig
+
+    return ModelConfig(vocab_size=65536, embed_size=1536, hidden_size=1536, transformer_depth=layers,
+                       intermediate_size=768, n_experts=65, n_shared_experts=1, n_experts_per_token=6,
+                       n_attention_heads=12, n_key_value_heads=4, attention_window_pattern=(None,) * layers,
+                       max_position_embeddings=4096, sequence_length=4096)
+
+
+def model_flops_per_token(cfg, seq_len):
+    """6 * active matmul parameters (incl. the LM head) + 6 * L * H * hd * S
+    (causal attention), the MFU numerator the metric is defined on."""
+    d, hd = cfg.hidden_size, cfg.hidden_size // cfg.n_attention_heads
+    kv = cfg.n_key_value_heads * hd
+    attn = 2 * d * d + 2 * d * kv + d * cfg.n_attention_heads
+    router = cfg.n_routed_experts * d
+    shared = 3 * d * cfg.intermediate_size * cfg.n_shared_experts
+    routed = cfg.n_experts_per_token * 3 * d * cfg.intermediate_size
+    active = cfg.transformer_depth * (attn + router + shared + routed) + cfg.vocab_size * d
+    return 6 * active + 6 * cfg.transformer_depth * cfg.n_attention_heads * hd * seq_len
+
+
+def run_config4(args):
+    """the full MoE LM training step (forward, CCE loss,
+    backward, MuonMD + AdamW + sparse embedding optimizer step, aux-loss-free
+    bias update), micro-batch 8 x 4096 tokens per GPU, data parallel."""
+    import torch
+    import torch.distributed as dist
+
+    from cut_cross_entropy import linear_cross_entropy
+    from modeling.model import MoEModel
+    from zs_b200 import _lib as Z
+    from zs_b200.train import auxillary_loss_free_update, build_muonmd_optimizer, build_next_token_loss_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = config4_model_config(args.layers)
+    torch.manual_seed(1234)
+    model = MoEModel(cfg).to(dev)
+    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3)
+    B, S = args.micro_batch, 4096
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), device=dev, generator=g)
+    mask = torch.ones(B, S, dtype=torch.long, device=dev)
+
+    def step():
+        opt.zero_grad(set_to_none=False)
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            emb, all_topk = model.headless_forward(ids)
+            le, labels = build_next_token_loss_inputs(emb, ids, mask)
+            loss = linear_cross_entropy(le, model.get_classifier_weights(), labels, ignore_index=-100)
+        loss.backward()
+        if world > 1:
+            for p_ in model.parameters():
+                if p_.grad is not None and not p_.grad.is_sparse:
+                    dist.all_reduce(p_.grad)
+        opt.step()
+        auxillary_loss_free_update(model, all_topk, 1e-3, mask, process_group=dist.group.WORLD if world > 1 else None)
+        return loss
+
+    for _ in range(max(args.warmup, 5)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.5)
+    Z.INSTR.events = {}
+    Z.INSTR.timing = True
+    l0 = Z.INSTR.launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ht0 = time.time()
+    t0.record()
+    for _ in range(args.steps):
+        loss = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ht1 = time.time()
+    Z.INSTR.timing = False
+    clocks = sampler.stop(ht0, ht1)
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    kern = {}
+    for name, evs in Z.INSTR.events.items():
+        durs = [a.elapsed_time(b) for a, b in evs]
+        kern[name] = {"launches_per_step": len(durs) / args.steps, "ms_per_step": sum(durs) / args.steps}
+    if rank == 0:
+        _, sustained, _, src = measured_peaks()
+        fpt = model_flops_per_token(cfg, S)
+        value = world * B * S * args.steps / (ms * 1e-3)
+        mfu = value * fpt / (world * sustained * 1e12)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 5), "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"config4: MoE LM L={cfg.transformer_depth} d=1536 H=12/4 hd=128 E=64+1 "
+                                       f"ffn=768 top-6 V=65536, seq 4096 x micro-batch {B}, full step incl. "
+                                       "MuonMD/AdamW/sparse-embedding optimizer",
+                           "parallelism": f"dp{world}", "model_gflop_per_token": fpt / 1e9, "mfu": mfu,
+                           "loss": float(loss.item())},
+                "roofline": {"bound": "tensor", "achieved": value * fpt / world / 1e12, "peak": sustained,
+                             "unit": "TFLOP/s", "frac": mfu, "traffic": None,
+                             "peak_source": f"{src} bf16_tflops_sustained; achieved = model FLOPs only",
+                             "kernels": kern},
+                "gpu_launches": Z.INSTR.launches - l0, "clocks": clocks, "device_error": Z.device_error()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -455,13 +575,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: config 2's 16384)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3], help="BASELINE config (default 2)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4], help="BASELINE config (default 2)")
+    ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
+    ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.config == 3:
         run_config3(args)
+    elif args.config == 4:
+        run_config4(args)
     else:
         run_gpu(args)
 
