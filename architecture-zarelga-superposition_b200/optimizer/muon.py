@@ -32,18 +32,27 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int) -> torch.Tensor:
         X = X.mT
     shape = X.shape
     m, n = shape[-2], shape[-1]
-    Xc = X.reshape(-1, m, n).contiguous()
+    Xc = X.reshape(-1, m, n)
+    # Zero rows and columns stay zero through the iteration and change neither
+    # X X^T's live block nor the Frobenius norm, so padding to the kernels'
+    # 8-element granularity is exact.
+    mp, np_ = -(-m // 8) * 8, -(-n // 8) * 8
+    if (mp, np_) != (m, n):
+        Xc = torch.nn.functional.pad(Xc, (0, np_ - n, 0, mp - m))
+    Xc = Xc.contiguous()
     batch = Xc.size(0)
     out = torch.empty_like(Xc)
-    ws = torch.empty(int(Z.lib().zs_newton_schulz5_workspace(batch, m, n, Z.ZS_BF16)), dtype=torch.uint8,
+    ws = torch.empty(int(Z.lib().zs_newton_schulz5_workspace(batch, mp, np_, Z.ZS_BF16)), dtype=torch.uint8,
                      device=G.device)
     a, b, c = NS_COEFFS
     Z.count(1 + 3 * int(steps))
     with Z.timed("newton_schulz5"):
-        Z.check(Z.lib().zs_newton_schulz5(Xc.data_ptr(), out.data_ptr(), batch, m, n, int(steps), a, b, c,
+        Z.check(Z.lib().zs_newton_schulz5(Xc.data_ptr(), out.data_ptr(), batch, mp, np_, int(steps), a, b, c,
                                           ws.data_ptr(), ws.numel(), Z.ZS_BF16, Z.stream_of(Xc)),
                 "zs_newton_schulz5")
-    out = out.view(shape)
+    if (mp, np_) != (m, n):
+        out = out[:, :m, :n]
+    out = out.reshape(shape)
     return out.mT if tall else out
 
 

@@ -38,7 +38,7 @@ def test_ns5_reference_fixture(golden):
 
 
 @pytest.mark.parametrize("shape", [(64, 1536, 1536), (64, 1536, 768), (1536, 1536), (64, 1536), (12, 256, 512),
-                                   (3, 8, 16)])
+                                   (3, 8, 16), (12, 1536), (5, 37, 20), (1, 1, 9)])
 def test_ns5_matches_torch_formula(shape):
     from optimizer.muon import zeropower_via_newtonschulz5
 
