@@ -34,6 +34,13 @@ def _mask(S, device, window, seq_ids=None, sink=False):
 
 
 def attention(q, k, v, *, window=None, seq_ids=None, k_sink=None, scale=None):
+    from . import _lib as Z
+
+    with Z.timed("attention_fwd"):
+        return _attention(q, k, v, window=window, seq_ids=seq_ids, k_sink=k_sink, scale=scale)
+
+
+def _attention(q, k, v, *, window=None, seq_ids=None, k_sink=None, scale=None):
     B, S, H, hd = q.shape
     Hkv = k.shape[2]
     scale = 1.0 / math.sqrt(hd) if scale is None else scale

@@ -493,21 +493,29 @@ def run_config4(args):
     opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3)
     B, S = args.micro_batch, 4096
     g = torch.Generator(device=dev).manual_seed(77 + rank)
-    ids = torch.randint(0, cfg.vocab_size, (B, S), device=dev, generator=g)
+    nb = max(args.warmup, 5) + args.steps
+    # a fresh batch of uniform token ids for every step (a fixed batch is
+    # memorised within a few steps by a model this size)
+    batches = torch.randint(0, cfg.vocab_size, (nb, B, S), device=dev, generator=g)
     mask = torch.ones(B, S, dtype=torch.long, device=dev)
+    it = [0]
 
     def step():
+        ids = batches[it[0] % nb]
+        it[0] += 1
         opt.zero_grad(set_to_none=False)
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             emb, all_topk = model.headless_forward(ids)
             le, labels = build_next_token_loss_inputs(emb, ids, mask)
             loss = linear_cross_entropy(le, model.get_classifier_weights(), labels, ignore_index=-100)
-        loss.backward()
+        with Z.timed("backward"):
+            loss.backward()
         if world > 1:
             for p_ in model.parameters():
                 if p_.grad is not None and not p_.grad.is_sparse:
                     dist.all_reduce(p_.grad)
-        opt.step()
+        with Z.timed("optimizer_step"):
+            opt.step()
         auxillary_loss_free_update(model, all_topk, 1e-3, mask, process_group=dist.group.WORLD if world > 1 else None)
         return loss
 

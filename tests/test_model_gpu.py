@@ -1,0 +1,51 @@
+"""Whole-model checks on the GPU: causality (no position sees later tokens),
+the loss of an untrained model on uniform tokens (~ log V), and agreement of
+the fused CCE with a materialised cross entropy on the model's hidden state."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny(layers=2, window=None):
+    from modeling.model_config import ModelConfig
+    from modeling.model import MoEModel
+
+    cfg = ModelConfig(vocab_size=8192, embed_size=256, hidden_size=256, transformer_depth=layers,
+                      intermediate_size=512, n_experts=9, n_shared_experts=1, n_experts_per_token=2,
+                      n_attention_heads=4, n_key_value_heads=4, attention_window_pattern=(window,) * layers,
+                      max_position_embeddings=256, sequence_length=256, pos_rope_dims=32)
+    torch.manual_seed(0)
+    return cfg, MoEModel(cfg).cuda()
+
+
+@pytest.mark.parametrize("window", [None, 16])
+def test_model_is_causal(window):
+    cfg, m = _tiny(window=window)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), device="cuda")
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        h1, _ = m.headless_forward(ids)
+        ids2 = ids.clone()
+        ids2[:, 100:] = torch.randint(0, cfg.vocab_size, (2, 156), device="cuda")
+        h2, _ = m.headless_forward(ids2)
+    # positions before 100 must not change when later tokens do
+    assert torch.equal(h1[:, :100], h2[:, :100])
+    assert not torch.equal(h1[:, 100:], h2[:, 100:])
+
+
+def test_untrained_loss_is_near_log_vocab_and_matches_materialised_ce():
+    from cut_cross_entropy import linear_cross_entropy
+
+    cfg, m = _tiny()
+    ids = torch.randint(0, cfg.vocab_size, (4, 256), device="cuda")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        h, _ = m.headless_forward(ids)
+        e = h[:, :-1].contiguous()
+        t = ids[:, 1:].contiguous()
+        loss = linear_cross_entropy(e, m.get_classifier_weights(), t)
+    ref = torch.nn.functional.cross_entropy((e.float() @ m.get_classifier_weights().float().T).view(-1, cfg.vocab_size),
+                                            t.view(-1))
+    assert abs(loss.item() - ref.item()) / ref.item() < 2e-2
+    assert abs(loss.item() - math.log(cfg.vocab_size)) < 2.0
