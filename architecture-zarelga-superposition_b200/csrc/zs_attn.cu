@@ -1,0 +1,1092 @@
+// Causal GQA flash attention forward on the 5th-generation tensor cores.
+//
+// Replaces flash_attn_varlen_func as GatedAttention uses it
+// (modeling/attention.py:131-169): causal, optional causal sliding window
+// (window W = current token + W-1 previous), optional packed sequences, and
+// the learned per-head key sink of modeling/hca.py:138-144,264-298 (one extra
+// always-visible key whose value is zero).  Scale 1/sqrt(head_dim).
+//
+// One CTA per (query tile of 128 rows, head, batch row), 192 threads:
+//   warp 0      TMA: the Q tile once, then K/V tiles into a 2-stage ring
+//   warp 1      MMA: S_j = Q K_j^T into one of two TMEM buffers, then
+//               O += P_{j-1} V_{j-1} with P from shared memory
+//   warps 2..5  softmax: one query row per thread; read S_j from TMEM, keep
+//               the running max (log2 domain) and sum, write P_j (bf16) to
+//               shared memory in the MMA's 128-byte swizzled layout, rescale
+//               the O accumulator in TMEM only when the max grows by > 8
+//               (2^8 headroom keeps P and the sums finite); finally O / sum
+//               and the log-sum-exp.
+// TMEM columns: S buffers [0,128) and [128,256), O [256, 256+hd).
+#include "zs_common.cuh"
+
+namespace zs {
+namespace attn {
+
+constexpr int BQ = 128;      // query rows per CTA
+constexpr int BKV = 128;     // keys per tile
+constexpr int NST = 2;       // K/V ring stages
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct FwdArgs {
+  int B, S, H, Hkv, hd;
+  int window;                 // <= 0: none
+  float scale_log2;           // softmax scale * log2(e)
+  const int* seg_start;       // nullable [B*S]: first position of the token's packed sequence (-1: padding)
+  const void* k_sink;         // nullable [H, hd] (dtype of sink_dtype)
+  int sink_dtype;
+  const __nv_bfloat16* q;     // [B*S, H*hd]
+  __nv_bfloat16* o;           // [B*S, H*hd]
+  float* lse;                 // [B, H, S] natural-log log-sum-exp
+};
+
+template <int HD>
+struct FwdSmem {
+  static constexpr int TILE = 128 * HD * 2;          // one 128-row tile (Q, K or V)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = TILE;                // NST x (K, V)
+  static constexpr int OFF_P = OFF_KV + NST * 2 * TILE;
+  static constexpr int P_BYTES = 128 * 128 * 2;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int NBAR = 1 + 2 * NST + 2 + 2 + 1 + 1 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int TOTAL = OFF_MISC + 16;
+  static constexpr int ALLOC = TOTAL + 1024;
+};
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using L = FwdSmem<HD>;
+  constexpr int ATOMS = HD / 64;           // 128-byte swizzle atoms across head_dim
+  constexpr int ATOM_BYTES = 128 * 128;    // 128 rows x 128 bytes
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 1 + NST;
+  uint64_t* s_full = bars + 1 + 2 * NST;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* done = pv_done + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (a.S + BQ - 1) / BQ;
+  const int qt = n_qt - 1 - (int)blockIdx.x;   // heaviest (latest) query tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.H / a.Hkv);
+  const int q0 = qt * BQ;
+  const int64_t row0 = (int64_t)b * a.S;
+
+  // key tile range [kt_lo, kt_hi] for this query tile
+  int k_first = 0;
+  if (a.window > 0) k_first = max(0, q0 - (a.window - 1));
+  if (a.seg_start != nullptr) {
+    int lo = 0x7fffffff;
+    for (int r = threadIdx.x; r < BQ; r += blockDim.x) {
+      const int q = q0 + r;
+      if (q < a.S) {
+        const int st = __ldg(a.seg_start + row0 + q);
+        if (st >= 0) lo = min(lo, st);
+      }
+    }
+    __shared__ int s_lo;
+    if (threadIdx.x == 0) s_lo = 0x7fffffff;
+    __syncthreads();
+    atomicMin(&s_lo, lo);
+    __syncthreads();
+    if (s_lo != 0x7fffffff) k_first = max(k_first, s_lo);
+  }
+  const int kt_lo = k_first / BKV;
+  const int kt_hi = min(q0 + BQ - 1, a.S - 1) / BKV;
+  const int n_kv = kt_hi - kt_lo + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  constexpr uint32_t IDESC_S = idesc_f16(128, 128, 1, 0, 0);
+  constexpr uint32_t IDESC_PV = idesc_f16(128, HD, 1, 0, 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t issued = 0, par = 0;
+      mbar_arrive_expect_tx(q_full, L::TILE);
+#pragma unroll
+      for (int at = 0; at < ATOMS; ++at)
+        tma_load_2d(smem + L::OFF_Q + at * ATOM_BYTES, &tmQ, q_full, h * HD + at * 64, (int)(row0 + q0));
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % NST;
+        if (!mbar_wait(&kv_empty[st], ((j / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        uint8_t* kb = smem + L::OFF_KV + st * 2 * L::TILE;
+        uint8_t* vb = kb + L::TILE;
+        const int krow = (int)(row0 + (kt_lo + j) * BKV);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::TILE);
+#pragma unroll
+        for (int at = 0; at < ATOMS; ++at) {
+          tma_load_2d(kb + at * ATOM_BYTES, &tmK, &kv_full[st], hk * HD + at * 64, krow);
+          tma_load_2d(vb + at * ATOM_BYTES, &tmV, &kv_full[st], hk * HD + at * 64, krow);
+        }
+        issued |= 1u << st;
+        par = (par & ~(1u << st)) | ((uint32_t)((j / NST) & 1) << st);
+      }
+      mbar_wait(q_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+      for (int s = 0; s < NST; ++s)
+        if (issued & (1u << s)) mbar_wait(&kv_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    bool ok = warp_wait(q_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
+    bool issued_any = false;
+    for (int j = 0; ok && j <= n_kv; ++j) {
+      if (j < n_kv) {
+        const int st = j % NST, sb = j & 1;
+        if (!warp_wait(&kv_full[st], (j / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        if (!warp_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + L::OFF_Q);
+          const uint32_t ka = smem_u32(smem + L::OFF_KV + st * 2 * L::TILE);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk / 4) * ATOM_BYTES + (kk % 4) * 32;
+            tc_mma_f16(tmem + sb * 128, smem_desc(qa + off, 16, 1024, 2), smem_desc(ka + off, 16, 1024, 2),
+                       IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[sb]);
+          issued_any = true;
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int jj = j - 1, st = jj % NST;
+        if (!warp_wait(p_full, jj & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t pa = smem_u32(smem + L::OFF_P);
+          const uint32_t va = smem_u32(smem + L::OFF_KV + st * 2 * L::TILE + L::TILE);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint64_t ad = smem_desc(pa + (kk / 4) * ATOM_BYTES + (kk % 4) * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(va + kk * 2048, ATOM_BYTES, 1024, 2);
+            tc_mma_f16(tmem + 256, ad, bd, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(pv_done);
+          tc_commit(&kv_empty[st]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0 && issued_any) {
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int q = q0 + r;
+    const bool qvalid = q < a.S;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    int qseg = 0;
+    if (a.seg_start != nullptr && qvalid) qseg = __ldg(a.seg_start + row0 + q);
+    // running max (log2 domain, relative to which P is formed) and sum
+    float m_used = -INFINITY, l = 0.f;
+    if (a.k_sink != nullptr && qvalid) {
+      const __nv_bfloat16* qr = a.q + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+      float dot = 0.f;
+      for (int c = 0; c < HD; ++c) {
+        const float ks = a.sink_dtype == ZS_F32 ? reinterpret_cast<const float*>(a.k_sink)[h * HD + c]
+                                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[h * HD + c]);
+        dot = fmaf(__bfloat162float(qr[c]), ks, dot);
+      }
+      m_used = dot * a.scale_log2;
+      l = 1.f;
+    }
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int sb = j & 1;
+      if (!warp_wait(&s_full[sb], (j >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld_32x32b_x32(tmem + lane_base + sb * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      const int k0 = (kt_lo + j) * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const int k = k0 + c;
+        bool vis = qvalid && k <= q;
+        if (a.window > 0) vis = vis && (q - k < a.window);
+        if (a.seg_start != nullptr) vis = vis && (k >= qseg) && qseg >= 0;
+        const float t = vis ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
+        sr[c] = __float_as_uint(t);
+        mx = fmaxf(mx, t);
+      }
+      const float m_new = fmaxf(m_used, mx);
+      const bool need = m_new > m_used + 8.0f;
+      // P_{j-1} has been consumed and O holds every earlier product once PV_{j-1} completes
+      if (j >= 1 && !warp_wait(pv_done, (j - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      float f = 1.0f;
+      if (need) {
+        f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
+        l *= f;
+        m_used = m_new;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, need)) {
+        // rescale O rows in TMEM; the access is warp-wide, lanes that keep
+        // their max scale by exactly 1
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t orow[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+          tc_wait_ld();
+#pragma unroll
+          for (int x = 0; x < 32; ++x) orow[x] = __float_as_uint(__uint_as_float(orow[x]) * f);
+          tmem_st_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+        }
+        tc_wait_st();
+      }
+      // P = exp2(t - m_used) -> bf16, swizzled rows of 128 bytes per 64 keys
+      uint8_t* prow = smem + L::OFF_P + r * 128;
+      // a row with every key so far masked keeps m_used = -inf and all t = -inf: P = 0
+      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float p0 = fast_exp2(__uint_as_float(sr[ch * 8 + 2 * x]) - mu);
+          const float p1 = fast_exp2(__uint_as_float(sr[ch * 8 + 2 * x + 1]) - mu);
+          __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+          const float2 back = __bfloat1622float2(pp);
+          rs += back.x + back.y;
+          w[x] = *reinterpret_cast<uint32_t*>(&pp);
+        }
+        const int atom = ch >> 3, c16 = ch & 7;
+        *reinterpret_cast<uint4*>(prow + atom * ATOM_BYTES + ((c16 ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_kv > 0 && warp_wait(pv_done, (n_kv - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      __nv_bfloat16* orow_g = a.o + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t orow[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+        tc_wait_ld();
+        if (qvalid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow_g + c * 32);
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            uint32_t w[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(orow[x * 8 + 2 * y]) * inv,
+                                                        __uint_as_float(orow[x * 8 + 2 * y + 1]) * inv);
+              w[y] = *reinterpret_cast<uint32_t*>(&pp);
+            }
+            dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      if (qvalid) a.lse[((int64_t)b * a.H + h) * a.S + q] = l > 0.f ? (m_used + log2f(l)) * LN2 : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace zs
+
+using namespace zs;
+
+extern "C" int zs_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int S,
+                                    int H, int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
+                                    int sink_dtype, float softmax_scale, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(q && k && v && o && lse, ZS_ERR_ARG);
+  ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(hd == 64 || hd == 128, ZS_ERR_SHAPE);
+  ZS_REQUIRE((int64_t)B * S < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_REQUIRE(k_sink == nullptr || sink_dtype == ZS_F32 || sink_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_BIND(q);
+  CUtensorMap tq, tk, tv;
+  int rc;
+  const uint64_t rows = (uint64_t)B * S;
+  if ((rc = make_tmap(&tq, q, ZS_BF16, (uint64_t)H * hd, rows, (uint64_t)H * hd * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk, k, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)Hkv * hd * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv, v, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)Hkv * hd * 2, 64, 128)) != ZS_OK) return rc;
+  attn::FwdArgs a{};
+  a.B = B;
+  a.S = S;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.hd = hd;
+  a.window = window;
+  a.scale_log2 = softmax_scale * attn::LOG2E;
+  a.seg_start = seg_start;
+  a.k_sink = k_sink;
+  a.sink_dtype = sink_dtype;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.o = reinterpret_cast<__nv_bfloat16*>(o);
+  a.lse = lse;
+  dim3 grid((S + attn::BQ - 1) / attn::BQ, H, B);
+  if (hd == 128) {
+    using L = attn::FwdSmem<128>;
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+    attn::attn_fwd_kernel<128><<<grid, 192, L::ALLOC, stream>>>(tq, tk, tv, a);
+  } else {
+    using L = attn::FwdSmem<64>;
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+    attn::attn_fwd_kernel<64><<<grid, 192, L::ALLOC, stream>>>(tq, tk, tv, a);
+  }
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+// ------------------------------------------------------------------ backward
+//
+// Two kernels, no atomics, both on tcgen05 with TMEM accumulators:
+//   dq kernel   one CTA per (128-row query tile, head, batch row); loops over
+//               64-key tiles: S = Q K^T, dP = dO V^T (double-buffered TMEM),
+//               dS = P (dP - D) * (bf16, shared memory), dQ += dS K.
+//   dkv kernel  one CTA per (128-key tile, kv head, batch row); loops over the
+//               GQA group's query heads and 64-row query tiles:
+//               S^T = K Q^T, dP^T = V dO^T, P^T and dS^T to shared memory,
+//               dV += P^T dO, dK += dS^T Q; the group's heads accumulate in TMEM.
+// P = exp(S * scale - lse) uses the forward's log-sum-exp; D = rowsum(dO * O)
+// comes from attn_bwd_prep_kernel.  The sink key (value 0) contributes
+// dS_sink = -P_sink * D per query row, returned for the caller to fold into
+// dQ and the sink parameter.
+
+namespace zs {
+namespace attn {
+
+struct BwdArgs {
+  int B, S, H, Hkv, hd;
+  int window;
+  float scale, scale_log2;
+  const int* seg_start;
+  const float* lse;     // [B, H, S]
+  const float* D;       // [B, H, S]
+  const void* k_sink;   // nullable [H, hd]
+  int sink_dtype;
+  const __nv_bfloat16* q;
+  __nv_bfloat16* dq;    // [B*S, H*hd]
+  __nv_bfloat16* dk;    // [B*S, Hkv*hd]
+  __nv_bfloat16* dv;
+};
+
+__device__ __forceinline__ float sink_at(const BwdArgs& a, int i) {
+  return a.sink_dtype == ZS_F32 ? __ldg(reinterpret_cast<const float*>(a.k_sink) + i)
+                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[i]);
+}
+
+// D[b, h, q] = sum_d dO * O over the head's row
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                     float* __restrict__ D, int B, int S, int H, int hd) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)B * S * H;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows; w += warps) {
+    const int64_t tok = w / H;
+    const int h = (int)(w - tok * H);
+    const __nv_bfloat16* po = o + tok * (int64_t)H * hd + (int64_t)h * hd;
+    const __nv_bfloat16* pd = dout + tok * (int64_t)H * hd + (int64_t)h * hd;
+    float acc = 0.f;
+    for (int c = lane * 2; c < hd; c += 64) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + c));
+      const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + c));
+      acc = fmaf(a.x, d.x, fmaf(a.y, d.y, acc));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    const int64_t b = tok / S, q = tok - b * S;
+    if (lane == 0) D[(b * H + h) * S + q] = acc;
+  }
+}
+
+template <int HD>
+struct DqSmem {
+  static constexpr int QT = 128 * HD * 2;       // Q and dO tiles
+  static constexpr int KT = 64 * HD * 2;        // K and V tiles of 64 keys
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = QT;
+  static constexpr int OFF_KV = 2 * QT;         // NST x (K, V)
+  static constexpr int OFF_DS = OFF_KV + NST * 2 * KT;
+  static constexpr int DS_BYTES = 128 * 64 * 2;
+  static constexpr int OFF_BAR = OFF_DS + DS_BYTES;
+  static constexpr int NBAR = 1 + 2 * NST + 4 + 2 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
+};
+
+// a 128-row tile occupies HD/64 atoms of 128 rows x 128 B; a 64-row tile
+// HD/64 atoms of 64 rows x 128 B
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                       const __grid_constant__ CUtensorMap tmK64, const __grid_constant__ CUtensorMap tmV64,
+                       const BwdArgs a, float* __restrict__ ds_sink) {
+  using L = DqSmem<HD>;
+  constexpr int ATOMS = HD / 64;
+  constexpr int A128 = 128 * 128, A64 = 64 * 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + NST;
+  uint64_t* sp_full = kv_empty + NST;   // [2]
+  uint64_t* sp_empty = sp_full + 2;     // [2]
+  uint64_t* ds_full = sp_empty + 2;
+  uint64_t* ds_free = ds_full + 1;
+  uint64_t* done = ds_free + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (a.S + 127) / 128;
+  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.H / a.Hkv);
+  const int q0 = qt * 128;
+  const int64_t row0 = (int64_t)b * a.S;
+  int k_first = a.window > 0 ? max(0, q0 - (a.window - 1)) : 0;
+  if (a.seg_start != nullptr) {
+    __shared__ int s_lo;
+    if (threadIdx.x == 0) s_lo = 0x7fffffff;
+    __syncthreads();
+    if (threadIdx.x < 128 && q0 + (int)threadIdx.x < a.S) {
+      const int st = __ldg(a.seg_start + row0 + q0 + threadIdx.x);
+      if (st >= 0) atomicMin(&s_lo, st);
+    }
+    __syncthreads();
+    if (s_lo != 0x7fffffff) k_first = max(k_first, s_lo);
+  }
+  const int kt_lo = k_first / 64;
+  const int kt_hi = min(q0 + 127, a.S - 1) / 64;
+  const int n_kv = kt_hi - kt_lo + 1;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sp_full[s], 1);
+      mbar_init(&sp_empty[s], 128);
+    }
+    mbar_init(ds_full, 128);
+    mbar_init(ds_free, 1);
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  // TMEM: S[sb] at sb*128, dP[sb] at sb*128 + 64, dQ at 256
+  constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
+  constexpr uint32_t IDESC_DQ = idesc_f16(128, HD, 1, 0, 1);
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t issued = 0, par = 0;
+      mbar_arrive_expect_tx(q_full, 2 * L::QT);
+      for (int at = 0; at < ATOMS; ++at) {
+        tma_load_2d(smem + L::OFF_Q + at * A128, &tmQ, q_full, h * HD + at * 64, (int)(row0 + q0));
+        tma_load_2d(smem + L::OFF_DO + at * A128, &tmDO, q_full, h * HD + at * 64, (int)(row0 + q0));
+      }
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % NST;
+        if (!mbar_wait(&kv_empty[st], ((j / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        uint8_t* kb = smem + L::OFF_KV + st * 2 * L::KT;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::KT);
+        const int krow = (int)(row0 + (kt_lo + j) * 64);
+        for (int at = 0; at < ATOMS; ++at) {
+          tma_load_2d(kb + at * A64, &tmK64, &kv_full[st], hk * HD + at * 64, krow);
+          tma_load_2d(kb + L::KT + at * A64, &tmV64, &kv_full[st], hk * HD + at * 64, krow);
+        }
+        issued |= 1u << st;
+        par = (par & ~(1u << st)) | ((uint32_t)((j / NST) & 1) << st);
+      }
+      mbar_wait(q_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+      for (int s = 0; s < NST; ++s)
+        if (issued & (1u << s)) mbar_wait(&kv_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    bool ok = warp_wait(q_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
+    bool any = false;
+    for (int j = 0; ok && j <= n_kv; ++j) {
+      if (j < n_kv) {
+        const int st = j % NST, sb = j & 1;
+        if (!warp_wait(&kv_full[st], (j / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        if (!warp_wait(&sp_empty[sb], ((j >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + L::OFF_Q), da = smem_u32(smem + L::OFF_DO);
+          const uint32_t ka = smem_u32(smem + L::OFF_KV + st * 2 * L::KT), va = ka + L::KT;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t offa = (kk / 4) * A128 + (kk % 4) * 32, offb = (kk / 4) * A64 + (kk % 4) * 32;
+            tc_mma_f16(tmem + sb * 128, smem_desc(qa + offa, 16, 1024, 2), smem_desc(ka + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+            tc_mma_f16(tmem + sb * 128 + 64, smem_desc(da + offa, 16, 1024, 2), smem_desc(va + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+          }
+          tc_commit(&sp_full[sb]);
+          any = true;
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int jj = j - 1, st = jj % NST;
+        if (!warp_wait(ds_full, jj & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t dsa = smem_u32(smem + L::OFF_DS);
+          const uint32_t ka = smem_u32(smem + L::OFF_KV + st * 2 * L::KT);
+#pragma unroll
+          for (int kk = 0; kk < 64 / 16; ++kk)
+            tc_mma_f16(tmem + 256, smem_desc(dsa + kk * 32, 16, 1024, 2), smem_desc(ka + kk * 2048, A64, 1024, 2),
+                       IDESC_DQ, (jj > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(ds_free);
+          tc_commit(&kv_empty[st]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0 && any) {
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int q = q0 + r;
+    const bool qvalid = q < a.S;
+    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
+    const int64_t bh = (int64_t)b * a.H + h;
+    const float lse2 = qvalid ? __ldg(a.lse + bh * a.S + q) * LOG2E : 0.f;
+    const float Dq = qvalid ? __ldg(a.D + bh * a.S + q) : 0.f;
+    int qseg = 0;
+    if (a.seg_start != nullptr && qvalid) qseg = __ldg(a.seg_start + row0 + q);
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int sb = j & 1;
+      if (!warp_wait(&sp_full[sb], (j >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64], dr[64];
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sp_empty[sb]);
+      if (j >= 1 && !warp_wait(ds_free, (j - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      const int k0 = (kt_lo + j) * 64;
+      uint8_t* row = smem + L::OFF_DS + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          float v2[2];
+#pragma unroll
+          for (int y = 0; y < 2; ++y) {
+            const int c = ch * 8 + 2 * x + y;
+            const int k = k0 + c;
+            bool vis = qvalid && k <= q;
+            if (a.window > 0) vis = vis && (q - k < a.window);
+            if (a.seg_start != nullptr) vis = vis && k >= qseg && qseg >= 0;
+            const float p = vis ? fast_exp2(__uint_as_float(sr[c]) * a.scale_log2 - lse2) : 0.f;
+            v2[y] = p * (__uint_as_float(dr[c]) - Dq);
+          }
+          __nv_bfloat162 pp = __floats2bfloat162_rn(v2[0], v2[1]);
+          w[x] = *reinterpret_cast<uint32_t*>(&pp);
+        }
+        *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && warp_wait(ds_free, (n_kv - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      // sink key (value 0): dS_sink = -P_sink * D; dQ gains dS_sink * k_sink
+      float dss = 0.f;
+      if (a.k_sink != nullptr && qvalid) {
+        const __nv_bfloat16* qr = a.q + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+        float dot = 0.f;
+        for (int c = 0; c < HD; ++c) dot = fmaf(__bfloat162float(qr[c]), sink_at(a, h * HD + c), dot);
+        dss = -fast_exp2(dot * a.scale_log2 - lse2) * Dq;
+        ds_sink[bh * a.S + q] = dss;
+      }
+      __nv_bfloat16* out = a.dq + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lb + 256 + c * 32, v);
+        tc_wait_ld();
+        if (qvalid) {
+          uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            uint32_t w[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              const int cc = c * 32 + x * 8 + 2 * y;
+              float v0 = __uint_as_float(v[x * 8 + 2 * y]), v1 = __uint_as_float(v[x * 8 + 2 * y + 1]);
+              if (a.k_sink != nullptr) {
+                v0 = fmaf(dss, sink_at(a, h * HD + cc), v0);
+                v1 = fmaf(dss, sink_at(a, h * HD + cc + 1), v1);
+              }
+              __nv_bfloat162 pp = __floats2bfloat162_rn(v0 * a.scale, v1 * a.scale);
+              w[y] = *reinterpret_cast<uint32_t*>(&pp);
+            }
+            dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int HD>
+struct DkvSmem {
+  static constexpr int KT = 128 * HD * 2;       // K and V tiles of 128 keys
+  static constexpr int QT = 64 * HD * 2;        // Q and dO tiles of 64 rows
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = KT;
+  static constexpr int OFF_QD = 2 * KT;         // NST x (Q, dO)
+  static constexpr int OFF_P = OFF_QD + NST * 2 * QT;
+  static constexpr int PB = 128 * 64 * 2;
+  static constexpr int OFF_DS = OFF_P + PB;
+  static constexpr int OFF_LD = OFF_DS + PB;
+  static constexpr int OFF_BAR = OFF_LD + 2 * 3 * 64 * 4;   // 2 buffers of lse2[64], D[64], seg[64]
+  static constexpr int NBAR = 1 + 2 * NST + 4 + 2 + 1 + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmDO64,
+                        const BwdArgs a) {
+  using L = DkvSmem<HD>;
+  constexpr int ATOMS = HD / 64;
+  constexpr int A128 = 128 * 128, A64 = 64 * 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = qd_full + NST;
+  uint64_t* sp_full = qd_empty + NST;
+  uint64_t* sp_empty = sp_full + 2;
+  uint64_t* ds_full = sp_empty + 2;
+  uint64_t* ds_free = ds_full + 1;
+  uint64_t* done = ds_free + 1;
+  uint64_t* ld_full = done + 1;          // [2]: the query tile's lse / D / seg staged
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  float* s_ld = reinterpret_cast<float*>(smem + L::OFF_LD);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;                 // earliest key tiles (most queries) first
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int G = a.H / a.Hkv;
+  const int k0 = kt * 128;
+  const int64_t row0 = (int64_t)b * a.S;
+  const int qt_lo = k0 / 64;
+  int q_last = a.S - 1;
+  if (a.window > 0) q_last = min(q_last, k0 + 127 + a.window - 1);
+  const int qt_hi = q_last / 64;
+  const int n_q = qt_hi - qt_lo + 1;        // per query head
+  const int n_it = G * n_q;
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&qd_full[s], 1);
+      mbar_init(&qd_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sp_full[s], 1);
+      mbar_init(&sp_empty[s], 128);
+    }
+    mbar_init(ds_full, 128);
+    mbar_init(ds_free, 1);
+    mbar_init(done, 1);
+    mbar_init(&ld_full[0], 128);
+    mbar_init(&ld_full[1], 128);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  // TMEM: S^T[sb] at sb*128, dP^T[sb] at sb*128 + 64, dV at 256, dK at 256 + HD
+  constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
+  constexpr uint32_t IDESC_ACC = idesc_f16(128, HD, 1, 0, 1);
+  if (warp == 0) {
+    if (lane == 0 && k0 < a.S) {
+      uint32_t issued = 0, par = 0;
+      mbar_arrive_expect_tx(kv_full, 2 * L::KT);
+      for (int at = 0; at < ATOMS; ++at) {
+        tma_load_2d(smem + L::OFF_K + at * A128, &tmK, kv_full, hk * HD + at * 64, (int)(row0 + k0));
+        tma_load_2d(smem + L::OFF_V + at * A128, &tmV, kv_full, hk * HD + at * 64, (int)(row0 + k0));
+      }
+      for (int i = 0; i < n_it; ++i) {
+        const int st = i % NST;
+        const int g = i / n_q, qi = qt_lo + i % n_q;
+        const int h = hk * G + g;
+        if (!mbar_wait(&qd_empty[st], ((i / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        uint8_t* qb = smem + L::OFF_QD + st * 2 * L::QT;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * L::QT);
+        for (int at = 0; at < ATOMS; ++at) {
+          tma_load_2d(qb + at * A64, &tmQ64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
+          tma_load_2d(qb + L::QT + at * A64, &tmDO64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
+        }
+        issued |= 1u << st;
+        par = (par & ~(1u << st)) | ((uint32_t)((i / NST) & 1) << st);
+      }
+      mbar_wait(kv_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+      for (int s = 0; s < NST; ++s)
+        if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    bool ok = k0 < a.S && warp_wait(kv_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
+    bool any = false;
+    for (int i = 0; ok && i <= n_it; ++i) {
+      if (i < n_it) {
+        const int st = i % NST, sb = i & 1;
+        if (!warp_wait(&qd_full[st], (i / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        if (!warp_wait(&sp_empty[sb], ((i >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ka = smem_u32(smem + L::OFF_K), va = smem_u32(smem + L::OFF_V);
+          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t offa = (kk / 4) * A128 + (kk % 4) * 32, offb = (kk / 4) * A64 + (kk % 4) * 32;
+            tc_mma_f16(tmem + sb * 128, smem_desc(ka + offa, 16, 1024, 2), smem_desc(qa + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+            tc_mma_f16(tmem + sb * 128 + 64, smem_desc(va + offa, 16, 1024, 2), smem_desc(da + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+          }
+          tc_commit(&sp_full[sb]);
+          any = true;
+        }
+        __syncwarp();
+      }
+      if (i >= 1) {
+        const int ii = i - 1, st = ii % NST;
+        if (!warp_wait(ds_full, ii & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t pa = smem_u32(smem + L::OFF_P), dsa = smem_u32(smem + L::OFF_DS);
+          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
+#pragma unroll
+          for (int kk = 0; kk < 64 / 16; ++kk) {
+            tc_mma_f16(tmem + 256, smem_desc(pa + kk * 32, 16, 1024, 2), smem_desc(da + kk * 2048, A64, 1024, 2),
+                       IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16(tmem + 256 + HD, smem_desc(dsa + kk * 32, 16, 1024, 2), smem_desc(qa + kk * 2048, A64, 1024, 2),
+                       IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(ds_free);
+          tc_commit(&qd_empty[st]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0 && any) {
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;   // key row
+    const int k = k0 + r;
+    const bool kvalid = k < a.S;
+    const int tid = threadIdx.x - 64;
+    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
+    bool ok = k0 < a.S;
+    for (int i = 0; i < n_it && ok; ++i) {
+      const int sb = i & 1;
+      const int g = i / n_q, qi = qt_lo + i % n_q;
+      const int h = hk * G + g;
+      const int qb0 = qi * 64;
+      const int64_t bh = (int64_t)b * a.H + h;
+      // double-buffered staging: buffer i&1 was last read in iteration i-2, and every
+      // thread has passed ld_full of iteration i-1 (all 128 arrivals) since then
+      float* s_lse2 = s_ld + (i & 1) * 192;
+      float* s_D = s_lse2 + 64;
+      int* s_seg = reinterpret_cast<int*>(s_lse2 + 128);
+      if (tid < 64) {
+        const int qq = qb0 + tid;
+        s_lse2[tid] = qq < a.S ? __ldg(a.lse + bh * a.S + qq) * LOG2E : INFINITY;
+        if (a.seg_start != nullptr) s_seg[tid] = qq < a.S ? __ldg(a.seg_start + row0 + qq) : -1;
+      } else {
+        const int qq = qb0 + tid - 64;
+        s_D[tid - 64] = qq < a.S ? __ldg(a.D + bh * a.S + qq) : 0.f;
+      }
+      mbar_arrive(&ld_full[i & 1]);
+      if (!warp_wait(&ld_full[i & 1], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      if (!warp_wait(&sp_full[sb], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64], dr[64];
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sp_empty[sb]);
+      if (i >= 1 && !warp_wait(ds_free, (i - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = smem + L::OFF_P + r * 128;
+      uint8_t* drow = smem + L::OFF_DS + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t wp[4], wd[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int y = 0; y < 2; ++y) {
+            const int c = ch * 8 + 2 * x + y;
+            const int q = qb0 + c;
+            bool vis = kvalid && q < a.S && q >= k;
+            if (a.window > 0) vis = vis && (q - k < a.window);
+            if (a.seg_start != nullptr) vis = vis && s_seg[c] >= 0 && s_seg[c] <= k;
+            const float p = vis ? fast_exp2(__uint_as_float(sr[c]) * a.scale_log2 - s_lse2[c]) : 0.f;
+            pv[y] = p;
+            dv2[y] = p * (__uint_as_float(dr[c]) - s_D[c]);
+          }
+          __nv_bfloat162 p2 = __floats2bfloat162_rn(pv[0], pv[1]);
+          __nv_bfloat162 d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
+          wp[x] = *reinterpret_cast<uint32_t*>(&p2);
+          wd[x] = *reinterpret_cast<uint32_t*>(&d2);
+        }
+        const int sw = (ch ^ (r & 7)) * 16;
+        *reinterpret_cast<uint4*>(prow + sw) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
+        *reinterpret_cast<uint4*>(drow + sw) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && n_it > 0 && warp_wait(ds_free, (n_it - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      __nv_bfloat16* dvo = a.dv + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
+      __nv_bfloat16* dko = a.dk + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {
+        const float mul = part == 0 ? 1.0f : a.scale;
+        __nv_bfloat16* dst_row = part == 0 ? dvo : dko;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + lb + 256 + part * HD + c * 32, v);
+          tc_wait_ld();
+          if (kvalid) {
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+              uint32_t w[4];
+#pragma unroll
+              for (int y = 0; y < 4; ++y) {
+                __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(v[x * 8 + 2 * y]) * mul,
+                                                          __uint_as_float(v[x * 8 + 2 * y + 1]) * mul);
+                w[y] = *reinterpret_cast<uint32_t*>(&pp);
+              }
+              dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace zs
+
+extern "C" int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                     const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H,
+                                     int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
+                                     int sink_dtype, float* ds_sink, float softmax_scale, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv && D, ZS_ERR_ARG);
+  ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(hd == 64 || hd == 128, ZS_ERR_SHAPE);
+  ZS_REQUIRE((k_sink == nullptr) == (ds_sink == nullptr), ZS_ERR_ARG);
+  ZS_REQUIRE(k_sink == nullptr || sink_dtype == ZS_F32 || sink_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_REQUIRE((int64_t)B * S < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  ZS_BIND(q);
+  int64_t blocks = ((int64_t)B * S * H + 7) / 8;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  attn::attn_bwd_prep_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dout), D, B, S, H, hd);
+  ZS_CUDA_TRY(cudaGetLastError());
+  const uint64_t rows = (uint64_t)B * S;
+  CUtensorMap tq128, tdo128, tk64, tv64, tk128, tv128, tq64, tdo64;
+  int rc;
+  const uint64_t qw = (uint64_t)H * hd, kw = (uint64_t)Hkv * hd;
+  if ((rc = make_tmap(&tq128, q, ZS_BF16, qw, rows, qw * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tdo128, dout, ZS_BF16, qw, rows, qw * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tq64, q, ZS_BF16, qw, rows, qw * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tdo64, dout, ZS_BF16, qw, rows, qw * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk128, k, ZS_BF16, kw, rows, kw * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv128, v, ZS_BF16, kw, rows, kw * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk64, k, ZS_BF16, kw, rows, kw * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv64, v, ZS_BF16, kw, rows, kw * 2, 64, 64)) != ZS_OK) return rc;
+  attn::BwdArgs a{};
+  a.B = B;
+  a.S = S;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.hd = hd;
+  a.window = window;
+  a.scale = softmax_scale;
+  a.scale_log2 = softmax_scale * attn::LOG2E;
+  a.seg_start = seg_start;
+  a.lse = lse;
+  a.D = D;
+  a.k_sink = k_sink;
+  a.sink_dtype = sink_dtype;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq);
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk);
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  dim3 gq((S + 127) / 128, H, B), gkv((S + 127) / 128, Hkv, B);
+  if (hd == 128) {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DqSmem<128>::ALLOC));
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DkvSmem<128>::ALLOC));
+    attn::attn_bwd_dq_kernel<128><<<gq, 192, attn::DqSmem<128>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+                                                                                 ds_sink);
+    ZS_CUDA_TRY(cudaGetLastError());
+    attn::attn_bwd_dkv_kernel<128><<<gkv, 192, attn::DkvSmem<128>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
+  } else {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DqSmem<64>::ALLOC));
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DkvSmem<64>::ALLOC));
+    attn::attn_bwd_dq_kernel<64><<<gq, 192, attn::DqSmem<64>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+                                                                               ds_sink);
+    ZS_CUDA_TRY(cudaGetLastError());
+    attn::attn_bwd_dkv_kernel<64><<<gkv, 192, attn::DkvSmem<64>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
+  }
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}

@@ -5,4 +5,5 @@
 #include "zs_moe.cu"
 #include "zs_routing.cu"
 #include "zs_norm.cu"
+#include "zs_attn.cu"
 #include "zs_api.cu"

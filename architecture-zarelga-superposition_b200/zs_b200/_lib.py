@@ -53,6 +53,10 @@ _SIGNATURES = {
     "zs_zrmsnorm_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "zs_rope": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                        _i32, _vp]),
+    "zs_attention_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i32,
+                                    _f32, _vp]),
+    "zs_attention_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+                                     _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp]),
     "zs_newton_schulz5_workspace": (_sz, [_i64, _i64, _i64, _i32]),
     "zs_newton_schulz5": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _f32, _f32, _f32, _vp, _sz, _i32, _vp]),
     "zs_xent_forward_workspace": (_sz, [_i64, _i64]),

@@ -280,6 +280,41 @@ int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const 
             const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch, int seq_len, int cos_batch,
             int n_q_heads, int n_kv_heads, int head_dim, int dtype, int table_dtype, int backward, void* stream);
 
+/* ------------------------------------------------ attention core (a13, a15) */
+
+/*
+ * Causal grouped-query attention as GatedAttention calls flash_attn_varlen_func
+ * (modeling/attention.py:131-169, window_size = (W-1, 0) at :31), with the
+ * optional per-head sink key of modeling/hca.py:138-144,264-298 (an extra
+ * always-visible key k_sink[h] whose value is zero):
+ *   o[b, q, h]  = sum_{k visible} softmax_k(scale * q.k) v[b, k, h / (H/Hkv)]
+ *   lse[b, h, q] = natural log of the softmax denominator (sink included)
+ * Key k is visible to query q when k <= q, q - k < window (window <= 0: no
+ * window) and, with seg_start, seg_start[q] >= 0 and k >= seg_start[q]
+ * (packed sequences: seg_start[b*S + i] is the first position of token i's
+ * sequence in batch row b, -1 marks padding).
+ * q [B*S, H*hd], k/v [B*S, Hkv*hd], o [B*S, H*hd]: bf16, rows contiguous;
+ * lse f32 [B, H, S]; hd 64 or 128; k_sink [H, hd] f32 or bf16 (sink_dtype) or NULL.
+ */
+int zs_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int S, int H,
+                         int Hkv, int hd, int window, const int* seg_start, const void* k_sink, int sink_dtype,
+                         float softmax_scale, void* stream);
+
+/*
+ * Backward of zs_attention_forward (flash_attn's backward as autograd runs it
+ * for attention.py:131-169).  Inputs: q, k, v, o, dout (bf16, layouts as in
+ * the forward), lse from the forward.  Outputs: dq, dk, dv (bf16, same
+ * layouts; dk/dv sum over the heads of a GQA group), D (f32 [B, H, S]
+ * scratch: rowsum(dout * o)), and with k_sink: ds_sink (f32 [B, H, S]) =
+ * d loss / d (sink logit) per query row; the sink's own gradient is
+ * scale * sum_{b,q} ds_sink[b, h, q] * q[b, q, h, :].  dq already holds the
+ * sink key's share.
+ */
+int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                          const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H, int Hkv,
+                          int hd, int window, const int* seg_start, const void* k_sink, int sink_dtype,
+                          float* ds_sink, float softmax_scale, void* stream);
+
 /* ------------------------------------------------ cross entropy (a16-a18) */
 
 /*

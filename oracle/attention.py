@@ -7,6 +7,14 @@ Restates (CoffeeVampir3/Architecture-Zarelga-Superposition):
   * ZeroCenteredRMSNorm            modeling/zRMSNorm.py:10-17
   * position-RoPE tables           modeling/attention.py:85-104
   * rotate-half RoPE fwd / bwd     modeling/liger_rope.py:98-119
+  * attention core                 modeling/attention.py:117-169 (flash_attn_varlen_func,
+                                   causal, window (W-1, 0) from :31) restated as exact
+                                   per-sequence causal softmax attention; the sink key
+                                   of modeling/hca.py:138-144,264-298 (k_sink[h], value 0,
+                                   always visible).  flash-attn itself (pyproject.toml:16)
+                                   ships no test for this, so this restatement is pinned
+                                   to PyTorch's scaled_dot_product_attention on the CPU
+                                   with hca.py's sink concatenation (tests/test_attn_oracle.py).
 """
 from __future__ import annotations
 
@@ -58,3 +66,89 @@ def rope(x, cos, sin, backward=False):
         s = -s
     x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
     return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+
+def attention_visibility(S, window=0, seg_start=None):
+    """bool [B or 1, S(q), S(k)]: k <= q, q - k < window (window > 0), same packed sequence.
+
+    seg_start [B, S] int: first row position of each token's sequence, -1 on padding.
+    """
+    i = np.arange(S)
+    vis = i[None, :] <= i[:, None]
+    if window and window > 0:
+        vis &= (i[:, None] - i[None, :]) < window
+    vis = vis[None]
+    if seg_start is not None:
+        seg = np.asarray(seg_start)
+        vis = vis & (seg[:, :, None] >= 0) & (i[None, None, :] >= seg[:, :, None])
+    return vis
+
+
+def attention_forward(q, k, v, *, window=0, seg_start=None, k_sink=None, scale=None):
+    """(o [B,S,H,hd], lse [B,H,S]) in float64.  q [B,S,H,hd], k/v [B,S,Hkv,hd], k_sink [H,hd] or None.
+
+    softmax over the visible keys (plus the sink logit scale*q.k_sink with a zero value row);
+    lse is the natural log of the denominator; a row that sees nothing gives o = 0, lse = -inf.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    B, S, H, hd = q.shape
+    G = H // k.shape[2]
+    scale = 1.0 / np.sqrt(hd) if scale is None else scale
+    vis = attention_visibility(S, window, seg_start)
+    vis = np.broadcast_to(vis, (B, S, S))
+    o = np.zeros_like(q)
+    lse = np.full((B, H, S), -np.inf)
+    for b in range(B):
+        for h in range(H):
+            s = scale * q[b, :, h] @ k[b, :, h // G].T
+            s = np.where(vis[b], s, -np.inf)
+            vv = v[b, :, h // G]
+            if k_sink is not None:
+                ks = np.asarray(k_sink, dtype=np.float64)[h]
+                s = np.concatenate([s, scale * (q[b, :, h] @ ks)[:, None]], axis=1)
+                vv = np.concatenate([vv, np.zeros((1, hd))], axis=0)
+            m = s.max(axis=1, keepdims=True)
+            live = np.isfinite(m[:, 0])
+            msafe = np.where(np.isfinite(m), m, 0.0)
+            p = np.exp(s - msafe)
+            l = p.sum(axis=1, keepdims=True)
+            o[b, :, h] = np.where(live[:, None], (p @ vv) / np.where(l > 0, l, 1.0), 0.0)
+            lse[b, h] = np.where(live, msafe[:, 0] + np.log(np.where(l[:, 0] > 0, l[:, 0], 1.0)), -np.inf)
+    return o, lse
+
+
+def attention_backward(do, q, k, v, *, window=0, seg_start=None, k_sink=None, scale=None):
+    """(dq, dk, dv, dk_sink or None) in float64 for the loss sum(do * o) of attention_forward."""
+    do = np.asarray(do, dtype=np.float64)
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    B, S, H, hd = q.shape
+    G = H // k.shape[2]
+    scale = 1.0 / np.sqrt(hd) if scale is None else scale
+    o, lse = attention_forward(q, k, v, window=window, seg_start=seg_start, k_sink=k_sink, scale=scale)
+    vis = np.broadcast_to(attention_visibility(S, window, seg_start), (B, S, S))
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    dks = np.zeros((H, hd)) if k_sink is not None else None
+    for b in range(B):
+        for h in range(H):
+            kk, vv = k[b, :, h // G], v[b, :, h // G]
+            L = lse[b, h][:, None]
+            Lsafe = np.where(np.isfinite(L), L, 0.0)
+            s = scale * q[b, :, h] @ kk.T
+            p = np.where(vis[b], np.exp(s - Lsafe), 0.0)
+            dP = do[b, :, h] @ vv.T
+            D = (do[b, :, h] * o[b, :, h]).sum(axis=1, keepdims=True)
+            dS = p * (dP - D)
+            dq[b, :, h] = scale * dS @ kk
+            dk[b, :, h // G] += scale * dS.T @ q[b, :, h]
+            dv[b, :, h // G] += p.T @ do[b, :, h]
+            if k_sink is not None:
+                ks = np.asarray(k_sink, dtype=np.float64)[h]
+                ps = np.where(np.isfinite(L[:, 0]), np.exp(scale * (q[b, :, h] @ ks) - Lsafe[:, 0]), 0.0)
+                dss = -ps * D[:, 0]
+                dq[b, :, h] += scale * dss[:, None] * ks[None, :]
+                dks[h] += scale * dss @ q[b, :, h]
+    return dq, dk, dv, dks
