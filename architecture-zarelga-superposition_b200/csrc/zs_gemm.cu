@@ -1464,15 +1464,25 @@ namespace zs {
 // X / (X.norm(dim=(-2,-1), keepdim=True) + 1e-7) evaluates it on a bf16 tensor:
 // the norm (f32 accumulation) is rounded to the dtype, the sum with 1e-7 and
 // the quotient each round once more.
+// Deterministic two-level reduction over 16-byte vectors: NS_SUMSQ_BLOCKS
+// blocks per matrix write partial sums of squares (fixed split, no atomics),
+// one thread per matrix adds them in order and forms the divisor, then a
+// grid-wide pass divides.  The result does not depend on the batch size.
+constexpr int NS_SUMSQ_BLOCKS = 32;
+
 template <typename T>
-__global__ void ns_normalize_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t per) {
-  const int64_t e = blockIdx.x;
-  const T* xe = x + e * per;
-  T* ye = y + e * per;
+__global__ void ns_sumsq_kernel(const T* __restrict__ x, float* __restrict__ partial, int64_t per_vec) {
+  const int64_t e = blockIdx.y;
+  const uint4* xe = reinterpret_cast<const uint4*>(x) + e * per_vec;
   float ss = 0.f;
-  for (int64_t i = threadIdx.x; i < per; i += blockDim.x) {
-    const float v = to_f32<T>(xe[i]);
-    ss = fmaf(v, v, ss);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_vec; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 u = __ldg(xe + i);
+    const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float v = to_f32<T>(t[k]);
+      ss = fmaf(v, v, ss);
+    }
   }
   __shared__ float sh[32];
 #pragma unroll
@@ -1483,18 +1493,58 @@ __global__ void ns_normalize_kernel(const T* __restrict__ x, T* __restrict__ y, 
     float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    if (threadIdx.x == 0) sh[0] = v;
+    if (threadIdx.x == 0) partial[e * NS_SUMSQ_BLOCKS + blockIdx.x] = v;
   }
-  __syncthreads();
-  const float nrm = to_f32<T>(from_f32<T>(sqrtf(sh[0])));
-  const float den = to_f32<T>(from_f32<T>(nrm + 1e-7f));
-  for (int64_t i = threadIdx.x; i < per; i += blockDim.x) ye[i] = from_f32<T>(__fdiv_rn(to_f32<T>(xe[i]), den));
+}
+
+// the divisor as X / (X.norm() + 1e-7) forms it on a 16-bit tensor: the norm
+// (f32 accumulation) rounds to the dtype, so do the sum with 1e-7
+template <typename T>
+__global__ void ns_divisor_kernel(float* __restrict__ partial, int64_t batch) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= batch) return;
+  float ss = 0.f;
+  for (int b = 0; b < NS_SUMSQ_BLOCKS; ++b) ss += partial[e * NS_SUMSQ_BLOCKS + b];
+  const float nrm = to_f32<T>(from_f32<T>(sqrtf(ss)));
+  partial[e * NS_SUMSQ_BLOCKS] = to_f32<T>(from_f32<T>(nrm + 1e-7f));
+}
+
+template <typename T>
+__global__ void ns_scale_kernel(const T* __restrict__ x, T* __restrict__ y, const float* __restrict__ div,
+                                int64_t per_vec, int64_t total_vec) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total_vec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i / per_vec;
+    const float den = __ldg(div + e * NS_SUMSQ_BLOCKS);
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    T* t = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = from_f32<T>(__fdiv_rn(to_f32<T>(t[k]), den));
+    reinterpret_cast<uint4*>(y)[i] = u;
+  }
+}
+
+template <typename T>
+static int ns_normalize(const void* G, void* X, float* partial, int64_t batch, int64_t per, cudaStream_t stream) {
+  const int64_t per_vec = per / 8;
+  ns_sumsq_kernel<T><<<dim3((unsigned)NS_SUMSQ_BLOCKS, (unsigned)batch), 256, 0, stream>>>(
+      reinterpret_cast<const T*>(G), partial, per_vec);
+  ZS_CUDA_TRY(cudaGetLastError());
+  ns_divisor_kernel<T><<<(unsigned)((batch + 127) / 128), 128, 0, stream>>>(partial, batch);
+  ZS_CUDA_TRY(cudaGetLastError());
+  const int64_t total = batch * per_vec;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  ns_scale_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(reinterpret_cast<const T*>(G), reinterpret_cast<T*>(X),
+                                                           partial, per_vec, total);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
 }
 }  // namespace zs
 
 extern "C" size_t zs_newton_schulz5_workspace(int64_t batch, int64_t m, int64_t n, int dtype) {
   const int es = elem_size(dtype);
-  return (size_t)(2 * batch * m * m + batch * m * n) * es + 3 * 256;
+  return (size_t)(2 * batch * m * m + batch * m * n) * es + (size_t)((batch * 32 * 4 + 255) / 256) * 256 + 4 * 256;
 }
 
 extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int64_t n, int steps, float a,
@@ -1506,6 +1556,8 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
   ZS_REQUIRE(batch * m < ((int64_t)1 << 31) && batch <= MAX_EXPERTS_GEMM && n < ((int64_t)1 << 24), ZS_ERR_SHAPE);
   ZS_REQUIRE((m * elem_size(dtype)) % 16 == 0 && (n * elem_size(dtype)) % 16 == 0, ZS_ERR_ALIGN);
   ZS_REQUIRE(workspace && workspace_bytes >= zs_newton_schulz5_workspace(batch, m, n, dtype), ZS_ERR_WORKSPACE);
+  ZS_REQUIRE((reinterpret_cast<uintptr_t>(G) % 16) == 0 && (reinterpret_cast<uintptr_t>(X_out) % 16) == 0,
+             ZS_ERR_ALIGN);
   ZS_BIND(G);
   const int es = elem_size(dtype);
   constexpr int BN = 256;
@@ -1513,14 +1565,13 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
   char* Abuf = ws;
   char* Bbuf = Abuf + ((batch * m * m * es + 255) / 256) * 256;
   char* Xtmp = Bbuf + ((batch * m * m * es + 255) / 256) * 256;
+  float* ss = reinterpret_cast<float*>(Xtmp + ((batch * m * n * es + 255) / 256) * 256);  // [batch, 32] partials
   // X0 = G / (||G|| + 1e-7) -> X_out; iterate X_out -> Xtmp -> X_out ...
-  if (dtype == ZS_BF16)
-    ns_normalize_kernel<__nv_bfloat16><<<(unsigned)batch, 1024, 0, stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(G), reinterpret_cast<__nv_bfloat16*>(X_out), m * n);
-  else
-    ns_normalize_kernel<__half><<<(unsigned)batch, 1024, 0, stream>>>(reinterpret_cast<const __half*>(G),
-                                                                      reinterpret_cast<__half*>(X_out), m * n);
-  ZS_CUDA_TRY(cudaGetLastError());
+  {
+    const int rc = dtype == ZS_BF16 ? ns_normalize<__nv_bfloat16>(G, X_out, ss, batch, m * n, stream)
+                                    : ns_normalize<__half>(G, X_out, ss, batch, m * n, stream);
+    if (rc != ZS_OK) return rc;
+  }
   char* X = reinterpret_cast<char*>(X_out);
   char* Xn = Xtmp;
   for (int it = 0; it < steps; ++it) {

@@ -6,4 +6,5 @@
 #include "zs_routing.cu"
 #include "zs_norm.cu"
 #include "zs_attn.cu"
+#include "zs_muon.cu"
 #include "zs_api.cu"

@@ -1,0 +1,496 @@
+// MuonMD bookkeeping around Newton-Schulz (optimizer/muon.py:398-508), fused.
+//
+// The reference runs the magnitude/direction step as ~40 f32 tensor passes
+// over each weight stack W [L, m, n] (the gain outer product is materialised,
+// W / g, g * G, the momentum lerps, the projection, the gain reductions ...).
+// Here it is three passes over the stack plus one tiny kernel:
+//   md_pre_kernel     reads W, G, buf -> writes buf and the bf16 Newton-Schulz
+//                     input X = lerp(g*G, buf', momentum); reduces the gain
+//                     gradients (W/g)*G over the axes each gain does not span
+//   md_reduce_kernel  reads W, U (the orthogonalised update) -> sum of squares
+//                     of W_hat' = W/g - lr*rescale*U per matrix / row / column
+//   md_gain_kernel    gain Adam steps (softplus chain rule), projection scales
+//   md_write_kernel   reads W, U -> p = g_new * W_hat' * target / ||W_hat'||
+// Tile: 64 rows x 256 columns per block of 256 threads; warp w owns rows
+// w*8 .. w*8+7, lane owns 8 consecutive columns (two float4 per f32 operand).
+#include <initializer_list>
+#include <type_traits>
+
+#include "zs_common.cuh"
+
+namespace zs {
+namespace md {
+
+constexpr int TR = 64, TC = 256, THREADS = 256;
+
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// torch.lerp's two-sided form
+__device__ __forceinline__ float lerp_f(float a, float b, float w) {
+  const float d = b - a;
+  return w < 0.5f ? a + w * d : b - d * (1.f - w);
+}
+
+struct Gains {
+  const float* sc;   // raw scalar gain [L] or null
+  const float* row;  // raw row gain [L, m] or null
+  const float* col;  // raw column gain [L, n] or null
+};
+
+// 8 consecutive f32 of a row (vectorised when VEC)
+template <bool VEC>
+__device__ __forceinline__ void load8(const float* p, int64_t c, int64_t n, float (&v)[8]) {
+  if (VEC) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p + c));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p + c + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = c + e < n ? p[c + e] : 0.f;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void load8_mut(const float* p, int64_t c, int64_t n, float (&v)[8]) {
+  if (VEC) {
+    const float4 a = *reinterpret_cast<const float4*>(p + c);
+    const float4 b = *reinterpret_cast<const float4*>(p + c + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = c + e < n ? p[c + e] : 0.f;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store8(float* p, int64_t c, int64_t n, const float (&v)[8]) {
+  if (VEC) {
+    *reinterpret_cast<float4*>(p + c) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + c + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (c + e < n) p[c + e] = v[e];
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, int64_t c, int64_t n, float (&v)[8]) {
+  if (VEC) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + c));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = c + e < n ? __bfloat162float(p[c + e]) : 0.f;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, int64_t c, int64_t n, const float (&v)[8]) {
+  if (VEC) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    *reinterpret_cast<uint4*>(p + c) = u;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (c + e < n) p[c + e] = __float2bfloat16_rn(v[e]);
+  }
+}
+
+// block-wide sum; every thread gets the result
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < THREADS / 32; ++w) t += sh[w];
+  return t;
+}
+
+// softplus'd gains of the tile into shared memory (1 where a gain is absent)
+__device__ __forceinline__ float tile_gains(const Gains& g, int64_t l, int64_t m, int64_t n, int64_t r0, int64_t c0,
+                                            float* s_r, float* s_c) {
+  for (int i = threadIdx.x; i < TR; i += THREADS)
+    s_r[i] = (g.row != nullptr && r0 + i < m) ? softplus_f(g.row[l * m + r0 + i]) : 1.f;
+  for (int i = threadIdx.x; i < TC; i += THREADS)
+    s_c[i] = (g.col != nullptr && c0 + i < n) ? softplus_f(g.col[l * n + c0 + i]) : 1.f;
+  return g.sc != nullptr ? softplus_f(g.sc[l]) : 1.f;
+}
+
+// Pre-Newton-Schulz: buf.lerp_(g*G, 1-mom); X = lerp(g*G, buf, mom) (bf16);
+// gain gradients (before the sigmoid factor) from the old gains:
+//   red_s[l]    += sum (W/g)*G * r*c     red_r[l,i] += sum_j (W/g)*G * c*s
+//   red_c[l,j]  += sum_i (W/g)*G * r*s
+template <bool VEC>
+__global__ void __launch_bounds__(THREADS) md_pre_kernel(const float* __restrict__ W, const float* __restrict__ G,
+                                                         float* __restrict__ buf, Gains gains,
+                                                         __nv_bfloat16* __restrict__ X, float* __restrict__ red_s,
+                                                         float* __restrict__ red_r, float* __restrict__ red_c,
+                                                         int64_t m, int64_t n, float mom) {
+  __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
+  const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
+  const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool have_g = gains.sc != nullptr || gains.row != nullptr || gains.col != nullptr;
+  const int64_t c = c0 + lane * 8;
+  float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float sacc = 0.f;
+  for (int k = 0; k < 8; ++k) {
+    const int rr = warp * 8 + k;
+    const int64_t row = r0 + rr;
+    if (row >= m) break;
+    float racc = 0.f;
+    if (c < n) {
+      const int64_t off = (l * m + row) * n;
+      float w[8], gr[8], b[8], x[8];
+      load8<VEC>(W + off, c, n, w);
+      load8<VEC>(G + off, c, n, gr);
+      load8_mut<VEC>(buf + off, c, n, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float cg = s_c[lane * 8 + e];
+        float gh = gr[e];
+        if (have_g) {
+          const float gv = (sc * s_r[rr]) * cg;
+          const float wg = (w[e] / gv) * gr[e];
+          gh = gv * gr[e];
+          racc += wg * (cg * sc);
+          colacc[e] += wg * (s_r[rr] * sc);
+          sacc += wg * (s_r[rr] * cg);
+        }
+        b[e] = lerp_f(b[e], gh, 1.f - mom);
+        x[e] = lerp_f(gh, b[e], mom);
+      }
+      store8<VEC>(buf + off, c, n, b);
+      store8_bf16<VEC>(X + off, c, n, x);
+    }
+    if (red_r != nullptr) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+      if (lane == 0) atomicAdd(red_r + l * m + row, racc);
+    }
+  }
+  if (red_c != nullptr) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_col[warp][lane * 8 + e] = colacc[e];
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += s_col[w][threadIdx.x];
+    if (c0 + threadIdx.x < n) atomicAdd(red_c + l * n + c0 + threadIdx.x, t);
+  }
+  if (red_s != nullptr) {
+    const float t = block_sum(sacc, sh);
+    if (threadIdx.x == 0) atomicAdd(red_s + l, t);
+  }
+}
+
+struct PostArgs {
+  const float* W;
+  const __nv_bfloat16* U;
+  int64_t m, n;
+  const float* lr_dev;
+  float lr_host;
+  float rescale;
+  int norm_axis;          // 0 frobenius, 1 row, 2 column
+};
+
+__device__ __forceinline__ float lr_of(const PostArgs& a) { return a.lr_dev != nullptr ? __ldg(a.lr_dev) : a.lr_host; }
+
+// sum of squares of W_hat' = W/g - lr * (rescale * U) per matrix / row / column
+template <bool VEC>
+__global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains gains, float* __restrict__ ss) {
+  __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
+  const int64_t m = a.m, n = a.n;
+  const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
+  const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float lr = lr_of(a);
+  const int64_t c = c0 + lane * 8;
+  float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float facc = 0.f;
+  for (int k = 0; k < 8; ++k) {
+    const int rr = warp * 8 + k;
+    const int64_t row = r0 + rr;
+    if (row >= m) break;
+    float racc = 0.f;
+    if (c < n) {
+      const int64_t off = (l * m + row) * n;
+      float w[8], u[8];
+      load8<VEC>(a.W + off, c, n, w);
+      load8_bf16<VEC>(a.U + off, c, n, u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (c + e >= n) continue;
+        const float gv = (sc * s_r[rr]) * s_c[lane * 8 + e];
+        const float wh = w[e] / gv - lr * (u[e] * a.rescale);
+        const float q = wh * wh;
+        racc += q;
+        colacc[e] += q;
+        facc += q;
+      }
+    }
+    if (a.norm_axis == 1) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+      if (lane == 0) atomicAdd(ss + l * m + row, racc);
+    }
+  }
+  if (a.norm_axis == 2) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_col[warp][lane * 8 + e] = colacc[e];
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += s_col[w][threadIdx.x];
+    if (c0 + threadIdx.x < n) atomicAdd(ss + l * n + c0 + threadIdx.x, t);
+  } else if (a.norm_axis == 0) {
+    const float t = block_sum(facc, sh);
+    if (threadIdx.x == 0) atomicAdd(ss + l, t);
+  }
+}
+
+struct GainArgs {
+  float* raw[3];          // scalar [L], row [L, m], col [L, n] (in/out), null when absent
+  float* m1[3];
+  float* m2[3];
+  const float* red[3];    // reductions from md_pre_kernel
+  float* sp_old[3];       // out: softplus of the old / new raw gains
+  float* sp_new[3];
+  int64_t len[3];
+  const float* step_dev;  // gain step after the increment (device) or null
+  float step_host;
+  float b1, b2, eps, gain_lr;
+  const float* ss;        // sums of squares [n_proj]
+  const float* target;    // target norms [n_proj]
+  float* proj;            // out: target / (sqrt(ss) + 1e-12)
+  int64_t n_proj;
+};
+
+// Adam on the raw gains with dL/draw = reduction * sigmoid(raw) (all from the old gains),
+// raw -= gain_lr * update; and the sphere projection factors.
+__global__ void md_gain_kernel(GainArgs a) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float step = a.step_dev != nullptr ? __ldg(a.step_dev) : a.step_host;
+  const float bc1 = 1.f - powf(a.b1, step), bc2 = 1.f - powf(a.b2, step);
+  for (int k = 0; k < 3; ++k) {
+    if (a.raw[k] == nullptr) continue;
+    for (int64_t i = tid; i < a.len[k]; i += stride) {
+      const float raw = a.raw[k][i];
+      const float gr = a.red[k][i] * sigmoid_f(raw);
+      const float m1 = lerp_f(a.m1[k][i], gr, 1.f - a.b1);
+      const float m2 = lerp_f(a.m2[k][i], gr * gr, 1.f - a.b2);
+      a.m1[k][i] = m1;
+      a.m2[k][i] = m2;
+      const float upd = (m1 / bc1) / (sqrtf(m2 / bc2) + a.eps);
+      const float nr = raw + (-a.gain_lr) * upd;
+      a.raw[k][i] = nr;
+      a.sp_old[k][i] = softplus_f(raw);
+      a.sp_new[k][i] = softplus_f(nr);
+    }
+  }
+  for (int64_t i = tid; i < a.n_proj; i += stride) a.proj[i] = a.target[i] / (sqrtf(a.ss[i]) + 1e-12f);
+}
+
+struct WriteArgs {
+  const float* sp_old[3];  // null when the gain is absent
+  const float* sp_new[3];
+  const float* proj;
+};
+
+template <bool VEC, typename TP>
+__global__ void __launch_bounds__(THREADS) md_write_kernel(PostArgs a, WriteArgs wa, TP* __restrict__ p) {
+  __shared__ float s_ro[TR], s_rn[TR], s_co[TC], s_cn[TC];
+  const int64_t m = a.m, n = a.n;
+  const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
+  for (int i = threadIdx.x; i < TR; i += THREADS) {
+    const bool ok = wa.sp_old[1] != nullptr && r0 + i < m;
+    s_ro[i] = ok ? wa.sp_old[1][l * m + r0 + i] : 1.f;
+    s_rn[i] = ok ? wa.sp_new[1][l * m + r0 + i] : 1.f;
+  }
+  for (int i = threadIdx.x; i < TC; i += THREADS) {
+    const bool ok = wa.sp_old[2] != nullptr && c0 + i < n;
+    s_co[i] = ok ? wa.sp_old[2][l * n + c0 + i] : 1.f;
+    s_cn[i] = ok ? wa.sp_new[2][l * n + c0 + i] : 1.f;
+  }
+  const float so = wa.sp_old[0] != nullptr ? wa.sp_old[0][l] : 1.f;
+  const float sn = wa.sp_new[0] != nullptr ? wa.sp_new[0][l] : 1.f;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float lr = lr_of(a);
+  const int64_t c = c0 + lane * 8;
+  if (c >= n) return;
+  const float pf = a.norm_axis == 0 ? wa.proj[l] : 1.f;
+  float pc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) pc[e] = (a.norm_axis == 2 && c + e < n) ? wa.proj[l * n + c + e] : 1.f;
+  for (int k = 0; k < 8; ++k) {
+    const int rr = warp * 8 + k;
+    const int64_t row = r0 + rr;
+    if (row >= m) break;
+    const float pr = a.norm_axis == 1 ? wa.proj[l * m + row] : pf;
+    const int64_t off = (l * m + row) * n;
+    float w[8], u[8], o[8];
+    load8<VEC>(a.W + off, c, n, w);
+    load8_bf16<VEC>(a.U + off, c, n, u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float go = (so * s_ro[rr]) * s_co[lane * 8 + e];
+      const float gn = (sn * s_rn[rr]) * s_cn[lane * 8 + e];
+      const float wh = (w[e] / go - lr * (u[e] * a.rescale)) * (a.norm_axis == 2 ? pc[e] : pr);
+      o[e] = gn * wh;
+    }
+    if constexpr (std::is_same<TP, float>::value) {
+      store8<VEC>(p + off, c, n, o);
+    } else {
+      store8_bf16<VEC>(p + off, c, n, o);
+    }
+  }
+}
+
+}  // namespace md
+}  // namespace zs
+
+using namespace zs;
+
+static bool md_vec_ok(int64_t n, std::initializer_list<const void*> ptrs) {
+  if (n % 8 != 0) return false;
+  for (const void* p : ptrs)
+    if (p != nullptr && (reinterpret_cast<uintptr_t>(p) % 16) != 0) return false;
+  return true;
+}
+
+static dim3 md_grid(int64_t L, int64_t m, int64_t n) {
+  return dim3((unsigned)((n + md::TC - 1) / md::TC), (unsigned)((m + md::TR - 1) / md::TR), (unsigned)L);
+}
+
+extern "C" int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
+                             const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col,
+                             int64_t L, int64_t m, int64_t n, float momentum, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(W && G && buf && x_out, ZS_ERR_ARG);
+  ZS_REQUIRE(L >= 1 && m >= 1 && n >= 1 && L < 65536 && (m + md::TR - 1) / md::TR < 65536, ZS_ERR_SHAPE);
+  ZS_REQUIRE((g_scalar == nullptr) == (red_scalar == nullptr) && (g_row == nullptr) == (red_row == nullptr) &&
+                 (g_col == nullptr) == (red_col == nullptr),
+             ZS_ERR_ARG);
+  ZS_BIND(W);
+  md::Gains g{g_scalar, g_row, g_col};
+  auto* X = reinterpret_cast<__nv_bfloat16*>(x_out);
+  const dim3 grid = md_grid(L, m, n);
+  if (md_vec_ok(n, {W, G, buf, x_out}))
+    md::md_pre_kernel<true><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, red_scalar, red_row, red_col, m, n,
+                                                              momentum);
+  else
+    md::md_pre_kernel<false><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, red_scalar, red_row, red_col, m, n,
+                                                               momentum);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n) {
+  // ss + proj (up to L*max(m,n) each) + softplus old/new of scalar, row, column gains
+  const int64_t mx = m > n ? m : n;
+  return (size_t)(2 * L * mx + 2 * (L + L * m + L * n)) * sizeof(float) + 8 * 256;
+}
+
+extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
+                              float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
+                              float* m1_col, float* m2_col, const float* red_scalar, const float* red_row,
+                              const float* red_col, const float* step_dev, float step_host, float b1, float b2,
+                              float eps, float gain_lr, const float* lr_dev, float lr_host, float rescale,
+                              int norm_axis, const float* target_norm, int64_t L, int64_t m, int64_t n,
+                              void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(W && U && p_out && target_norm, ZS_ERR_ARG);
+  ZS_REQUIRE(p_dtype == ZS_F32 || p_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(norm_axis >= 0 && norm_axis <= 2, ZS_ERR_ARG);
+  ZS_REQUIRE(L >= 1 && m >= 1 && n >= 1 && L < 65536 && (m + md::TR - 1) / md::TR < 65536, ZS_ERR_SHAPE);
+  ZS_REQUIRE((g_scalar == nullptr || (m1_scalar && m2_scalar && red_scalar)) &&
+                 (g_row == nullptr || (m1_row && m2_row && red_row)) &&
+                 (g_col == nullptr || (m1_col && m2_col && red_col)),
+             ZS_ERR_ARG);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_muonmd_post_workspace(L, m, n), ZS_ERR_WORKSPACE);
+  ZS_BIND(W);
+  const int64_t n_proj = norm_axis == 0 ? L : (norm_axis == 1 ? L * m : L * n);
+  float* ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  const int64_t mx = m > n ? m : n;
+  float* ss = ws;
+  float* proj = ss + L * mx;
+  float* sp = proj + L * mx;  // old: sc [L], row [L*m], col [L*n]; then new
+  float* sp_old[3] = {sp, sp + L, sp + L + L * m};
+  float* sp_new[3] = {sp_old[2] + L * n, sp_old[2] + L * n + L, sp_old[2] + L * n + L + L * m};
+  ZS_CUDA_TRY(cudaMemsetAsync(ss, 0, (size_t)n_proj * sizeof(float), stream));
+  md::PostArgs a{W, reinterpret_cast<const __nv_bfloat16*>(U), m, n, lr_dev, lr_host, rescale, norm_axis};
+  md::Gains g{g_scalar, g_row, g_col};
+  const dim3 grid = md_grid(L, m, n);
+  const bool vec = md_vec_ok(n, {W, U, p_out});
+  if (vec)
+    md::md_reduce_kernel<true><<<grid, md::THREADS, 0, stream>>>(a, g, ss);
+  else
+    md::md_reduce_kernel<false><<<grid, md::THREADS, 0, stream>>>(a, g, ss);
+  ZS_CUDA_TRY(cudaGetLastError());
+  md::GainArgs ga{};
+  float* raws[3] = {g_scalar, g_row, g_col};
+  float* m1s[3] = {m1_scalar, m1_row, m1_col};
+  float* m2s[3] = {m2_scalar, m2_row, m2_col};
+  const float* reds[3] = {red_scalar, red_row, red_col};
+  const int64_t lens[3] = {L, L * m, L * n};
+  md::WriteArgs wa{};
+  for (int k = 0; k < 3; ++k) {
+    ga.raw[k] = raws[k];
+    ga.m1[k] = m1s[k];
+    ga.m2[k] = m2s[k];
+    ga.red[k] = reds[k];
+    ga.sp_old[k] = sp_old[k];
+    ga.sp_new[k] = sp_new[k];
+    ga.len[k] = lens[k];
+    wa.sp_old[k] = raws[k] != nullptr ? sp_old[k] : nullptr;
+    wa.sp_new[k] = raws[k] != nullptr ? sp_new[k] : nullptr;
+  }
+  ga.step_dev = step_dev;
+  ga.step_host = step_host;
+  ga.b1 = b1;
+  ga.b2 = b2;
+  ga.eps = eps;
+  ga.gain_lr = gain_lr;
+  ga.ss = ss;
+  ga.target = target_norm;
+  ga.proj = proj;
+  ga.n_proj = n_proj;
+  wa.proj = proj;
+  const int64_t work = n_proj > L * (1 + m + n) ? n_proj : L * (1 + m + n);
+  int64_t blocks = (work + 255) / 256;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  md::md_gain_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ga);
+  ZS_CUDA_TRY(cudaGetLastError());
+  if (p_dtype == ZS_F32) {
+    if (vec)
+      md::md_write_kernel<true, float><<<grid, md::THREADS, 0, stream>>>(a, wa, reinterpret_cast<float*>(p_out));
+    else
+      md::md_write_kernel<false, float><<<grid, md::THREADS, 0, stream>>>(a, wa, reinterpret_cast<float*>(p_out));
+  } else {
+    if (vec)
+      md::md_write_kernel<true, __nv_bfloat16><<<grid, md::THREADS, 0, stream>>>(
+          a, wa, reinterpret_cast<__nv_bfloat16*>(p_out));
+    else
+      md::md_write_kernel<false, __nv_bfloat16><<<grid, md::THREADS, 0, stream>>>(
+          a, wa, reinterpret_cast<__nv_bfloat16*>(p_out));
+  }
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}

@@ -6,7 +6,8 @@ window, and a per-head sigmoid output gate.  An optional learned sink logit
 per head (the key-sink of modeling/hca.py:138-144, value 0) is off by default
 so the state dict matches the reference's.
 
-QK-norm and RoPE run in libzs.so; the projections are cuBLAS linears.
+QK-norm, RoPE and the attention core (tcgen05 flash attention, forward and
+backward) run in libzs.so; the projections are cuBLAS linears.
 """
 from __future__ import annotations
 
@@ -32,7 +33,7 @@ def _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len):
 
 
 class GatedAttention(nn.Module):
-    def __init__(self, config, window_size: Optional[int] = None, use_sink: bool = False):
+    def __init__(self, config, window_size: Optional[int] = None, use_sink: Optional[bool] = None):
         super().__init__()
         self.hidden_size = config.hidden_size
         self.num_heads = config.n_attention_heads
@@ -59,6 +60,8 @@ class GatedAttention(nn.Module):
         else:
             self.q_norm = nn.Identity()
             self.k_norm = nn.Identity()
+        if use_sink is None:
+            use_sink = getattr(config, "attention_sink", False)
         self.k_sink = nn.Parameter(torch.empty(self.num_heads, self.head_dim)) if use_sink else None
         self.reset_parameters()
         self.pos_rope_dims = config.pos_rope_dims

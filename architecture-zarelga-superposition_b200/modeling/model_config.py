@@ -49,6 +49,9 @@ class ModelConfig:
     initializer_range: float = field(init=False)
     tie_word_embeddings: bool = False
     pos_rope_dims: int = 16
+    # learned per-head sink key (value 0) in every GatedAttention layer; off keeps the
+    # reference's state dict
+    attention_sink: bool = False
     superposition_enabled: bool = False
     superposition_max_size: int = field(init=False)
     engram: EngramSettings = field(default_factory=EngramSettings)

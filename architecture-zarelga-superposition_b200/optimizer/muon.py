@@ -1,5 +1,5 @@
 """Muon / MuonMD optimizers with the Newton-Schulz orthogonalisation on the
-B200 tensor cores.
+B200 tensor cores and the magnitude/direction bookkeeping fused into three passes.
 
 Same public functions and classes as the reference module (optimizer/muon.py):
 zeropower_via_newtonschulz5 (:6-32), muon_update (:35-42), adam_update
@@ -7,8 +7,10 @@ zeropower_via_newtonschulz5 (:6-32), muon_update (:35-42), adam_update
 SingleDeviceMuonMDWithAuxAdam (:574-653), with the same arguments, state
 layout and defaults.  zeropower_via_newtonschulz5 runs in libzs.so (three
 batched tcgen05 GEMMs per iteration with the linear combinations fused into
-their epilogues); the magnitude/direction bookkeeping around it is f32 tensor
-arithmetic without host syncs, so a whole step can be captured in a CUDA graph.
+their epilogues); the magnitude/direction bookkeeping around it runs as the
+fused zs_muonmd_pre / zs_muonmd_post passes (f32), and the optimizers batch
+the Newton-Schulz launches of same-shape matrices across parameters.  No step
+has host syncs, so a whole step can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
@@ -40,6 +42,8 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int) -> torch.Tensor:
     if (mp, np_) != (m, n):
         Xc = torch.nn.functional.pad(Xc, (0, np_ - n, 0, mp - m))
     Xc = Xc.contiguous()
+    if Xc.data_ptr() % 16:
+        Xc = Xc.clone()
     batch = Xc.size(0)
     out = torch.empty_like(Xc)
     ws = torch.empty(int(Z.lib().zs_newton_schulz5_workspace(batch, mp, np_, Z.ZS_BF16)), dtype=torch.uint8,
@@ -138,47 +142,147 @@ def _init_md_state(state, W, gain_mode, norm_axis, capturable):
     state["target_norm"] = _direction_norm(W, norm_axis)
 
 
+def _flat3(t, m, n):
+    return t.reshape(-1, m, n)
+
+
+def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
+    """Fused first half of the MD step: returns (W f32, gain reductions, X bf16 [..., m, n]).
+
+    W = p (f32 view or copy); buf.lerp_(g*G, 1-momentum); X = lerp(g*G, buf, momentum) in
+    bf16 (the Newton-Schulz input); the gain gradients' reductions of (W/g)*G from the old gains."""
+    W = p if p.dtype == torch.float32 else p.float()
+    G = grad if grad.dtype == torch.float32 else grad.float()
+    W, G = W.contiguous(), G.contiguous()
+    m, n = W.shape[-2], W.shape[-1]
+    if len(state) == 0:
+        _init_md_state(state, W, gain_mode, norm_axis, capturable)
+    L = W.numel() // (m * n)
+    X = torch.empty(W.shape, dtype=torch.bfloat16, device=W.device)
+    red = {k: torch.zeros_like(state[k]) for k in ("g_scalar", "g_row", "g_col") if k in state}
+    buf = state["momentum_buffer"]
+    Z.count(1)
+    Z.check(Z.lib().zs_muonmd_pre(W.data_ptr(), G.data_ptr(), buf.data_ptr(),
+                                  Z.ptr(state.get("g_scalar")), Z.ptr(state.get("g_row")), Z.ptr(state.get("g_col")),
+                                  X.data_ptr(), Z.ptr(red.get("g_scalar")), Z.ptr(red.get("g_row")),
+                                  Z.ptr(red.get("g_col")), L, m, n, float(momentum), Z.stream_of(W)), "zs_muonmd_pre")
+    return W, red, X
+
+
+_AXIS = {"frobenius": 0, "row": 1, "col": 2}
+
+
+def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axis, rescale_mode):
+    """Fused second half: W_hat' = W/g - lr*rescale*U projected onto the sphere, gain Adam
+    steps from the old gains, p = g_new * W_hat' in p's dtype."""
+    if norm_axis not in _AXIS:
+        raise ValueError(f"unknown norm_axis {norm_axis!r}")
+    m, n = W.shape[-2], W.shape[-1]
+    L = W.numel() // (m * n)
+    rescale = (max(1.0, m / n) ** 0.5) if rescale_mode == "muon" else (max(m, n) / min(m, n)) ** 0.5
+    if red:
+        state["gain_step"] += 1
+    step = state["gain_step"]
+    step_dev = step if torch.is_tensor(step) else None
+    if step_dev is not None and step_dev.dtype != torch.float32:
+        raise Z.ZsError("gain_step must be a float32 device scalar")
+    lr_dev = lr if torch.is_tensor(lr) else None
+    if lr_dev is not None:
+        lr_dev = lr_dev.to(device=W.device, dtype=torch.float32)
+    U = U.contiguous()
+    target = state["target_norm"].contiguous()
+    direct = p.is_contiguous() and p.dtype in (torch.float32, torch.bfloat16)
+    out = p if direct else W
+    ws = torch.empty(int(Z.lib().zs_muonmd_post_workspace(L, m, n)), dtype=torch.uint8, device=W.device)
+    g = lambda k: state.get(k)  # noqa: E731
+    Z.count(3)
+    Z.check(Z.lib().zs_muonmd_post(
+        W.data_ptr(), U.data_ptr(), out.data_ptr(), Z.dtype_code(out.dtype),
+        Z.ptr(g("g_scalar")), Z.ptr(g("g_row")), Z.ptr(g("g_col")),
+        Z.ptr(g("g_scalar_m1")), Z.ptr(g("g_scalar_m2")), Z.ptr(g("g_row_m1")), Z.ptr(g("g_row_m2")),
+        Z.ptr(g("g_col_m1")), Z.ptr(g("g_col_m2")),
+        Z.ptr(red.get("g_scalar")), Z.ptr(red.get("g_row")), Z.ptr(red.get("g_col")),
+        Z.ptr(step_dev), float(step) if step_dev is None else 0.0, float(gain_betas[0]), float(gain_betas[1]),
+        float(gain_eps), float(gain_lr), Z.ptr(lr_dev), 0.0 if lr_dev is not None else float(lr), float(rescale),
+        _AXIS[norm_axis], target.data_ptr(), L, m, n, ws.data_ptr(), ws.numel(), Z.stream_of(W)), "zs_muonmd_post")
+    if not direct:
+        p.copy_(W.to(p.dtype))
+
+
+def _zeropower_many(Xs, steps):
+    """zeropower_via_newtonschulz5 of every tensor in Xs; matrices of one oriented shape
+    (and step count) from different tensors share batched launches."""
+    out = [None] * len(Xs)
+    groups = {}
+    for i, (X, st) in enumerate(zip(Xs, steps)):
+        m, n = X.shape[-2], X.shape[-1]
+        groups.setdefault((min(m, n), max(m, n), int(st)), []).append(i)
+    for (mm, nn, st), idx in groups.items():
+        chunk, batch = [], 0
+
+        def flush(chunk):
+            if not chunk:
+                return
+            parts = []
+            for i in chunk:
+                X = Xs[i]
+                Xo = X.mT if X.shape[-2] > X.shape[-1] else X
+                parts.append(Xo.reshape(-1, mm, nn))
+            stack = parts[0] if len(parts) == 1 else torch.cat(parts, 0)
+            Y = zeropower_via_newtonschulz5(stack, st)
+            off = 0
+            for i, part in zip(chunk, parts):
+                X = Xs[i]
+                b = part.shape[0]
+                tall = X.shape[-2] > X.shape[-1]
+                y = Y[off:off + b]
+                off += b
+                y = y.reshape(X.mT.shape if tall else X.shape)
+                out[i] = y.mT if tall else y
+
+        for i in idx:
+            b = Xs[i].numel() // (mm * nn)
+            # a stack of 32+ matrices fills the GPU on its own; small ones are merged up to
+            # 64 matrices (and about 1 GiB of Newton-Schulz workspace) per launch
+            if b >= 32:
+                flush([i])
+                continue
+            if chunk and (batch + b > 64 or (batch + b) * mm * (2 * mm + nn) * 2 > (1 << 30)):
+                flush(chunk)
+                chunk, batch = [], 0
+            chunk.append(i)
+            batch += b
+        flush(chunk)
+    return out
+
+
 @torch.no_grad()
 def md_decoupled_step(p, grad, state, *, lr, momentum, gain_lr, gain_betas, gain_eps, gain_mode, norm_axis,
                       ns_steps, capturable=False, rescale_mode="balanced"):
     """One magnitude/direction-decoupled Muon step on p (a matrix or a stack of
-    matrices over leading dims), in place; f32 bookkeeping, p's dtype on write."""
-    W = p.float()
-    G = grad.float()
-    m, n = W.shape[-2], W.shape[-1]
-    if len(state) == 0:
-        _init_md_state(state, W, gain_mode, norm_axis, capturable)
-    sc, rw, cl = _softplus_gains(state)
-    g = _gain_product((sc, rw, cl))
-    W_hat = W if g is None else W / g
-    G_hat = G if g is None else g * G
-    buf = state["momentum_buffer"]
-    buf.lerp_(G_hat, 1 - momentum)
-    update = zeropower_via_newtonschulz5(G_hat.lerp(buf, momentum), steps=ns_steps).float()
-    update.mul_((max(1.0, m / n) ** 0.5) if rescale_mode == "muon" else (max(m, n) / min(m, n)) ** 0.5)
-    W_hat = _project_to_sphere(W_hat - lr * update, state["target_norm"], norm_axis)
-    if g is not None:
-        # gain gradients from the old gains: reduce (W_hat_old * G) times the
-        # other gains over the axes each gain does not span, through softplus
-        WG = (W / g) * G
-        state["gain_step"] += 1
-        step = state["gain_step"]
-        grads = {}
-        if sc is not None:
-            grads["g_scalar"] = (WG * _gain_product((rw, cl)) if (rw is not None or cl is not None) else WG).sum(
-                dim=(-2, -1)) * torch.sigmoid(state["g_scalar"])
-        if rw is not None:
-            other = _gain_product((cl, sc))
-            grads["g_row"] = (WG * other if other is not None else WG).sum(dim=-1) * torch.sigmoid(state["g_row"])
-        if cl is not None:
-            other = _gain_product((rw, sc))
-            grads["g_col"] = (WG * other if other is not None else WG).sum(dim=-2) * torch.sigmoid(state["g_col"])
-        for key in ("g_scalar", "g_row", "g_col"):
-            if key in grads:
-                upd = adam_update(grads[key], state[key + "_m1"], state[key + "_m2"], step, gain_betas, gain_eps)
-                _scaled_add_(state[key], upd, gain_lr)
-    g_new = _effective_gain(state)
-    p.copy_((W_hat if g_new is None else g_new * W_hat).to(p.dtype))
+    matrices over leading dims), in place; f32 bookkeeping, p's dtype on write.
+    Three fused passes (libzs.so) around the tensor-core Newton-Schulz."""
+    Z.require_cuda(p, grad)
+    W, red, X = _md_pre(p, grad, state, momentum=momentum, gain_mode=gain_mode, norm_axis=norm_axis,
+                        capturable=capturable)
+    U = zeropower_via_newtonschulz5(X, steps=ns_steps)
+    _md_post(p, W, red, U, state, lr=lr, gain_lr=gain_lr, gain_betas=gain_betas, gain_eps=gain_eps,
+             norm_axis=norm_axis, rescale_mode=rescale_mode)
+
+
+def md_decoupled_steps(jobs, states):
+    """md_decoupled_step for many parameters at once: jobs = [(p, hyper-parameter dict)].
+    Same result per parameter; the Newton-Schulz launches are shared across parameters
+    whose matrices have the same shape."""
+    pre = []
+    for p, hp in jobs:
+        Z.require_cuda(p, p.grad)
+        pre.append(_md_pre(p, p.grad, states[p], momentum=hp["momentum"], gain_mode=hp["gain_mode"],
+                           norm_axis=hp["norm_axis"], capturable=hp["capturable"]))
+    Us = _zeropower_many([x for _, _, x in pre], [hp["ns_steps"] for _, hp in jobs])
+    for (p, hp), (W, red, _), U in zip(jobs, pre, Us):
+        _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
+                 gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"])
 
 
 _MD_KEYS = {"params", "lr", "momentum", "gain_lr", "gain_betas", "gain_eps", "gain_mode", "norm_axis", "ns_steps",
@@ -198,12 +302,14 @@ class SingleDeviceMuonMD(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        jobs = []
         for group in self.param_groups:
             for p in group["params"]:
                 if p.grad is None:
                     continue
                 assert p.ndim >= 2, "MD decoupling needs a matrix or a stack of matrices (>=2D)"
-                md_decoupled_step(p, p.grad, self.state[p], **{k: group[k] for k in _MD_KEYS if k != "params"})
+                jobs.append((p, group))
+        md_decoupled_steps(jobs, self.state)
         return loss
 
 
@@ -231,12 +337,11 @@ class SingleDeviceMuonMDWithAuxAdam(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        md_decoupled_steps([(p, group) for group in self.param_groups if group["use_muon"]
+                            for p in group["params"] if p.grad is not None], self.state)
         for group in self.param_groups:
             for p in group["params"]:
-                if p.grad is None:
-                    continue
-                if group["use_muon"]:
-                    md_decoupled_step(p, p.grad, self.state[p], **{k: group[k] for k in _MD_KEYS if k != "params"})
+                if p.grad is None or group["use_muon"]:
                     continue
                 state = self.state[p]
                 if len(state) == 0:

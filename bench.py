@@ -452,7 +452,7 @@ def config4_model_config(layers=16):
     return ModelConfig(vocab_size=65536, embed_size=1536, hidden_size=1536, transformer_depth=layers,
                        intermediate_size=768, n_experts=65, n_shared_experts=1, n_experts_per_token=6,
                        n_attention_heads=12, n_key_value_heads=4, attention_window_pattern=(None,) * layers,
-                       max_position_embeddings=4096, sequence_length=4096)
+                       max_position_embeddings=4096, sequence_length=4096, attention_sink=True)
 
 
 def model_flops_per_token(cfg, seq_len):
@@ -559,7 +559,7 @@ def run_config4(args):
                 "warmup": max(args.warmup, 5), "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": f"config4: MoE LM L={cfg.transformer_depth} d=1536 H=12/4 hd=128 E=64+1 "
-                                       f"ffn=768 top-6 V=65536, seq 4096 x micro-batch {B}, full step incl. "
+                                       f"ffn=768 top-6 V=65536, gated sink attention, seq 4096 x micro-batch {B}, full step incl. "
                                        "MuonMD/AdamW/sparse-embedding optimizer",
                            "parallelism": f"dp{world}", "model_gflop_per_token": fpt / 1e9, "mfu": mfu,
                            "loss": float(loss.item())},

@@ -365,6 +365,42 @@ size_t zs_newton_schulz5_workspace(int64_t batch, int64_t m, int64_t n, int dtyp
 int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int64_t n, int steps, float a, float b,
                       float c, void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
+/* ------------------------------------------------ MuonMD step (a23, a24) */
+
+/*
+ * md_decoupled_step (optimizer/muon.py:398-508) around the Newton-Schulz call,
+ * for one weight stack W [L, m, n] (f32, contiguous) with gradient G and
+ * momentum buffer buf (f32, same layout) and raw gains g_scalar [L], g_row
+ * [L, m], g_col [L, n] (f32, each NULL when the gain mode lacks it; the
+ * effective gain is softplus(scalar) * softplus(row) * softplus(col)).
+ *
+ * zs_muonmd_pre:  buf = lerp(buf, g*G, 1 - momentum);
+ *                 x_out (bf16 [L, m, n]) = lerp(g*G, buf, momentum);
+ *                 red_* += the gain-gradient reductions of (W/g)*G times the
+ *                 other gains over the axes each gain does not span (red_*
+ *                 f32, same shapes as the gains, zeroed by the caller; NULL
+ *                 exactly where the gain is NULL).
+ * zs_muonmd_post: with U the orthogonalised update (bf16 [L, m, n]):
+ *                 W' = W/g - lr * rescale * U, projected to target_norm
+ *                 per matrix (norm_axis 0, target [L]), row (1, [L, m]) or
+ *                 column (2, [L, n]); gain Adam (betas b1, b2, eps, step from
+ *                 step_dev (f32 device scalar, already incremented) or
+ *                 step_host) on dL/draw = red * sigmoid(raw), raw -= gain_lr
+ *                 * update; p_out (f32 or bf16 by p_dtype, may alias W) =
+ *                 g_new * W'.  lr from lr_dev (f32 device scalar) or lr_host.
+ *                 Workspace: zs_muonmd_post_workspace bytes.
+ */
+int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
+                  const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col, int64_t L,
+                  int64_t m, int64_t n, float momentum, void* stream);
+size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n);
+int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
+                   float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row, float* m1_col,
+                   float* m2_col, const float* red_scalar, const float* red_row, const float* red_col,
+                   const float* step_dev, float step_host, float b1, float b2, float eps, float gain_lr,
+                   const float* lr_dev, float lr_host, float rescale, int norm_axis, const float* target_norm,
+                   int64_t L, int64_t m, int64_t n, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,3 +75,163 @@ def test_md_decoupled_step_reference_fixture(golden, case, gain_mode, norm_axis,
     for key in ("g_scalar", "g_row", "g_col"):
         if key in gd:
             assert rel_err(state[key], gd[key]) < 1e-3
+
+
+def _torch_md_step(p, grad, state, *, lr, momentum, gain_lr, gain_betas, gain_eps, gain_mode, norm_axis, ns_steps,
+                   capturable=False, rescale_mode="balanced", U=None, X_fused=None):
+    """optimizer/muon.py:398-508 restated with torch f32 ops on the GPU.  With U given, that
+    orthogonalised update replaces the Newton-Schulz call (so both sides share it); with
+    X_fused given, the restatement's own Newton-Schulz input is checked against it."""
+    import torch.nn.functional as F
+    from optimizer.muon import _direction_norm, _init_md_state, zeropower_via_newtonschulz5
+
+    def eff(st):
+        g = None
+        if "g_scalar" in st:
+            gs = F.softplus(st["g_scalar"])
+            g = gs.reshape(gs.shape + (1, 1))
+        if "g_row" in st:
+            gr = F.softplus(st["g_row"]).unsqueeze(-1)
+            g = gr if g is None else g * gr
+        if "g_col" in st:
+            gc = F.softplus(st["g_col"]).unsqueeze(-2)
+            g = gc if g is None else g * gc
+        return g
+
+    def adam(grad, b1, b2, step):
+        b1.lerp_(grad, 1 - gain_betas[0])
+        b2.lerp_(grad.square(), 1 - gain_betas[1])
+        return (b1 / (1 - gain_betas[0] ** step)) / ((b2 / (1 - gain_betas[1] ** step)).sqrt() + gain_eps)
+
+    W, G = p.float(), grad.float()
+    m, n = W.shape[-2:]
+    if len(state) == 0:
+        _init_md_state(state, W, gain_mode, norm_axis, capturable)
+    g = eff(state)
+    W_hat = W if g is None else W / g
+    G_hat = G if g is None else g * G
+    WG = None if g is None else W_hat * G
+    buf = state["momentum_buffer"]
+    buf.lerp_(G_hat, 1 - momentum)
+    X = G_hat.lerp(buf, momentum).bfloat16()
+    if X_fused is not None:
+        # f32 lerps that differ in the last bit (fma contraction) round a few values to the
+        # neighbouring bf16 (at most 1e-3 of them); the lerp subtracts values of the
+        # momentum's size, so near-zero results carry an absolute f32 error on top
+        diff = (X.float() - X_fused.float()).abs()
+        assert (X != X_fused).float().mean().item() < 1e-3
+        assert (diff <= X.float().abs() * 2 ** -7 + 1e-6 * X.float().abs().max()).all()
+    upd = (zeropower_via_newtonschulz5(X, steps=ns_steps) if U is None else U).float()
+    upd.mul_((max(1.0, m / n) ** 0.5) if rescale_mode == "muon" else (max(m, n) / min(m, n)) ** 0.5)
+    W_hat = W_hat - lr * upd
+    W_hat = W_hat * (state["target_norm"] / (_direction_norm(W_hat, norm_axis) + 1e-12))
+    if g is not None:
+        state["gain_step"] += 1
+        step = state["gain_step"]
+        sp = {k: F.softplus(state[k]) for k in ("g_scalar", "g_row", "g_col") if k in state}
+        sb = {"g_scalar": (lambda t: t.reshape(t.shape + (1, 1))), "g_row": (lambda t: t.unsqueeze(-1)),
+              "g_col": (lambda t: t.unsqueeze(-2))}
+        grads = {}
+        for key, dims in (("g_scalar", (-2, -1)), ("g_row", -1), ("g_col", -2)):
+            if key in state:
+                red = WG
+                for other in ("g_row", "g_col", "g_scalar"):
+                    if other != key and other in sp:
+                        red = red * sb[other](sp[other])
+                grads[key] = red.sum(dim=dims) * torch.sigmoid(state[key])
+        for key, gr in grads.items():
+            u = adam(gr, state[key + "_m1"], state[key + "_m2"], step)
+            state[key].add_(u, alpha=-gain_lr)
+    g_new = eff(state)
+    p.copy_((W_hat if g_new is None else g_new * W_hat).to(p.dtype))
+
+
+MD_SHAPES = [(64, 256, 512), (1536, 1536), (12, 1536), (5, 37, 20), (3, 96, 40), (200, 72)]
+
+
+@pytest.mark.parametrize("shape", MD_SHAPES)
+@pytest.mark.parametrize("gain_mode,norm_axis,rescale", [("both", "frobenius", "balanced"), ("col", "row", "muon"),
+                                                         ("scalar", "col", "balanced"), ("row", "row", "balanced"),
+                                                         ("none", "frobenius", "muon")])
+def test_fused_md_step_matches_torch_formula(shape, gain_mode, norm_axis, rescale):
+    from optimizer.muon import _md_post, _md_pre, zeropower_via_newtonschulz5
+
+    gen = torch.Generator(device="cuda").manual_seed(len(shape) * 1000 + shape[-1])
+    W0 = torch.randn(*shape, device="cuda", generator=gen) * 0.05
+    grads = [torch.randn(*shape, device="cuda", generator=gen) for _ in range(3)]
+    pa, pb = W0.clone(), W0.clone()
+    sa, sb = {}, {}
+    lr = torch.tensor(0.02, device="cuda")
+    kw = dict(lr=lr, momentum=0.95, gain_lr=1e-2, gain_betas=(0.9, 0.95), gain_eps=1e-10, gain_mode=gain_mode,
+              norm_axis=norm_axis, ns_steps=5, capturable=True, rescale_mode=rescale)
+    # The bf16 Newton-Schulz amplifies a one-ulp change of a few inputs to ~0.5 % of its
+    # output, so both sides share the fused path's orthogonalised update; the
+    # restatement's own input is checked against the fused one.  What remains differs by
+    # f32 rounding and reduction order only.
+    for gr in grads:
+        W, red, X = _md_pre(pa, gr, sa, momentum=0.95, gain_mode=gain_mode, norm_axis=norm_axis, capturable=True)
+        U = zeropower_via_newtonschulz5(X, 5)
+        _md_post(pa, W, red, U, sa, lr=lr, gain_lr=1e-2, gain_betas=(0.9, 0.95), gain_eps=1e-10,
+                 norm_axis=norm_axis, rescale_mode=rescale)
+        _torch_md_step(pb, gr, sb, U=U, X_fused=X, **kw)
+        torch.cuda.synchronize()
+        assert rel_err(pa, pb) < 2e-6
+    assert rel_err(sa["momentum_buffer"], sb["momentum_buffer"]) < 1e-6
+    for key in ("g_scalar", "g_row", "g_col", "g_scalar_m1", "g_row_m2", "g_col_m1"):
+        if key in sb:
+            assert rel_err(sa[key], sb[key]) < 1e-5, key
+    assert float(sa["gain_step"]) == float(sb["gain_step"]) == (0.0 if gain_mode == "none" else 3.0)
+
+
+def test_fused_md_step_bf16_param_and_float_lr():
+    from optimizer.muon import _md_post, _md_pre, md_decoupled_step, zeropower_via_newtonschulz5
+
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    W0 = (torch.randn(4, 64, 128, device="cuda", generator=gen) * 0.05).bfloat16()
+    pa, pb = W0.clone(), W0.clone()
+    sa, sb = {}, {}
+    kw = dict(lr=0.01, momentum=0.9, gain_lr=1e-3, gain_betas=(0.9, 0.95), gain_eps=1e-10, gain_mode="both",
+              norm_axis="frobenius", ns_steps=5, capturable=False, rescale_mode="balanced")
+    for _ in range(2):
+        gr = torch.randn(4, 64, 128, device="cuda", generator=gen).bfloat16()
+        W, red, X = _md_pre(pa, gr, sa, momentum=0.9, gain_mode="both", norm_axis="frobenius", capturable=False)
+        U = zeropower_via_newtonschulz5(X, 5)
+        _md_post(pa, W, red, U, sa, lr=0.01, gain_lr=1e-3, gain_betas=(0.9, 0.95), gain_eps=1e-10,
+                 norm_axis="frobenius", rescale_mode="balanced")
+        _torch_md_step(pb, gr, sb, U=U, **kw)
+        # p is stored in bf16 on both sides: agreement to a bf16 rounding of the update
+        assert rel_err(pa, pb) < 2e-3
+    assert pa.dtype == torch.bfloat16 and sa["gain_step"] == sb["gain_step"] == 2
+    md_decoupled_step(pa, gr, sa, **kw)
+    assert sa["gain_step"] == 3
+
+
+def test_batched_optimizer_matches_per_parameter_steps():
+    """SingleDeviceMuonMDWithAuxAdam batches Newton-Schulz across same-shape matrices;
+    the result equals stepping each parameter alone."""
+    from optimizer.muon import SingleDeviceMuonMDWithAuxAdam, md_decoupled_step
+
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    shapes = [(256, 512), (256, 512), (512, 256), (4, 256, 512), (64, 512), (12, 128), (12, 128), (40, 33)]
+    ps = [torch.nn.Parameter(torch.randn(*s, device="cuda", generator=gen) * 0.05) for s in shapes]
+    ref = [p.detach().clone() for p in ps]
+    lr = torch.tensor(0.02, device="cuda")
+    opt = SingleDeviceMuonMDWithAuxAdam([
+        dict(params=ps[:6], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, capturable=True),
+        dict(params=ps[6:], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, norm_axis="row", gain_mode="col",
+             rescale_mode="muon", capturable=True)])
+    states = [{} for _ in ps]
+    for _ in range(2):
+        gs = [torch.randn(*s, device="cuda", generator=gen) for s in shapes]
+        for p, g in zip(ps, gs):
+            p.grad = g
+        opt.step()
+        for i, (r, g) in enumerate(zip(ref, gs)):
+            group = opt.param_groups[0] if i < 6 else opt.param_groups[1]
+            md_decoupled_step(r, g, states[i], lr=lr, momentum=0.95, gain_lr=1e-3, gain_betas=group["gain_betas"],
+                              gain_eps=group["gain_eps"], gain_mode=group["gain_mode"], norm_axis=group["norm_axis"],
+                              ns_steps=5, capturable=True, rescale_mode=group["rescale_mode"])
+    # same kernels, same inputs, Newton-Schulz per matrix independent of the batching (its
+    # norm is reduced in a fixed order): equal up to the gain reductions' atomic order
+    for p, r in zip(ps, ref):
+        assert rel_err(p.detach(), r) < 1e-6
