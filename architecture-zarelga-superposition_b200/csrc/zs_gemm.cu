@@ -1063,18 +1063,15 @@ int launch_colsum_per_expert(void* Db, int64_t db_se, int64_t db_sn, const void*
                              int num_experts, const int64_t* expert_offsets, int dtype, cudaStream_t stream);
 }
 
-extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db,
-                            int64_t db_se, int64_t db_sn, const void* DY, int64_t dy_sm, const void* X, int64_t x_sm,
-                            int64_t n, int64_t K, int64_t N, const int64_t* expert_offsets, int dtype,
-                            void* stream_) {
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  ZS_REQUIRE(DW && DY && X && expert_offsets, ZS_ERR_ARG);
-  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
-  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
-  ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0, ZS_ERR_SHAPE);
-  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
-  ZS_BIND(DY);
+namespace zs {
+// DW[e] = X_e^T DY_e for every expert; EPI_STORE writes the input dtype,
+// EPI_F32 writes (or with accumulate adds into) f32.
+template <int EPI>
+static int group_xty_impl(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, const void* DY,
+                          int64_t dy_sm, const void* X, int64_t x_sm, int64_t n, int64_t K, int64_t N,
+                          const int64_t* expert_offsets, int dtype, int accumulate, cudaStream_t stream) {
   const int es = elem_size(dtype);
+  const int oes = EPI == EPI_F32 ? 4 : es;
   constexpr int BN = 256;
 
   // Orientation: GEMM rows m run along the stride-1 side when possible so the
@@ -1110,8 +1107,9 @@ extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw
   a.ldo_n = 1;
   a.out_se = dw_se;
   a.out_dtype = dtype;
-  a.vec_ok = ((reinterpret_cast<uintptr_t>(DW) & 15) == 0) && ((a.ldo_m * es) % 16 == 0) &&
-             ((dw_se * es) % 16 == 0);
+  a.accumulate = accumulate;
+  a.vec_ok = ((reinterpret_cast<uintptr_t>(DW) & 15) == 0) && ((a.ldo_m * oes) % 16 == 0) &&
+             ((dw_se * oes) % 16 == 0);
 
   const int64_t max_tiles = (int64_t)num_experts * a.m_tiles_xty * a.n_tiles;
   if (n == 0) {
@@ -1124,11 +1122,41 @@ extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw
   if (rc != ZS_OK) return rc;
   rc = make_tmap(&tmB, Bop, dtype, (uint64_t)Next, (uint64_t)n, (uint64_t)b_sm * es, 64, 64);
   if (rc != ZS_OK) return rc;
-  rc = launch_gemm<BN, 4, true, true, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
+  return launch_gemm<BN, 4, true, true, EPI>(tmA, tmB, a, max_tiles, stream);
+}
+}  // namespace zs
+
+extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db,
+                            int64_t db_se, int64_t db_sn, const void* DY, int64_t dy_sm, const void* X, int64_t x_sm,
+                            int64_t n, int64_t K, int64_t N, const int64_t* expert_offsets, int dtype,
+                            void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(DW && DY && X && expert_offsets, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
+  ZS_BIND(DY);
+  int rc = group_xty_impl<EPI_STORE>(num_experts, DW, dw_se, dw_sk, dw_sn, DY, dy_sm, X, x_sm, n, K, N,
+                                     expert_offsets, dtype, 0, stream);
   if (rc != ZS_OK) return rc;
   if (Db != nullptr)
     rc = launch_colsum_per_expert(Db, db_se, db_sn, DY, dy_sm, N, num_experts, expert_offsets, dtype, stream);
   return rc;
+}
+
+extern "C" int zs_group_xty_f32(int num_experts, float* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn,
+                                const void* DY, int64_t dy_sm, const void* X, int64_t x_sm, int64_t n, int64_t K,
+                                int64_t N, const int64_t* expert_offsets, int dtype, int accumulate, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(DW && DY && X && expert_offsets, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(num_experts >= 1 && num_experts <= MAX_EXPERTS_GEMM, ZS_ERR_SHAPE);
+  ZS_REQUIRE(K >= 1 && N >= 1 && n >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(n < (int64_t)1 << 30 && K < (int64_t)1 << 24 && N < (int64_t)1 << 24, ZS_ERR_SHAPE);
+  ZS_BIND(DY);
+  return group_xty_impl<EPI_F32>(num_experts, DW, dw_se, dw_sk, dw_sn, DY, dy_sm, X, x_sm, n, K, N, expert_offsets,
+                                 dtype, accumulate != 0, stream);
 }
 
 extern "C" int zs_expert_up_swiglu(void* act, void* hfull, const void* W1, int64_t num_experts, int64_t K, int64_t F,

@@ -74,6 +74,112 @@ __global__ void zrmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restric
   for (int c = threadIdx.x; c < d; c += blockDim.x) dw_part[(int64_t)blockIdx.x * d + c] = sdw[c];
 }
 
+// Vectorised backward for rows of d = 128 * NV elements: lane holds NV chunks
+// of 4 consecutive columns (x, dy and the dw accumulators in registers); the
+// block's 8 warps reduce their dw through shared memory without atomics.
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  using type = float4;
+  __device__ static void unpack(const float4& v, float (&o)[4]) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
+  __device__ static float4 pack(const float (&o)[4]) { return make_float4(o[0], o[1], o[2], o[3]); }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  using type = uint2;
+  __device__ static void unpack(const uint2& v, float (&o)[4]) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+  __device__ static uint2 pack(const float (&o)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+};
+template <>
+struct Vec4<__half> {
+  using type = uint2;
+  __device__ static void unpack(const uint2& v, float (&o)[4]) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+  __device__ static uint2 pack(const float (&o)[4]) {
+    __half2 a = __floats2half2_rn(o[0], o[1]), b = __floats2half2_rn(o[2], o[3]);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+};
+
+template <typename T, typename W, int NV>
+__global__ void __launch_bounds__(256) zrmsnorm_bwd_vec_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                               const W* __restrict__ w, const float* __restrict__ rstd,
+                                                               T* __restrict__ dx, float* __restrict__ dw_part,
+                                                               int64_t rows) {
+  constexpr int D = 128 * NV;
+  using V = Vec4<T>;
+  using VT = typename V::type;
+  extern __shared__ float sdw[];  // [8][D] per-warp dw, then [D] of (1 + w)
+  float* swp = sdw + 8 * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) swp[c] = 1.0f + to_f32<W>(w[c]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[j][v] = 0.f;
+  const int64_t warps = (int64_t)gridDim.x * 8;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += warps) {
+    const VT* xr = reinterpret_cast<const VT*>(x + r * D);
+    const VT* gr = reinterpret_cast<const VT*>(dy + r * D);
+    const float rs = __ldg(rstd + r);
+    float xv[NV][4], gv[NV][4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      V::unpack(xr[j * 32 + lane], xv[j]);
+      V::unpack(gr[j * 32 + lane], gv[j]);
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int c = (j * 32 + lane) * 4 + v;
+        const float n = xv[j][v] * rs;
+        dot = fmaf(gv[j][v] * swp[c], n, dot);
+        acc[j][v] = fmaf(gv[j][v], n, acc[j][v]);
+      }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / (float)D;
+    VT* dxr = reinterpret_cast<VT*>(dx + r * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      float o[4];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int c = (j * 32 + lane) * 4 + v;
+        const float n = xv[j][v] * rs;
+        o[v] = rs * (gv[j][v] * swp[c] - n * mean);
+      }
+      dxr[j * 32 + lane] = V::pack(o);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) sdw[warp * D + (j * 32 + lane) * 4 + v] = acc[j][v];
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t += sdw[q * D + c];
+    dw_part[(int64_t)blockIdx.x * D + c] = t;
+  }
+}
+
 __global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int d, float* __restrict__ out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
@@ -165,6 +271,39 @@ extern "C" int zs_zrmsnorm_backward(const void* dy, const void* x, const void* w
   if (blocks > 296) blocks = 296;
   if (blocks < 1) blocks = 1;
   float* part = reinterpret_cast<float*>(workspace);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) |
+                         reinterpret_cast<uintptr_t>(dx)) & 15) == 0;
+  const int nv = d % 128 == 0 ? d / 128 : 0;
+  if (aligned && (nv == 1 || nv == 2 || nv == 3 || nv == 4 || nv == 6 || nv == 8 || nv == 12 || nv == 16)) {
+    const size_t shv = (size_t)9 * d * sizeof(float);
+    int rc = ZS_OK;
+#define ZS_NORM_BWD_VEC(NVC)                                                                                   \
+  ZS_DISPATCH_XW(x_dtype, w_dtype, {                                                                           \
+    if (shv > 48 * 1024) {                                                                                     \
+      ZS_CUDA_TRY(cudaFuncSetAttribute(zrmsnorm_bwd_vec_kernel<TX, TW, NVC>,                                   \
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shv));                \
+    }                                                                                                          \
+    zrmsnorm_bwd_vec_kernel<TX, TW, NVC><<<(unsigned)blocks, 256, shv, stream>>>(                              \
+        reinterpret_cast<const TX*>(dy), reinterpret_cast<const TX*>(x), reinterpret_cast<const TW*>(weight), \
+        rstd, reinterpret_cast<TX*>(dx), part, rows);                                                          \
+  })
+    switch (nv) {
+      case 1: ZS_NORM_BWD_VEC(1); break;
+      case 2: ZS_NORM_BWD_VEC(2); break;
+      case 3: ZS_NORM_BWD_VEC(3); break;
+      case 4: ZS_NORM_BWD_VEC(4); break;
+      case 6: ZS_NORM_BWD_VEC(6); break;
+      case 8: ZS_NORM_BWD_VEC(8); break;
+      case 12: ZS_NORM_BWD_VEC(12); break;
+      default: ZS_NORM_BWD_VEC(16); break;
+    }
+#undef ZS_NORM_BWD_VEC
+    if (rc != ZS_OK) return rc;
+    ZS_CUDA_TRY(cudaGetLastError());
+    sum_rows_kernel<<<(d + 255) / 256, 256, 0, stream>>>(part, (int)blocks, d, dweight);
+    ZS_CUDA_TRY(cudaGetLastError());
+    return ZS_OK;
+  }
   const size_t sh = (size_t)d * sizeof(float);
   ZS_DISPATCH_XW(x_dtype, w_dtype, {
     if (sh > 48 * 1024) {

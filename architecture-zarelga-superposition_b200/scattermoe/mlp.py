@@ -78,9 +78,32 @@ def swiglu_backward(dact, hfull):
     return dh
 
 
+def accumulate_weight_grad(W, DY, X, offs, tag):
+    """W.grad (f32, W's [E, N, K] layout) += DY_e^T X_e per expert, straight from the GEMM
+    epilogue; W.grad is created (written, not added) when absent."""
+    E, N, K = W.shape
+    if W.grad is None:
+        W.grad = torch.empty_like(W, memory_format=torch.contiguous_format)
+        acc = 0
+    else:
+        acc = 1
+    g = W.grad
+    if g.dtype != torch.float32 or not g.is_contiguous() or g.is_sparse:
+        raise Z.ZsError("fused weight-gradient accumulation needs a dense contiguous f32 .grad")
+    Z.count(1)
+    with Z.timed(tag):
+        Z.check(Z.lib().zs_group_xty_f32(E, g.data_ptr(), N * K, 1, K, DY.data_ptr(), DY.stride(0), X.data_ptr(),
+                                         X.stride(0), X.size(0), K, N, offs.data_ptr(), Z.dtype_code(X.dtype), acc,
+                                         Z.stream_of(X)), "zs_group_xty_f32")
+
+
 class GLUExpertsFunction(torch.autograd.Function):
+    """Fused GLU experts.  With fuse_wgrad the f32 weights' gradients are accumulated into
+    W1.grad / W2.grad by the weight-gradient GEMMs themselves (and None is returned for them),
+    which skips the bf16 gradient, its cast and autograd's accumulation pass."""
+
     @staticmethod
-    def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k):
+    def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k, fuse_wgrad=False):
         Z.require_cuda(x, expert_p, expert_idxs, W1, W2)
         cdt = _compute_dtype(x)
         xc = x.to(cdt).contiguous()
@@ -97,6 +120,8 @@ class GLUExpertsFunction(torch.autograd.Function):
         y = weighted_row_sum(y_rows, pc, T, k)
         ctx.save_for_backward(xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c)
         ctx.meta = (x.dtype, expert_p.dtype, W1.dtype, W2.dtype, num_experts, k, T)
+        ctx.fused_params = ((W1, W2) if fuse_wgrad and W1.dtype == torch.float32 and W2.dtype == torch.float32
+                            and W1.is_leaf and W2.is_leaf else None)
         return y.to(x.dtype)
 
     @staticmethod
@@ -109,14 +134,22 @@ class GLUExpertsFunction(torch.autograd.Function):
         d_p = ops.rowwise_sum_product(y_rows.view(T, k, d), dyc, dtype=p_dt)
         dyg = ops.group(dyc, ssi, fan_out=k, coeff=pc.flatten())
         dhfull = down_dswiglu(dyg, W2c, hfull, sei, offs)
-        dW2, _ = ops.group_bwd_W(dyg, act, offs, E, tag="down_dw")   # [E, f, d] view of [E, d, f]
-        dW1, _ = ops.group_bwd_W(dhfull, xg, offs, E, tag="up_dw")   # [E, d, 2f] view of [E, 2f, d]
+        if ctx.fused_params is not None:
+            W1, W2 = ctx.fused_params
+            if ctx.needs_input_grad[4]:
+                accumulate_weight_grad(W2, dyg, act, offs, "down_dw")
+            if ctx.needs_input_grad[3]:
+                accumulate_weight_grad(W1, dhfull, xg, offs, "up_dw")
+            gW1 = gW2 = None
+        else:
+            dW2, _ = ops.group_bwd_W(dyg, act, offs, E, tag="down_dw")   # [E, f, d] view of [E, d, f]
+            dW1, _ = ops.group_bwd_W(dhfull, xg, offs, E, tag="up_dw")   # [E, d, 2f] view of [E, 2f, d]
+            gW1, gW2 = dW1.permute(0, 2, 1).to(w1_dt), dW2.permute(0, 2, 1).to(w2_dt)
         dx_rows = torch.empty((T * k, xg.size(1)), dtype=cdt, device=dy.device)
         ops._launch_scatter2scatter(dx_rows, W1c, dhfull, 1, sei, ssi, None, True, False, expert_offsets=offs,
                                     tag="up_dx")
         dx = weighted_row_sum(dx_rows, None, T, k)
-        return (dx.to(x_dt), d_p, None, dW1.permute(0, 2, 1).to(w1_dt), dW2.permute(0, 2, 1).to(w2_dt), None,
-                None)
+        return dx.to(x_dt), d_p, None, gW1, gW2, None, None, None
 
 
 class MLP(nn.Module):
@@ -153,6 +186,9 @@ class GLUMLP(nn.Module):
         self.output_experts = ParallelExperts(num_experts, hidden_size, input_size, bias=bias)
         self.top_k = min(top_k, self.num_experts)
         self.activation = activation
+        # When set, backward adds the f32 expert weight gradients into .grad directly (see
+        # GLUExpertsFunction); torch.autograd.grad then sees no gradient for these weights.
+        self.fuse_weight_grad = False
 
     def extra_repr(self):
         return "k={}".format(self.top_k)
@@ -166,7 +202,7 @@ class GLUMLP(nn.Module):
         if self._fused_ok():
             y = GLUExpertsFunction.apply(x, expert_p.reshape(x.size(0), -1), expert_idxs.reshape(x.size(0), -1),
                                          self.experts.weight, self.output_experts.weight, self.num_experts,
-                                         self.top_k)
+                                         self.top_k, self.fuse_weight_grad)
         else:
             sei, ssi, offs = flatten_sort_count(expert_idxs, num_experts=self.num_experts)
             h, gates = self.experts(x, self.top_k, sei, ssi, offs, grouped_out=True).chunk(2, dim=-1)

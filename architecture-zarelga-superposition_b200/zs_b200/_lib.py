@@ -41,6 +41,8 @@ _SIGNATURES = {
                                   _i64, _i32, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "zs_group_xty": (_i32, [_i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                             _vp, _i32, _vp]),
+    "zs_group_xty_f32": (_i32, [_i32, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
+                                _i32, _vp]),
     "zs_group": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp]),
     "zs_rowwise_sum_product": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
                                       _i64, _i64, _i64, _vp]),

@@ -47,6 +47,20 @@ def auxillary_loss_free_update(model, all_topk_indices, update_rate, attention_m
                                             Z.stream_of(counts)), "zs_bias_sign_update")
 
 
+def enable_fused_weight_grad(model, enabled=True):
+    """Let every GLUMLP in the model accumulate its f32 expert weight gradients into .grad
+    straight from the weight-gradient GEMMs (training loops that call loss.backward() and
+    read param.grad; not for torch.autograd.grad on those weights).  Returns the count."""
+    from scattermoe.mlp import GLUMLP
+
+    n = 0
+    for m in model.modules():
+        if isinstance(m, GLUMLP):
+            m.fuse_weight_grad = bool(enabled)
+            n += 1
+    return n
+
+
 def build_muonmd_optimizer(model, device, muon_lr=0.02, adam_lr=3e-4, momentum=0.95, gain_lr=1e-3,
                            adam_betas=(0.9, 0.95), adam_eps=1e-16, embedding_weight_decay=0.1, embedding_lr=3e-3,
                            embedding_beta=0.9, capture_warmup_steps=5, enable_cuda_graph=True):

@@ -478,7 +478,8 @@ def run_config4(args):
     from cut_cross_entropy import linear_cross_entropy
     from modeling.model import MoEModel
     from zs_b200 import _lib as Z
-    from zs_b200.train import auxillary_loss_free_update, build_muonmd_optimizer, build_next_token_loss_inputs
+    from zs_b200.train import (auxillary_loss_free_update, build_muonmd_optimizer, build_next_token_loss_inputs,
+                               enable_fused_weight_grad)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -490,6 +491,7 @@ def run_config4(args):
     cfg = config4_model_config(args.layers)
     torch.manual_seed(1234)
     model = MoEModel(cfg).to(dev)
+    enable_fused_weight_grad(model)
     opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3)
     B, S = args.micro_batch, 4096
     g = torch.Generator(device=dev).manual_seed(77 + rank)

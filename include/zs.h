@@ -182,6 +182,18 @@ int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_
                  int64_t N, const int64_t* expert_offsets, int dtype, void* stream);
 
 /*
+ * groupXtY with an f32 result written straight into a weight-gradient buffer:
+ * DW[e] = X_e^T DY_e (accumulate == 0) or DW[e] += X_e^T DY_e (accumulate != 0),
+ * DW f32 with the same addressing as zs_group_xty; X and DY in dtype.  This is
+ * the autograd step "dW (bf16) -> .to(f32) -> param.grad += dW" of the
+ * reference's ParallelLinear backward under autocast (parallel_experts.py:
+ * 106-120) in one pass, used when the caller accumulates into param.grad itself.
+ */
+int zs_group_xty_f32(int num_experts, float* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, const void* DY,
+                     int64_t dy_sm, const void* X, int64_t x_sm, int64_t n, int64_t K, int64_t N,
+                     const int64_t* expert_offsets, int dtype, int accumulate, void* stream);
+
+/*
  * group (scattermoe/kernels/ops.py:449-482, kernel :490-529):
  *   Y[i, :] = A[sorted_scattered_idxs[i] / fan_out, :] (* coeff[sorted_scattered_idxs[i]])
  * A: [n / fan_out, K] row stride a_sm; Y: [n, K] row stride y_sm; coeff may be NULL.

@@ -270,3 +270,36 @@ def test_up_swiglu_and_down_dswiglu_kernels(n_per, E, d, f):
     assert rel_err(dh, ref) < TOL
     from zs_b200 import device_error
     assert device_error() == 0
+
+
+@pytest.mark.parametrize("set_to_none", [True, False])
+def test_glumlp_fused_weight_grad_accumulation(set_to_none):
+    """fuse_weight_grad: the f32 expert grads come straight from the GEMM epilogue into .grad
+    (accumulated over two backward passes) and equal the unfused bf16-dW-then-cast path to
+    bf16 rounding of dW; the input and gate gradients are unchanged."""
+    from scattermoe.mlp import GLUMLP
+
+    torch.manual_seed(0)
+    T, d, E, k, f = 1000, 256, 16, 4, 192
+    ref = GLUMLP(d, f, E, k).cuda()
+    fus = GLUMLP(d, f, E, k).cuda()
+    fus.load_state_dict(ref.state_dict())
+    fus.fuse_weight_grad = True
+    x = torch.randn(T, d, device="cuda")
+    logits = torch.randn(T, E, device="cuda")
+    p, idx = torch.topk(torch.softmax(logits, -1), k)
+    for m in (ref, fus):
+        for prm in m.parameters():
+            prm.grad = None if set_to_none else torch.full_like(prm, 0.25)
+    outs = []
+    for m in (ref, fus):
+        xs, ps = x.clone().requires_grad_(True), p.clone().requires_grad_(True)
+        for rep in range(2):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = m(xs, ps, idx)
+            (y.float() * torch.linspace(-1, 1, d, device="cuda")).sum().backward()
+        outs.append((xs.grad, ps.grad))
+    for a, b in ((ref.experts.weight, fus.experts.weight), (ref.output_experts.weight, fus.output_experts.weight)):
+        assert b.grad.dtype == torch.float32
+        assert rel_err(b.grad, a.grad) < 5e-3 and cosine(b.grad, a.grad) > 0.99999
+    assert rel_err(outs[1][0], outs[0][0]) < 1e-6 and rel_err(outs[1][1], outs[0][1]) < 1e-6
