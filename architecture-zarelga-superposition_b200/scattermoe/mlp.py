@@ -79,28 +79,44 @@ def swiglu_backward(dact, hfull):
 
 
 def accumulate_weight_grad(W, DY, X, offs, tag):
-    """W.grad (f32, W's [E, N, K] layout) += DY_e^T X_e per expert, straight from the GEMM
-    epilogue; W.grad is created (written, not added) when absent."""
+    """W.grad (W's [E, N, K] layout) += DY_e^T X_e per expert, straight from the GEMM epilogue:
+    f32 weights accumulate in f32; 16-bit weights get their gradient written in their dtype
+    (added to an existing .grad).  W.grad is created when absent.  Data-parallel reducers
+    registered for W are told the gradient is complete (zs_b200.dp.notify_grad_ready)."""
+    from zs_b200.dp import notify_grad_ready
+
     E, N, K = W.shape
-    if W.grad is None:
-        W.grad = torch.empty_like(W, memory_format=torch.contiguous_format)
-        acc = 0
-    else:
-        acc = 1
     g = W.grad
-    if g.dtype != torch.float32 or not g.is_contiguous() or g.is_sparse:
-        raise Z.ZsError("fused weight-gradient accumulation needs a dense contiguous f32 .grad")
+    if g is not None and (g.dtype != W.dtype or not g.is_contiguous() or g.is_sparse):
+        raise Z.ZsError("fused weight-gradient accumulation needs a dense contiguous .grad of the weight's dtype")
     Z.count(1)
-    with Z.timed(tag):
-        Z.check(Z.lib().zs_group_xty_f32(E, g.data_ptr(), N * K, 1, K, DY.data_ptr(), DY.stride(0), X.data_ptr(),
-                                         X.stride(0), X.size(0), K, N, offs.data_ptr(), Z.dtype_code(X.dtype), acc,
-                                         Z.stream_of(X)), "zs_group_xty_f32")
+    if W.dtype == torch.float32:
+        acc = 1
+        if g is None:
+            g = W.grad = torch.empty_like(W, memory_format=torch.contiguous_format)
+            acc = 0
+        with Z.timed(tag):
+            Z.check(Z.lib().zs_group_xty_f32(E, g.data_ptr(), N * K, 1, K, DY.data_ptr(), DY.stride(0),
+                                             X.data_ptr(), X.stride(0), X.size(0), K, N, offs.data_ptr(),
+                                             Z.dtype_code(X.dtype), acc, Z.stream_of(X)), "zs_group_xty_f32")
+    else:
+        out = torch.empty_like(W, memory_format=torch.contiguous_format) if g is None else torch.empty_like(g)
+        with Z.timed(tag):
+            Z.check(Z.lib().zs_group_xty(E, out.data_ptr(), N * K, 1, K, None, 0, 0, DY.data_ptr(), DY.stride(0),
+                                         X.data_ptr(), X.stride(0), X.size(0), K, N, offs.data_ptr(),
+                                         Z.dtype_code(X.dtype), Z.stream_of(X)), "zs_group_xty")
+        if g is None:
+            W.grad = out
+        else:
+            g.add_(out)
+    notify_grad_ready(W)
 
 
 class GLUExpertsFunction(torch.autograd.Function):
-    """Fused GLU experts.  With fuse_wgrad the f32 weights' gradients are accumulated into
+    """Fused GLU experts.  With fuse_wgrad the weights' gradients are accumulated into
     W1.grad / W2.grad by the weight-gradient GEMMs themselves (and None is returned for them),
-    which skips the bf16 gradient, its cast and autograd's accumulation pass."""
+    which skips the bf16 gradient's permuted copy, its cast and autograd's accumulation pass,
+    and lets a data-parallel reducer start on each as soon as it is complete."""
 
     @staticmethod
     def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k, fuse_wgrad=False):
@@ -120,8 +136,7 @@ class GLUExpertsFunction(torch.autograd.Function):
         y = weighted_row_sum(y_rows, pc, T, k)
         ctx.save_for_backward(xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c)
         ctx.meta = (x.dtype, expert_p.dtype, W1.dtype, W2.dtype, num_experts, k, T)
-        ctx.fused_params = ((W1, W2) if fuse_wgrad and W1.dtype == torch.float32 and W2.dtype == torch.float32
-                            and W1.is_leaf and W2.is_leaf else None)
+        ctx.fused_params = (W1, W2) if fuse_wgrad and W1.is_leaf and W2.is_leaf else None
         return y.to(x.dtype)
 
     @staticmethod
@@ -135,11 +150,13 @@ class GLUExpertsFunction(torch.autograd.Function):
         dyg = ops.group(dyc, ssi, fan_out=k, coeff=pc.flatten())
         dhfull = down_dswiglu(dyg, W2c, hfull, sei, offs)
         if ctx.fused_params is not None:
+            # W1's gradient first: its data-parallel all-reduce (the larger one) then
+            # overlaps the two GEMMs that follow
             W1, W2 = ctx.fused_params
-            if ctx.needs_input_grad[4]:
-                accumulate_weight_grad(W2, dyg, act, offs, "down_dw")
             if ctx.needs_input_grad[3]:
                 accumulate_weight_grad(W1, dhfull, xg, offs, "up_dw")
+            if ctx.needs_input_grad[4]:
+                accumulate_weight_grad(W2, dyg, act, offs, "down_dw")
             gW1 = gW2 = None
         else:
             dW2, _ = ops.group_bwd_W(dyg, act, offs, E, tag="down_dw")   # [E, f, d] view of [E, d, f]

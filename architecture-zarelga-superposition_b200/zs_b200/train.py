@@ -40,7 +40,9 @@ def auxillary_loss_free_update(model, all_topk_indices, update_rate, attention_m
         Z.check(Z.lib().zs_expert_counts(t.data_ptr(), Z.ptr(valid), t.size(0), t.size(1), E, counts[i].data_ptr(),
                                          Z.stream_of(t)), "zs_expert_counts")
     if process_group is not None:
-        torch.distributed.all_reduce(counts, group=process_group)
+        from .dp import all_reduce_counts
+
+        all_reduce_counts(counts, process_group)
     for i, gate in enumerate(layers):
         Z.count(1)
         Z.check(Z.lib().zs_bias_sign_update(counts[i].data_ptr(), E, float(update_rate), gate.expert_biases.data_ptr(),

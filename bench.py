@@ -238,7 +238,15 @@ def run_gpu(args):
         m.experts.weight.copy_(torch.randn(E, 2 * f, d, device=dev, generator=wg) * 0.02)
         m.output_experts.weight.copy_(torch.randn(E, d, f, device=dev, generator=wg) * 0.02)
     m = m.to(bf)
+    # weight gradients straight from the GEMM epilogues into .grad; with N > 1 each one's
+    # all-reduce starts as soon as it is written and overlaps the rest of the backward
+    m.fuse_weight_grad = True
     params = [m.experts.weight, m.output_experts.weight]
+    reducer = None
+    if world > 1:
+        from zs_b200.dp import GradAllReducer
+
+        reducer = GradAllReducer(params, bucket_mb=1.0)
 
     def step(xs, ls, dys):
         for p_ in params:
@@ -249,9 +257,8 @@ def run_gpu(args):
         idx, w = GateTopK.apply(probs, bias, k)
         y = m(xs, w, idx)
         y.backward(dys)
-        if world > 1:
-            for p_ in params:
-                dist.all_reduce(p_.grad)
+        if reducer is not None:
+            reducer.finish()
         return xs.grad
 
     def barrier():
@@ -521,6 +528,13 @@ def run_config4(args):
     model = MoEModel(cfg).to(dev)
     enable_fused_weight_grad(model)
     opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3)
+    reducer = None
+    if world > 1:
+        from zs_b200.dp import GradAllReducer
+
+        # gradients averaged over ranks: each rank's loss is the mean over its own
+        # batch, so the average is the gradient of the global batch mean
+        reducer = GradAllReducer(list(model.parameters()), bucket_mb=64.0, average=True)
     B, S = args.micro_batch, 4096
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     nb = max(args.warmup, 5) + args.steps
@@ -540,10 +554,8 @@ def run_config4(args):
             loss = linear_cross_entropy(le, model.get_classifier_weights(), labels, ignore_index=-100)
         with Z.timed("backward"):
             loss.backward()
-        if world > 1:
-            for p_ in model.parameters():
-                if p_.grad is not None and not p_.grad.is_sparse:
-                    dist.all_reduce(p_.grad)
+        if reducer is not None:
+            reducer.finish()
         with Z.timed("optimizer_step"):
             opt.step()
         auxillary_loss_free_update(model, all_topk, 1e-3, mask, process_group=dist.group.WORLD if world > 1 else None)

@@ -272,8 +272,9 @@ def test_up_swiglu_and_down_dswiglu_kernels(n_per, E, d, f):
     assert device_error() == 0
 
 
-@pytest.mark.parametrize("set_to_none", [True, False])
-def test_glumlp_fused_weight_grad_accumulation(set_to_none):
+@pytest.mark.parametrize("set_to_none,wdtype", [(True, torch.float32), (False, torch.float32),
+                                                (True, torch.bfloat16), (False, torch.bfloat16)])
+def test_glumlp_fused_weight_grad_accumulation(set_to_none, wdtype):
     """fuse_weight_grad: the f32 expert grads come straight from the GEMM epilogue into .grad
     (accumulated over two backward passes) and equal the unfused bf16-dW-then-cast path to
     bf16 rounding of dW; the input and gate gradients are unchanged."""
@@ -284,6 +285,7 @@ def test_glumlp_fused_weight_grad_accumulation(set_to_none):
     ref = GLUMLP(d, f, E, k).cuda()
     fus = GLUMLP(d, f, E, k).cuda()
     fus.load_state_dict(ref.state_dict())
+    ref, fus = ref.to(wdtype), fus.to(wdtype)
     fus.fuse_weight_grad = True
     x = torch.randn(T, d, device="cuda")
     logits = torch.randn(T, E, device="cuda")
@@ -300,6 +302,6 @@ def test_glumlp_fused_weight_grad_accumulation(set_to_none):
             (y.float() * torch.linspace(-1, 1, d, device="cuda")).sum().backward()
         outs.append((xs.grad, ps.grad))
     for a, b in ((ref.experts.weight, fus.experts.weight), (ref.output_experts.weight, fus.output_experts.weight)):
-        assert b.grad.dtype == torch.float32
+        assert b.grad.dtype == wdtype and b.grad.is_contiguous()
         assert rel_err(b.grad, a.grad) < 5e-3 and cosine(b.grad, a.grad) > 0.99999
     assert rel_err(outs[1][0], outs[0][0]) < 1e-6 and rel_err(outs[1][1], outs[0][1]) < 1e-6
