@@ -99,7 +99,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast).  c0 is the innermost coordinate in
+// 2-D tiled TMA load into this CTA only.  c0 is the innermost coordinate in
 // elements and must be a multiple of 16 bytes' worth of elements.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1) {

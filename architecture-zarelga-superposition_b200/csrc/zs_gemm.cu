@@ -931,6 +931,12 @@ static int make_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t inner
   return ZS_OK;
 }
 
+static int& gemm_cta_limit_ref() {
+  static int lim = 0;
+  return lim;
+}
+int zs_gemm_cta_limit() { return gemm_cta_limit_ref(); }
+
 int num_sms() {
   static int n = 0;
   static int dev_cached = -1;
@@ -951,6 +957,9 @@ static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
                                        : grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_BF16>;
   ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   int64_t grid = num_sms();
+  // leave SMs free for kernels that must run alongside (a collective on another stream)
+  const int lim = zs_gemm_cta_limit();
+  if (lim > 0 && grid > lim) grid = lim;
   if (max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
   kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, args);
@@ -1143,6 +1152,12 @@ extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw
   if (Db != nullptr)
     rc = launch_colsum_per_expert(Db, db_se, db_sn, DY, dy_sm, N, num_experts, expert_offsets, dtype, stream);
   return rc;
+}
+
+extern "C" int zs_set_gemm_cta_limit(int max_ctas) {
+  ZS_REQUIRE(max_ctas >= 0, ZS_ERR_ARG);
+  gemm_cta_limit_ref() = max_ctas;
+  return ZS_OK;
 }
 
 extern "C" int zs_group_xty_f32(int num_experts, float* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn,

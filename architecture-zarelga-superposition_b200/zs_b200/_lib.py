@@ -41,6 +41,7 @@ _SIGNATURES = {
                                   _i64, _i32, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "zs_group_xty": (_i32, [_i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                             _vp, _i32, _vp]),
+    "zs_set_gemm_cta_limit": (_i32, [_i32]),
     "zs_group_xty_f32": (_i32, [_i32, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
                                 _i32, _vp]),
     "zs_group": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp]),

@@ -182,6 +182,14 @@ int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_
                  int64_t N, const int64_t* expert_offsets, int dtype, void* stream);
 
 /*
+ * Upper bound on the CTAs of the persistent tensor-core GEMMs (0: one per SM,
+ * the default).  A data-parallel step lowers it so the all-reduce kernels of
+ * gradients already computed find free SMs and overlap the GEMMs that follow.
+ * Process-wide; applies to launches made after the call.
+ */
+int zs_set_gemm_cta_limit(int max_ctas);
+
+/*
  * groupXtY with an f32 result written straight into a weight-gradient buffer:
  * DW[e] = X_e^T DY_e (accumulate == 0) or DW[e] += X_e^T DY_e (accumulate != 0),
  * DW f32 with the same addressing as zs_group_xty; X and DY in dtype.  This is
