@@ -101,3 +101,42 @@ def build_muonmd_optimizer(model, device, muon_lr=0.02, adam_lr=3e-4, momentum=0
                               unit_norm=True)
     return HybridGraphOptimizer(dense, sparse, capture_warmup_steps=capture_warmup_steps,
                                 enable_cuda_graph=enable_cuda_graph)
+
+
+def _lr_value(lr):
+    return float(lr.item()) if torch.is_tensor(lr) else float(lr)
+
+
+class LinearDecayScheduler:
+    """Linear LR decay without warmup by default (main.py:512-555): every group's LR is its
+    peak times fraction = 1 - (1 - min_lr_ratio) * progress, progress = (step - warmup) /
+    (total - warmup) clamped to [0, 1]; with warmup_steps > 0 the first steps ramp linearly.
+    0-dim LR tensors are updated in place (fill_), so a CUDA-graph-captured optimizer step
+    reads the new LR on every replay; float LRs are replaced.  Returns the first group's LR."""
+
+    def __init__(self, optimizer, total_steps, warmup_steps=0, min_lr_ratio=0.0):
+        self.optimizer = optimizer
+        self.total_steps = max(1, int(total_steps))
+        self.warmup_steps = min(max(0, int(warmup_steps)), self.total_steps)
+        self.min_lr_ratio = float(min_lr_ratio)
+        self.base_lrs = [_lr_value(g["lr"]) for g in optimizer.param_groups]
+        self.step_count = 0
+        self.peak_lr = self.base_lrs[0]
+        self.min_lr = self.peak_lr * self.min_lr_ratio
+
+    def _fraction(self):
+        if self.warmup_steps > 0 and self.step_count < self.warmup_steps:
+            return self.step_count / self.warmup_steps
+        span = max(1, self.total_steps - self.warmup_steps)
+        progress = min(1.0, max(0.0, (self.step_count - self.warmup_steps) / span))
+        return 1.0 - (1.0 - self.min_lr_ratio) * progress
+
+    def step(self, increment=1):
+        self.step_count += increment
+        frac = self._fraction()
+        for base, group in zip(self.base_lrs, self.optimizer.param_groups):
+            if torch.is_tensor(group["lr"]):
+                group["lr"].fill_(base * frac)
+            else:
+                group["lr"] = base * frac
+        return self.base_lrs[0] * frac
