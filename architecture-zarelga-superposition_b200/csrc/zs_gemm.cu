@@ -27,6 +27,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 namespace zs {
@@ -83,10 +84,10 @@ struct GemmArgs {
   float alpha, beta;                   // EPI_AXPBY: out = alpha * acc + beta * aux
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;   // a CTA pair splits B along N
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OFF_STAGES = 0;
   static constexpr int OFF_BARS = STAGES * STAGE_BYTES;
@@ -122,7 +123,7 @@ __device__ __forceinline__ int64_t lower_bound_i64(const int64_t* a, int64_t n, 
 
 // Tiles are numbered expert by expert in the order order[0..E); tprefix[p] is
 // the first tile of the expert at position p.
-template <int BN>
+template <int BN, int TM>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const int* tprefix, const int* rstart,
                                                 const int* order) {
   TileInfo ti;
@@ -140,8 +141,8 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const 
   ti.mt = local / a.n_tiles;
   ti.nt = local - ti.mt * a.n_tiles;
   if (a.mode == MODE_ROWS) {
-    ti.r0 = rstart[lo] + ti.mt * BM;
-    ti.r1 = min(ti.r0 + BM, rstart[lo + 1]);
+    ti.r0 = rstart[lo] + ti.mt * TM;
+    ti.r1 = min(ti.r0 + TM, rstart[lo + 1]);
     ti.nkb = a.kb_rows;
   } else {
     ti.r0 = rstart[lo];
@@ -329,11 +330,22 @@ __device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, i
   for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT>
+// PAIR: a cluster of two CTAs computes 256-row MODE_ROWS tiles with one
+// tcgen05.mma.cta_group::2 of M = 256 issued by rank 0: each CTA loads its
+// 128 rows of A and its half of B's N columns; the stage's bytes of both CTAs
+// complete on rank 0's full barrier; rank 0's commits arrive on both CTAs'
+// empty / accumulator-full barriers; the epilogue warps of both CTAs release
+// the accumulator on rank 0's barrier.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, PAIR>;
+  static_assert(!PAIR || !A_MN, "pair tiles are MODE_ROWS only");
+  constexpr int TM = PAIR ? 2 * BM : BM;    // rows of a MODE_ROWS tile
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int t_first = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int t_step = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BARS);
@@ -361,15 +373,20 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 32 * NUM_EPI_WARPS);
+      mbar_init(&tempty[b], NUM_EPI_WARPS * (PAIR ? 2 : 1));   // one arrival per epilogue warp
     }
     mbar_init(done, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(s_tmem, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(s_tmem, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s_tmem, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 1 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -418,7 +435,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     for (int p = beg; p < end; ++p) {
       const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
-      local += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+      local += (args.mode == MODE_ROWS) ? ((cnt + TM - 1) / TM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
     }
     int incl = local;
 #pragma unroll
@@ -431,19 +448,20 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       s_tprefix[p] = run;
       const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
-      run += (args.mode == MODE_ROWS) ? ((cnt + BM - 1) / BM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+      run += (args.mode == MODE_ROWS) ? ((cnt + TM - 1) / TM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
     }
     if (lane == 31) s_tprefix[E] = incl;
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();   // both CTAs' barriers initialised before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
   const int total_tiles = s_tprefix[E];
 
   constexpr uint32_t STAGE_TX = (uint32_t)L::STAGE_BYTES;
-  constexpr uint32_t IDESC_BF16 = idesc_f16(BM, BN, 1, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  constexpr uint32_t IDESC_F16 = idesc_f16(BM, BN, 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t IDESC_BF16 = idesc_f16(TM, BN, 1, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t IDESC_F16 = idesc_f16(TM, BN, 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -453,8 +471,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       uint32_t issued_mask = 0;       // stages that received at least one load
       uint32_t issued_parity = 0;     // parity of the last load per stage
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
+      for (int t = t_first; t < total_tiles && ok; t += t_step) {
+        const TileInfo ti = decode_tile<BN, TM>(t, args, s_tprefix, s_rstart, s_order);
         for (int kb = 0; kb < ti.nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -462,10 +480,29 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           }
           uint8_t* sA = smem + L::OFF_STAGES + stage * L::STAGE_BYTES;
           uint8_t* sB = sA + L::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
-          if (args.mode == MODE_ROWS) {
+          if (PAIR) {
+            // rank 0's barrier counts both CTAs' bytes; rank 1's loads land
+            // in its own shared memory and complete on rank 0's barrier
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_TX);
+            if (!B_MN) {
+              const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset;
+              const int r = EPI == EPI_SWIGLU ? brow + (crank ? args.swiglu_half : 0) + ti.nt * (BN / 2)
+                                              : brow + ti.nt * BN + (int)crank * (BN / 2);
+              tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
+              tma_load_2d_pair(sB, &tmB, &full[stage], kb * BK, r);
+            } else {
+              const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset + kb * BK;
+              tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_2d_pair(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + (int)crank * (BN / 2) + j * 64,
+                                 brow);
+            }
+          } else if (args.mode == MODE_ROWS) {
+            mbar_arrive_expect_tx(&full[stage], STAGE_TX);
             if (!A_MN) tma_load_2d(sA, &tmA, &full[stage], kb * BK, ti.r0);
             if (!B_MN) {
+              // B boxes are 128 rows: two loads per 256-row tile
               const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset;
               if (EPI == EPI_SWIGLU) {
                 tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * (BN / 2));
@@ -473,6 +510,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                             brow + args.swiglu_half + ti.nt * (BN / 2));
               } else {
                 tma_load_2d(sB, &tmB, &full[stage], kb * BK, brow + ti.nt * BN);
+                tma_load_2d(sB + (BN / 2) * 128, &tmB, &full[stage], kb * BK, brow + ti.nt * BN + BN / 2);
               }
             } else {
               const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset + kb * BK;
@@ -481,6 +519,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                 tma_load_2d(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + j * 64, brow);
             }
           } else {
+            mbar_arrive_expect_tx(&full[stage], STAGE_TX);
             const int row = ti.r0 + kb * BK;
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
@@ -497,9 +536,12 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           }
         }
       }
-      // Drain: never leave the CTA with a TMA write still in flight.
-      for (int s = 0; s < STAGES; ++s)
-        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
+      // Drain: never leave the CTA with a TMA write still in flight.  In a
+      // pair, rank 0's full barriers count both CTAs' writes; rank 1 is held
+      // by the cluster barrier at the end until rank 0 has drained.
+      if (!PAIR || crank == 0)
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -509,8 +551,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     bool ok = true;
     const uint32_t idesc = DT == ZS_BF16 ? IDESC_BF16 : IDESC_F16;
     bool issued_any = false;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
+    for (int t = t_first; t < total_tiles && ok && (!PAIR || crank == 0); t += t_step) {
+      const TileInfo ti = decode_tile<BN, TM>(t, args, s_tprefix, s_rstart, s_order);
       if (ti.nkb == 0) continue;
       const uint32_t buf = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
@@ -560,9 +602,15 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                                         : smem_desc(a_base + kk * 32, 16, 1024, 2);
             const uint64_t bdesc = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024, 2)
                                         : smem_desc(b_base + kk * 32, 16, 1024, 2);
-            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            if (PAIR)
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          if (PAIR)
+            tc_commit_pair(&empty[stage], 0x3);
+          else
+            tc_commit(&empty[stage]);
           issued_any = true;
         }
         __syncwarp();
@@ -572,13 +620,21 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
         }
       }
       if (!ok) break;
-      if (lane == 0) tc_commit(&tfull[buf]);
+      if (lane == 0) {
+        if (PAIR)
+          tc_commit_pair(&tfull[buf], 0x3);
+        else
+          tc_commit(&tfull[buf]);
+      }
       __syncwarp();
       ++acc_iter;
     }
     // Make sure every MMA this thread issued has finished before TMEM is freed.
     if (lane == 0 && issued_any) {
-      tc_commit(done);
+      if (PAIR)
+        tc_commit_pair(done, 0x1);
+      else
+        tc_commit(done);
       mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
     __syncwarp();
@@ -592,8 +648,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     uint8_t* stg = smem + L::OFF_STG + (warp - 2) * STG_BYTES;
     const bool vec = args.vec_ok;
     uint32_t acc_iter = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile<BN>(t, args, s_tprefix, s_rstart, s_order);
+    for (int t = t_first; t < total_tiles; t += t_step) {
+      const TileInfo ti = decode_tile<BN, TM>(t, args, s_tprefix, s_rstart, s_order);
       if (args.mode == MODE_XTY && ti.nkb == 0) {
         // Expert without rows: its weight gradient is zero.
         const int m = ti.mt * BM + row_in_tile;
@@ -621,7 +677,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
       // Row bookkeeping and (EPI_DSWIGLU) the saved-activation loads do not
       // depend on the accumulator: issue them before waiting for the MMA.
-      const int row = ti.r0 + row_in_tile;
+      const int row = ti.r0 + (int)crank * BM + row_in_tile;
       int64_t out_row = row;
       bool valid = args.mode == MODE_ROWS && row < ti.r1;
       if (valid && args.row_map != nullptr) {
@@ -878,18 +934,32 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           emit_chunk<DT>(args.out, ti.e * args.out_se + (int64_t)m * args.ldo_m, col0, ncols, mvalid, v, vec, stg);
         }
       }
+      // every lane's TMEM reads of this buffer are complete (tcgen05.wait::ld
+      // after each load); one arrival per warp releases it
       tc_fence_before();
-      mbar_arrive(&tempty[buf]);
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR)
+          mbar_arrive_cluster(&tempty[buf], 0);
+        else
+          mbar_arrive(&tempty[buf]);
+      }
       ++acc_iter;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // a pair stays resident until neither CTA touches the other's shared memory
+  // (rank 0's MMAs read rank 1's operands; rank 1 arrives on rank 0's barriers)
+  if (PAIR) cluster_sync_all();
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -949,12 +1019,78 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
+// Pair (2-SM) tiles are used for MODE_ROWS unless disabled with
+// ZS_GEMM_PAIR=0 in the environment, or the groups are uniform and shorter
+// than a pair tile (small batched matrices waste less with 128-row tiles).
+static bool pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("ZS_GEMM_PAIR");
+    on = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int DT>
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
+                       cudaStream_t stream) {
+  constexpr int STAGES = 6;
+  using L = Smem<BN, STAGES, true>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, DT, true>;
+  static int max_clusters = -1;   // per instantiation
+  if (max_clusters < 0) {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+    cudaLaunchConfig_t q = {};
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.gridDim = dim3(2 * (unsigned)(num_sms() / 2));
+    q.blockDim = dim3(64 + 32 * NUM_EPI_WARPS);
+    q.dynamicSmemBytes = L::ALLOC;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int n = 0;
+    ZS_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &q));
+    max_clusters = n;
+  } else {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  }
+  // persistent: no more clusters than can be resident at once
+  int64_t clusters = max_clusters;
+  const int lim = zs_gemm_cta_limit();
+  if (lim > 0 && clusters > lim / 2) clusters = lim / 2;
+  if (max_tiles < clusters) clusters = max_tiles;
+  if (clusters < 1) clusters = 1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.blockDim = dim3(64 + 32 * NUM_EPI_WARPS);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ZS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, args));
+  return ZS_OK;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
                        cudaStream_t stream) {
+  if constexpr (!A_MN) {
+    if (args.mode == MODE_ROWS && pair_enabled() && !(args.group_rows > 0 && args.group_rows < 2 * BM)) {
+      return args.out_dtype == ZS_F16 ? launch_pair<BN, A_MN, B_MN, EPI, ZS_F16>(tmA, tmB, args, max_tiles, stream)
+                                      : launch_pair<BN, A_MN, B_MN, EPI, ZS_BF16>(tmA, tmB, args, max_tiles, stream);
+    }
+  }
   using L = Smem<BN, STAGES>;
-  auto kern = args.out_dtype == ZS_F16 ? grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_F16>
-                                       : grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_BF16>;
+  auto kern = args.out_dtype == ZS_F16 ? grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_F16, false>
+                                       : grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, ZS_BF16, false>;
   ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   int64_t grid = num_sms();
   // leave SMs free for kernels that must run alongside (a collective on another stream)
@@ -1031,7 +1167,7 @@ extern "C" int zs_scatter2scatter(void* out, int64_t out_sm, const void* W, int6
   if (rc != ZS_OK) return rc;
   constexpr int BN = 256;
   if (!b_mn)
-    rc = make_tmap(&tmB, W, dtype, (uint64_t)K, (uint64_t)(num_experts * N), (uint64_t)w_sn * es, 64, BN);
+    rc = make_tmap(&tmB, W, dtype, (uint64_t)K, (uint64_t)(num_experts * N), (uint64_t)w_sn * es, 64, BN / 2);
   else
     rc = make_tmap(&tmB, W, dtype, (uint64_t)N, (uint64_t)(num_experts * K), (uint64_t)w_sk * es, 64, 64);
   if (rc != ZS_OK) return rc;
@@ -1358,7 +1494,7 @@ extern "C" int zs_xent_forward(const void* hidden, int64_t T, int64_t D, int64_t
   CUtensorMap tmA, tmB;
   int rc = make_tmap(&tmA, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 128);
   if (rc != ZS_OK) return rc;
-  rc = make_tmap(&tmB, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN);
+  rc = make_tmap(&tmB, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN / 2);
   if (rc != ZS_OK) return rc;
   GemmArgs a{};
   a.mode = MODE_ROWS;
@@ -1417,7 +1553,7 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
   CUtensorMap tmH_k, tmC_k, tmC_mn, tmH_mn;
   int rc = make_tmap(&tmH_k, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 128);
   if (rc != ZS_OK) return rc;
-  rc = make_tmap(&tmC_k, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN);
+  rc = make_tmap(&tmC_k, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, BN / 2);
   if (rc != ZS_OK) return rc;
   rc = make_tmap(&tmC_mn, classifier, dtype, (uint64_t)D, (uint64_t)V, (uint64_t)c_sm * es, 64, 64);
   if (rc != ZS_OK) return rc;
@@ -1621,10 +1757,10 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128;
     int rc;
     if ((rc = make_tmap(&tX_k128, X, dtype, n, batch * m, n * es, 64, 128)) != ZS_OK) return rc;
-    if ((rc = make_tmap(&tX_k256, X, dtype, n, batch * m, n * es, 64, BN)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tX_k256, X, dtype, n, batch * m, n * es, 64, BN / 2)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tX_mn, X, dtype, n, batch * m, n * es, 64, 64)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tA_k128, Abuf, dtype, m, batch * m, m * es, 64, 128)) != ZS_OK) return rc;
-    if ((rc = make_tmap(&tA_k256, Abuf, dtype, m, batch * m, m * es, 64, BN)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tA_k256, Abuf, dtype, m, batch * m, m * es, 64, BN / 2)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tB_k128, Bbuf, dtype, m, batch * m, m * es, 64, 128)) != ZS_OK) return rc;
     GemmArgs g{};
     g.mode = MODE_ROWS;
