@@ -82,6 +82,9 @@ struct GemmArgs {
   int accumulate;                      // EPI_F32: out += acc instead of out = acc
   int64_t group_rows;                  // > 0: uniform groups (batched GEMM), group e = rows [e*g, (e+1)*g)
   float alpha, beta;                   // EPI_AXPBY: out = alpha * acc + beta * aux
+  int sym_upper;                       // uniform square groups (pair tiles): the product is symmetric,
+                                       // only tiles (i, j >= i) are computed, strictly-upper ones also
+                                       // write their transpose (EPI_STORE / EPI_AXPBY)
 };
 
 template <int BN, int STAGES, bool PAIR = false>
@@ -135,11 +138,22 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const 
     else
       hi = mid;
   }
-  const int local = t - tprefix[lo];
+  int local = t - tprefix[lo];
   lo = order[lo];
   ti.e = lo;
-  ti.mt = local / a.n_tiles;
-  ti.nt = local - ti.mt * a.n_tiles;
+  if (a.sym_upper) {
+    // row i holds tiles (i, i..n_tiles-1)
+    int i = 0;
+    while (local >= a.n_tiles - i) {
+      local -= a.n_tiles - i;
+      ++i;
+    }
+    ti.mt = i;
+    ti.nt = i + local;
+  } else {
+    ti.mt = local / a.n_tiles;
+    ti.nt = local - ti.mt * a.n_tiles;
+  }
   if (a.mode == MODE_ROWS) {
     ti.r0 = rstart[lo] + ti.mt * TM;
     ti.r1 = min(ti.r0 + TM, rstart[lo + 1]);
@@ -229,6 +243,29 @@ __device__ __forceinline__ void emit_chunk(char* out, int64_t row_off, int col0,
 #pragma unroll
   for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], DT);
   emit_packed<DT>(out, row_off, col0, ncols, valid, p, vec, stg);
+}
+
+// The transpose of a warp's 32 rows x 32 columns chunk: lane l writes output
+// row mrow0 + l, columns [mcol0, mcol0 + 32) (64 contiguous bytes), i.e. the
+// chunk's column l.  Through the warp's staging buffer.
+__device__ __forceinline__ void emit_packed_mirror(char* out, int64_t ldo, int64_t mrow0, int64_t mcol0,
+                                                   const uint32_t (&p)[16], uint8_t* stg) {
+  const int lane = threadIdx.x & 31;
+  uint4* my = reinterpret_cast<uint4*>(stg + lane * STG_PITCH);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) my[q] = make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+  __syncwarp();
+  uint32_t t[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t lo = *reinterpret_cast<const uint16_t*>(stg + (2 * i) * STG_PITCH + lane * 2);
+    const uint32_t hi = *reinterpret_cast<const uint16_t*>(stg + (2 * i + 1) * STG_PITCH + lane * 2);
+    t[i] = lo | (hi << 16);
+  }
+  __syncwarp();
+  uint4* dst = reinterpret_cast<uint4*>(out + ((mrow0 + lane) * ldo + mcol0) * 2);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) dst[q] = make_uint4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
 }
 
 // Read 32 consecutive 16-bit columns of this lane's row as f32.
@@ -435,7 +472,9 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     for (int p = beg; p < end; ++p) {
       const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
-      local += (args.mode == MODE_ROWS) ? ((cnt + TM - 1) / TM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+      local += (args.mode == MODE_ROWS) ? (args.sym_upper ? args.n_tiles * (args.n_tiles + 1) / 2
+                                                          : ((cnt + TM - 1) / TM) * args.n_tiles)
+                                        : args.m_tiles_xty * args.n_tiles;
     }
     int incl = local;
 #pragma unroll
@@ -448,7 +487,9 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       s_tprefix[p] = run;
       const int e = s_order[p];
       int cnt = max(s_rstart[e + 1] - s_rstart[e], 0);
-      run += (args.mode == MODE_ROWS) ? ((cnt + TM - 1) / TM) * args.n_tiles : args.m_tiles_xty * args.n_tiles;
+      run += (args.mode == MODE_ROWS) ? (args.sym_upper ? args.n_tiles * (args.n_tiles + 1) / 2
+                                                        : ((cnt + TM - 1) / TM) * args.n_tiles)
+                                      : args.m_tiles_xty * args.n_tiles;
     }
     if (lane == 31) s_tprefix[E] = incl;
   }
@@ -868,7 +909,15 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = fmaf(args.alpha, __uint_as_float(r[j]), args.beta * av[j]);
-            emit_chunk<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, v, vec, stg);
+            uint32_t pv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pv[j] = pack2(v[2 * j], v[2 * j + 1], DT);
+            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            if (args.sym_upper && ti.mt < ti.nt) {
+              const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;   // first row of this square group
+              emit_packed_mirror(args.out, args.ldo_m, gbase + col0, ti.r0 - gbase + (int)crank * BM + quarter * 32,
+                                 pv, stg);
+            }
           }
         } else if (EPI == EPI_F32) {
 #pragma unroll 1
@@ -906,7 +955,15 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
                 }
               }
             }
-            emit_chunk<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, v, vec, stg);
+            uint32_t pv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pv[j] = pack2(v[2 * j], v[2 * j + 1], DT);
+            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            if (args.sym_upper && ti.mt < ti.nt) {
+              const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;
+              emit_packed_mirror(args.out, args.ldo_m, gbase + col0, ti.r0 - gbase + (int)crank * BM + quarter * 32,
+                                 pv, stg);
+            }
           }
         }
       } else {
@@ -1779,6 +1836,10 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.ldo_m = m;
     g.b_rows_per_expert = (int)m;
     g.vec_ok = 1;
+    // X X^T and A A are symmetric: on 256 x 256 pair tiles only the upper
+    // triangle of tiles is computed, each off-diagonal tile also writes its
+    // transpose (the third product, B X, is not symmetric)
+    g.sym_upper = (pair_enabled() && m % 256 == 0) ? 1 : 0;
     if ((rc = launch_gemm<BN, 4, false, false, EPI_STORE>(tX_k128, tX_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
       return rc;
     // B = b A + c A A   (B operand = A^T = A)
@@ -1791,6 +1852,7 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     if ((rc = launch_gemm<BN, 4, false, false, EPI_AXPBY>(tA_k128, tA_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
       return rc;
     // X' = a X + B X    (B operand = X^T: X is [K = m rows, N = n cols] per matrix, MN-major)
+    g.sym_upper = 0;
     g.n_tiles = (int)((n + BN - 1) / BN);
     g.kb_rows = (int)((m + BK - 1) / BK);
     g.N_out = (int)n;

@@ -148,10 +148,11 @@ __global__ void __launch_bounds__(THREADS) md_pre_kernel(const float* __restrict
   const int64_t c = c0 + lane * 8;
   float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float sacc = 0.f;
+#pragma unroll 2
   for (int k = 0; k < 8; ++k) {
     const int rr = warp * 8 + k;
     const int64_t row = r0 + rr;
-    if (row >= m) break;
+    if (row >= m) continue;
     float racc = 0.f;
     if (c < n) {
       const int64_t off = (l * m + row) * n;
@@ -223,10 +224,11 @@ __global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains ga
   const int64_t c = c0 + lane * 8;
   float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float facc = 0.f;
+#pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int rr = warp * 8 + k;
     const int64_t row = r0 + rr;
-    if (row >= m) break;
+    if (row >= m) continue;   // warp-uniform; unrolled so the rows' loads overlap
     float racc = 0.f;
     if (c < n) {
       const int64_t off = (l * m + row) * n;
@@ -339,10 +341,11 @@ __global__ void __launch_bounds__(THREADS) md_write_kernel(PostArgs a, WriteArgs
   float pc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) pc[e] = (a.norm_axis == 2 && c + e < n) ? wa.proj[l * n + c + e] : 1.f;
+#pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int rr = warp * 8 + k;
     const int64_t row = r0 + rr;
-    if (row >= m) break;
+    if (row >= m) continue;
     const float pr = a.norm_axis == 1 ? wa.proj[l * m + row] : pf;
     const int64_t off = (l * m + row) * n;
     float w[8], u[8], o[8];
