@@ -741,17 +741,18 @@ __global__ void __launch_bounds__(192, 1)
 
 template <int HD>
 struct DkvSmem {
+  static constexpr int NQS = 3;                 // Q/dO ring stages
   static constexpr int KT = 128 * HD * 2;       // K and V tiles of 128 keys
   static constexpr int QT = 64 * HD * 2;        // Q and dO tiles of 64 rows
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = KT;
-  static constexpr int OFF_QD = 2 * KT;         // NST x (Q, dO)
-  static constexpr int OFF_P = OFF_QD + NST * 2 * QT;
+  static constexpr int OFF_QD = 2 * KT;         // NQS x (Q, dO)
+  static constexpr int OFF_P = OFF_QD + NQS * 2 * QT;
   static constexpr int PB = 128 * 64 * 2;
   static constexpr int OFF_DS = OFF_P + PB;
   static constexpr int OFF_LD = OFF_DS + PB;
   static constexpr int OFF_BAR = OFF_LD + 2 * 3 * 64 * 4;   // 2 buffers of lse2[64], D[64], seg[64]
-  static constexpr int NBAR = 1 + 2 * NST + 4 + 2 + 1 + 2;
+  static constexpr int NBAR = 1 + 2 * NQS + 4 + 2 + 1 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int ALLOC = OFF_MISC + 16 + 1024;
 };
@@ -762,6 +763,7 @@ __global__ void __launch_bounds__(192, 1)
                         const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmDO64,
                         const BwdArgs a) {
   using L = DkvSmem<HD>;
+  constexpr int NST = L::NQS;   // this kernel's Q/dO ring depth
   constexpr int ATOMS = HD / 64;
   constexpr int A128 = 128 * 128, A64 = 64 * 128;
   extern __shared__ uint8_t smem_raw[];
