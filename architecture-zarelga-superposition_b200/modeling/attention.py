@@ -15,6 +15,7 @@ from typing import Optional
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from zs_b200.attn import attention as attention_core
 
@@ -99,9 +100,15 @@ class GatedAttention(nn.Module):
         bsz, seq_len, _ = hidden_states.shape
         if self.do_rope and position_ids is None:
             position_ids = torch.arange(seq_len, device=hidden_states.device).expand(bsz, seq_len)
-        q = self.q_proj(hidden_states).view(bsz, seq_len, self.num_heads, self.head_dim)
-        k = self.k_proj(hidden_states).view(bsz, seq_len, self.num_key_value_heads, self.head_dim)
-        v = self.v_proj(hidden_states).view(bsz, seq_len, self.num_key_value_heads, self.head_dim)
+        # q, k, v and the head gate read the same input: one GEMM over the
+        # concatenated weights (the input is cast once, and its gradient is one
+        # f32-accumulated product instead of a sum of four)
+        qd, kd = self.num_heads * self.head_dim, self.num_key_value_heads * self.head_dim
+        w_cat = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.head_gate_proj.weight], 0)
+        q, k, v, gate_logits = torch.split(F.linear(hidden_states, w_cat), [qd, kd, kd, self.num_heads], dim=-1)
+        q = q.reshape(bsz, seq_len, self.num_heads, self.head_dim)
+        k = k.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
+        v = v.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
         q = self.q_norm(q)
         k = self.k_norm(k)
         if self.do_rope:
@@ -112,6 +119,6 @@ class GatedAttention(nn.Module):
         if cu_seqlens is not None:
             seq_ids = _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len)
         attn = attention_core(q, k, v, window=self.window_size, seq_ids=seq_ids, k_sink=self.k_sink)
-        gate = torch.sigmoid(self.head_gate_proj(hidden_states))
+        gate = torch.sigmoid(gate_logits)
         attn = attn * gate.unsqueeze(-1)
         return self.o_proj(attn.reshape(bsz, seq_len, self.num_heads * self.head_dim))

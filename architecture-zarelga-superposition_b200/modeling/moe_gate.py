@@ -74,6 +74,9 @@ class MoEGate(nn.Module):
 
     def forward(self, hidden_states):
         bsz, seq_len, h = hidden_states.shape
-        scores = torch.sigmoid(F.linear(hidden_states.view(-1, h), self.weight, None))
-        idx, w = GateTopK.apply(scores, self.expert_biases, self.top_k)
+        idx, w = self.route(F.linear(hidden_states.view(-1, h), self.weight, None))
         return idx.view(bsz, seq_len, -1), w.view(bsz, seq_len, -1)
+
+    def route(self, logits):
+        """(topk_idx [T, k], topk_weight [T, k]) from router logits [T, E] = x W^T."""
+        return GateTopK.apply(torch.sigmoid(logits), self.expert_biases, self.top_k)
