@@ -74,22 +74,33 @@ __global__ void group_kernel(const char* A, int64_t a_sm, int64_t K, char* Y, in
     const char* srow = A + (src / fan_out) * a_sm * es;
     char* drow = Y + i * y_sm * es;
     if (vec) {
+      // four 16-byte vectors per lane in flight before any is stored
       const int64_t nv = K * es / 16;
-      for (int64_t v = lane; v < nv; v += 32) {
-        uint4 w = __ldg(reinterpret_cast<const uint4*>(srow) + v);
-        if (coeff != nullptr) {
-          if (dtype == ZS_F32) {
-            float* f = reinterpret_cast<float*>(&w);
-            for (int q = 0; q < 4; ++q) f[q] *= c;
-          } else {
-            float f[8];
-            unpack8(w, dtype, f);
+      for (int64_t v0 = 0; v0 < nv; v0 += 128) {
+        uint4 w[4];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) f[q] *= c;
-            w = pack8(f, dtype);
-          }
+        for (int u = 0; u < 4; ++u) {
+          const int64_t v = v0 + u * 32 + lane;
+          if (v < nv) w[u] = __ldg(reinterpret_cast<const uint4*>(srow) + v);
         }
-        reinterpret_cast<uint4*>(drow)[v] = w;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t v = v0 + u * 32 + lane;
+          if (v >= nv) continue;
+          if (coeff != nullptr) {
+            if (dtype == ZS_F32) {
+              float* f = reinterpret_cast<float*>(&w[u]);
+              for (int q = 0; q < 4; ++q) f[q] *= c;
+            } else {
+              float f[8];
+              unpack8(w[u], dtype, f);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) f[q] *= c;
+              w[u] = pack8(f, dtype);
+            }
+          }
+          reinterpret_cast<uint4*>(drow)[v] = w[u];
+        }
       }
     } else {
       for (int64_t k = lane; k < K; k += 32) {
@@ -151,12 +162,26 @@ __global__ void rowwise_sum_product_kernel(char* out, int out_dtype, int64_t o_s
     if (vec) {
       const uint4* pa = reinterpret_cast<const uint4*>(A + (t * a_s0 + f * a_s1) * 2);
       const uint4* pb = reinterpret_cast<const uint4*>(B + (t * b_s0) * 2);
-      for (int64_t v = lane; v < H / 8; v += 32) {
-        float fa[8], fb[8];
-        unpack8(__ldg(pa + v), a_dtype, fa);
-        unpack8(__ldg(pb + v), b_dtype, fb);
+      // four vectors of each operand per lane in flight before the products
+      for (int64_t v0 = 0; v0 < H / 8; v0 += 128) {
+        uint4 ra[4], rb[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc = fmaf(fa[q], fb[q], acc);
+        for (int u = 0; u < 4; ++u) {
+          const int64_t v = v0 + u * 32 + lane;
+          if (v < H / 8) {
+            ra[u] = __ldg(pa + v);
+            rb[u] = __ldg(pb + v);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (v0 + u * 32 + lane >= H / 8) continue;
+          float fa[8], fb[8];
+          unpack8(ra[u], a_dtype, fa);
+          unpack8(rb[u], b_dtype, fb);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc = fmaf(fa[q], fb[q], acc);
+        }
       }
     } else {
       for (int64_t h = lane; h < H; h += 32)
@@ -178,7 +203,25 @@ __global__ void weighted_row_sum_kernel(char* out, int64_t o_sm, const char* in,
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
     float wt[32];
     for (int j = 0; j < k; ++j) wt[j] = w ? load_as_f32(w, t * k + j, w_dtype) : 1.0f;
-    if (vec) {
+    if (vec && k <= 8) {
+      // all k slot rows' vectors in flight before the accumulation (same j order)
+      for (int64_t v = lane; v < C / 8; v += 32) {
+        uint4 raw[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(in + ((t * k + j) * i_sm) * 2) + v);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j >= k) break;
+          float f[8];
+          unpack8(raw[j], dtype, f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt[j], f[q], acc[q]);
+        }
+        reinterpret_cast<uint4*>(out + (t * o_sm) * 2)[v] = pack8(acc, dtype);
+      }
+    } else if (vec) {
       for (int64_t v = lane; v < C / 8; v += 32) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int j = 0; j < k; ++j) {
