@@ -476,27 +476,32 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const 
 
 template <int HD>
 struct DqSmem {
+  static constexpr int NKS = 4;                 // K/V ring stages
   static constexpr int QT = 128 * HD * 2;       // Q and dO tiles
   static constexpr int KT = 64 * HD * 2;        // K and V tiles of 64 keys
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = QT;
-  static constexpr int OFF_KV = 2 * QT;         // NST x (K, V)
-  static constexpr int OFF_DS = OFF_KV + NST * 2 * KT;
-  static constexpr int DS_BYTES = 128 * 64 * 2;
-  static constexpr int OFF_BAR = OFF_DS + DS_BYTES;
-  static constexpr int NBAR = 1 + 2 * NST + 4 + 2 + 1;
+  static constexpr int OFF_KV = 2 * QT;         // NKS x (K, V)
+  static constexpr int OFF_BAR = OFF_KV + NKS * 2 * KT;
+  // q_full, kv_full[NKS], kv_empty[NKS], sp_full[2], ds_full[2], done
+  static constexpr int NBAR = 1 + 2 * NKS + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int ALLOC = OFF_MISC + 16 + 1024;
 };
 
-// a 128-row tile occupies HD/64 atoms of 128 rows x 128 B; a 64-row tile
-// HD/64 atoms of 64 rows x 128 B
+// dQ per 128-row query tile.  320 threads: warp 0 TMA, warp 1 MMA, warps 2..5
+// and 6..9 two softmax groups taking alternate 64-key tiles, each with its own
+// TMEM buffer (S in columns [0, 64), dP in [64, 128)); dS (bf16 pairs) goes
+// back over S's columns, 16 keys at a time, and feeds dQ += dS K as the A
+// operand straight from tensor memory.  The sink key (value 0) adds
+// dS_sink = -P_sink * D per row; dQ gains dS_sink * k_sink.
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmK64, const __grid_constant__ CUtensorMap tmV64,
                        const BwdArgs a, float* __restrict__ ds_sink) {
   using L = DqSmem<HD>;
+  constexpr int NKS = L::NKS;
   constexpr int ATOMS = HD / 64;
   constexpr int A128 = 128 * 128, A64 = 64 * 128;
   extern __shared__ uint8_t smem_raw[];
@@ -504,12 +509,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + NST;
-  uint64_t* sp_full = kv_empty + NST;   // [2]
-  uint64_t* sp_empty = sp_full + 2;     // [2]
-  uint64_t* ds_full = sp_empty + 2;
-  uint64_t* ds_free = ds_full + 1;
-  uint64_t* done = ds_free + 1;
+  uint64_t* kv_empty = kv_full + NKS;
+  uint64_t* sp_full = kv_empty + NKS;   // [2]
+  uint64_t* ds_full = sp_full + 2;      // [2]
+  uint64_t* done = ds_full + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -536,16 +539,14 @@ __global__ void __launch_bounds__(192, 1)
   const int n_kv = kt_hi - kt_lo + 1;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < NST; ++s) {
+    for (int s = 0; s < NKS; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sp_full[s], 1);
-      mbar_init(&sp_empty[s], 128);
+      mbar_init(&ds_full[s], 128);
     }
-    mbar_init(ds_full, 128);
-    mbar_init(ds_free, 1);
     mbar_init(done, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -558,7 +559,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  // TMEM: S[sb] at sb*128, dP[sb] at sb*128 + 64, dQ at 256
+  // TMEM: buffer g at g*128 (S / dS in [0, 64), dP in [64, 128)), dQ at 256
   constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
   constexpr uint32_t IDESC_DQ = idesc_f16(128, HD, 1, 0, 1);
   if (warp == 0) {
@@ -570,8 +571,8 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_2d(smem + L::OFF_DO + at * A128, &tmDO, q_full, h * HD + at * 64, (int)(row0 + q0));
       }
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % NST;
-        if (!mbar_wait(&kv_empty[st], ((j / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        const int st = j % NKS;
+        if (!mbar_wait(&kv_empty[st], ((j / NKS) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
         uint8_t* kb = smem + L::OFF_KV + st * 2 * L::KT;
         mbar_arrive_expect_tx(&kv_full[st], 2 * L::KT);
         const int krow = (int)(row0 + (kt_lo + j) * 64);
@@ -580,10 +581,10 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(kb + L::KT + at * A64, &tmV64, &kv_full[st], hk * HD + at * 64, krow);
         }
         issued |= 1u << st;
-        par = (par & ~(1u << st)) | ((uint32_t)((j / NST) & 1) << st);
+        par = (par & ~(1u << st)) | ((uint32_t)((j / NKS) & 1) << st);
       }
       mbar_wait(q_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < NST; ++s)
+      for (int s = 0; s < NKS; ++s)
         if (issued & (1u << s)) mbar_wait(&kv_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
@@ -591,9 +592,8 @@ __global__ void __launch_bounds__(192, 1)
     bool any = false;
     for (int j = 0; ok && j <= n_kv; ++j) {
       if (j < n_kv) {
-        const int st = j % NST, sb = j & 1;
-        if (!warp_wait(&kv_full[st], (j / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        if (!warp_wait(&sp_empty[sb], ((j >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        const int st = j % NKS, g = j & 1;
+        if (!warp_wait(&kv_full[st], (j / NKS) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t qa = smem_u32(smem + L::OFF_Q), da = smem_u32(smem + L::OFF_DO);
@@ -601,28 +601,26 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t offa = (kk / 4) * A128 + (kk % 4) * 32, offb = (kk / 4) * A64 + (kk % 4) * 32;
-            tc_mma_f16(tmem + sb * 128, smem_desc(qa + offa, 16, 1024, 2), smem_desc(ka + offb, 16, 1024, 2),
+            tc_mma_f16(tmem + g * 128, smem_desc(qa + offa, 16, 1024, 2), smem_desc(ka + offb, 16, 1024, 2),
                        IDESC_SP, kk > 0);
-            tc_mma_f16(tmem + sb * 128 + 64, smem_desc(da + offa, 16, 1024, 2), smem_desc(va + offb, 16, 1024, 2),
+            tc_mma_f16(tmem + g * 128 + 64, smem_desc(da + offa, 16, 1024, 2), smem_desc(va + offb, 16, 1024, 2),
                        IDESC_SP, kk > 0);
           }
-          tc_commit(&sp_full[sb]);
+          tc_commit(&sp_full[g]);
           any = true;
         }
         __syncwarp();
       }
       if (j >= 1) {
-        const int jj = j - 1, st = jj % NST;
-        if (!warp_wait(ds_full, jj & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        const int jj = j - 1, st = jj % NKS, g = jj & 1;
+        if (!warp_wait(&ds_full[g], (jj >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t dsa = smem_u32(smem + L::OFF_DS);
           const uint32_t ka = smem_u32(smem + L::OFF_KV + st * 2 * L::KT);
 #pragma unroll
           for (int kk = 0; kk < 64 / 16; ++kk)
-            tc_mma_f16(tmem + 256, smem_desc(dsa + kk * 32, 16, 1024, 2), smem_desc(ka + kk * 2048, A64, 1024, 2),
-                       IDESC_DQ, (jj > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(ds_free);
+            tc_mma_f16_ts(tmem + 256, tmem + g * 128 + kk * 8, smem_desc(ka + kk * 2048, A64, 1024, 2), IDESC_DQ,
+                          (jj > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&kv_empty[st]);
         }
         __syncwarp();
@@ -634,77 +632,77 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int q = q0 + r;
     const bool qvalid = q < a.S;
     const uint32_t lb = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tb = tmem + lb + grp * 128;
     const int64_t bh = (int64_t)b * a.H + h;
     const float lse2 = qvalid ? __ldg(a.lse + bh * a.S + q) * LOG2E : 0.f;
     const float Dq = qvalid ? __ldg(a.D + bh * a.S + q) : 0.f;
     int qseg = 0;
     if (a.seg_start != nullptr && qvalid) qseg = __ldg(a.seg_start + row0 + q);
     bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(&sp_full[sb], (j >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+    for (int j = grp; j < n_kv && ok; j += 2) {
+      const int u = j >> 1;
+      if (!warp_wait(&sp_full[grp], u & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[64], dr[64];
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&sp_empty[sb]);
-      if (j >= 1 && !warp_wait(ds_free, (j - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
       const int k0 = (kt_lo + j) * 64;
-      uint8_t* row = smem + L::OFF_DS + r * 128;
+      const bool edge = (k0 + 63 > q0) || (q0 + 127 >= a.S) || a.seg_start != nullptr ||
+                        (a.window > 0 && q0 + 127 - k0 >= a.window);
+      // 16 keys at a time; dS (bf16 pairs) overwrites S columns already read
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sr[16], dr[16];
+        tmem_ld_32x32b_x16(tb + ch * 16, sr);
+        tmem_ld_32x32b_x16(tb + 64 + ch * 16, dr);
+        tc_wait_ld();
+        uint32_t w[8];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t w[4];
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int x = 0; x < 8; ++x) {
           float v2[2];
 #pragma unroll
           for (int y = 0; y < 2; ++y) {
-            const int c = ch * 8 + 2 * x + y;
-            const int k = k0 + c;
-            bool vis = qvalid && k <= q;
-            if (a.window > 0) vis = vis && (q - k < a.window);
-            if (a.seg_start != nullptr) vis = vis && k >= qseg && qseg >= 0;
-            const float p = vis ? fast_exp2(__uint_as_float(sr[c]) * a.scale_log2 - lse2) : 0.f;
-            v2[y] = p * (__uint_as_float(dr[c]) - Dq);
+            const int cl = 2 * x + y;
+            const int k = k0 + ch * 16 + cl;
+            bool vis = qvalid;
+            if (edge) {
+              vis = vis && k <= q;
+              if (a.window > 0) vis = vis && (q - k < a.window);
+              if (a.seg_start != nullptr) vis = vis && k >= qseg && qseg >= 0;
+            }
+            const float p = vis ? fast_exp2(fmaf(__uint_as_float(sr[cl]), a.scale_log2, -lse2)) : 0.f;
+            v2[y] = p * (__uint_as_float(dr[cl]) - Dq);
           }
           __nv_bfloat162 pp = __floats2bfloat162_rn(v2[0], v2[1]);
           w[x] = *reinterpret_cast<uint32_t*>(&pp);
         }
-        *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st_32x32b_x8(tb + ch * 8, w);
       }
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[grp]);
     }
-    if (ok && warp_wait(ds_free, (n_kv - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+    // all dQ products (the MMA warp's single-phase commit); group g writes dQ
+    // columns [g*HD/2, (g+1)*HD/2)
+    if (ok && warp_wait(done, 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      // sink key (value 0): dS_sink = -P_sink * D; dQ gains dS_sink * k_sink
       float dss = 0.f;
       if (a.k_sink != nullptr && qvalid) {
         const __nv_bfloat16* qr = a.q + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
         float dot = 0.f;
         for (int c = 0; c < HD; ++c) dot = fmaf(__bfloat162float(qr[c]), sink_at(a, h * HD + c), dot);
         dss = -fast_exp2(dot * a.scale_log2 - lse2) * Dq;
-        ds_sink[bh * a.S + q] = dss;
+        if (grp == 0) ds_sink[bh * a.S + q] = dss;
       }
       __nv_bfloat16* out = a.dq + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = grp * (HD / 64); c < (grp + 1) * (HD / 64); ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem + lb + 256 + c * 32, v);
         tc_wait_ld();
@@ -741,29 +739,35 @@ __global__ void __launch_bounds__(192, 1)
 
 template <int HD>
 struct DkvSmem {
-  static constexpr int NQS = 3;                 // Q/dO ring stages
-  static constexpr int KT = 128 * HD * 2;       // K and V tiles of 128 keys
-  static constexpr int QT = 64 * HD * 2;        // Q and dO tiles of 64 rows
+  static constexpr int NQS = 4;                     // Q/dO ring stages
+  static constexpr int KT = 128 * HD * 2;           // K and V tiles of 128 keys
+  static constexpr int QT = 64 * HD * 2;            // Q and dO tiles of 64 rows
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = KT;
-  static constexpr int OFF_QD = 2 * KT;         // NQS x (Q, dO)
-  static constexpr int OFF_P = OFF_QD + NQS * 2 * QT;
-  static constexpr int PB = 128 * 64 * 2;
-  static constexpr int OFF_DS = OFF_P + PB;
-  static constexpr int OFF_LD = OFF_DS + PB;
-  static constexpr int OFF_BAR = OFF_LD + 2 * 3 * 64 * 4;   // 2 buffers of lse2[64], D[64], seg[64]
-  static constexpr int NBAR = 1 + 2 * NQS + 4 + 2 + 1 + 2;
+  static constexpr int OFF_QD = 2 * KT;             // NQS x (Q, dO)
+  static constexpr int OFF_LD = OFF_QD + NQS * 2 * QT;  // [2 groups][2] x (lse2[64], D[64], seg[64])
+  static constexpr int OFF_BAR = OFF_LD + 4 * 192 * 4;
+  // kv_full, qd_full[NQS], qd_empty[NQS], sp_full[2], ds_full[2], done, ld_full[4]
+  static constexpr int NBAR = 1 + 2 * NQS + 4 + 1 + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int ALLOC = OFF_MISC + 16 + 1024;
 };
 
+// 320 threads: warp 0 TMA, warp 1 MMA, warps 2..5 and 6..9 two softmax groups
+// taking alternate query tiles (group g: iterations i = g, g+2, ...), each with
+// its own TMEM buffer: S^T (64 f32 columns) and dP^T (64 columns) come in from
+// the MMA, P^T and dS^T (bf16 pairs, 32 columns each) go back into the same
+// columns and feed the dV / dK products as the A operand straight from tensor
+// memory.  The tensor pipe executes this CTA's MMAs in issue order, so the
+// next S^T into a buffer (issued after that buffer's dV/dK) cannot overwrite
+// P^T/dS^T before they are read.
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmDO64,
                         const BwdArgs a) {
   using L = DkvSmem<HD>;
-  constexpr int NST = L::NQS;   // this kernel's Q/dO ring depth
+  constexpr int NQS = L::NQS;
   constexpr int ATOMS = HD / 64;
   constexpr int A128 = 128 * 128, A64 = 64 * 128;
   extern __shared__ uint8_t smem_raw[];
@@ -771,18 +775,16 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
   uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = qd_full + NST;
-  uint64_t* sp_full = qd_empty + NST;
-  uint64_t* sp_empty = sp_full + 2;
-  uint64_t* ds_full = sp_empty + 2;
-  uint64_t* ds_free = ds_full + 1;
-  uint64_t* done = ds_free + 1;
-  uint64_t* ld_full = done + 1;          // [2]: the query tile's lse / D / seg staged
+  uint64_t* qd_empty = qd_full + NQS;
+  uint64_t* sp_full = qd_empty + NQS;   // [2]
+  uint64_t* ds_full = sp_full + 2;      // [2]
+  uint64_t* done = ds_full + 2;
+  uint64_t* ld_full = done + 1;         // [4]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   float* s_ld = reinterpret_cast<float*>(smem + L::OFF_LD);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;                 // earliest key tiles (most queries) first
+  const int kt = blockIdx.x;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int G = a.H / a.Hkv;
   const int k0 = kt * 128;
@@ -795,19 +797,16 @@ __global__ void __launch_bounds__(192, 1)
   const int n_it = G * n_q;
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < NST; ++s) {
+    for (int s = 0; s < NQS; ++s) {
       mbar_init(&qd_full[s], 1);
       mbar_init(&qd_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sp_full[s], 1);
-      mbar_init(&sp_empty[s], 128);
+      mbar_init(&ds_full[s], 128);
     }
-    mbar_init(ds_full, 128);
-    mbar_init(ds_free, 1);
     mbar_init(done, 1);
-    mbar_init(&ld_full[0], 128);
-    mbar_init(&ld_full[1], 128);
+    for (int s = 0; s < 4; ++s) mbar_init(&ld_full[s], 128);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -819,7 +818,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  // TMEM: S^T[sb] at sb*128, dP^T[sb] at sb*128 + 64, dV at 256, dK at 256 + HD
+  // TMEM: buffer g at g*128 (S^T / P^T in columns [0, 64), dP^T / dS^T in [64, 128)),
+  // dV at 256, dK at 256 + HD
   constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
   constexpr uint32_t IDESC_ACC = idesc_f16(128, HD, 1, 0, 1);
   if (warp == 0) {
@@ -831,10 +831,10 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_2d(smem + L::OFF_V + at * A128, &tmV, kv_full, hk * HD + at * 64, (int)(row0 + k0));
       }
       for (int i = 0; i < n_it; ++i) {
-        const int st = i % NST;
+        const int st = i % NQS;
         const int g = i / n_q, qi = qt_lo + i % n_q;
         const int h = hk * G + g;
-        if (!mbar_wait(&qd_empty[st], ((i / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        if (!mbar_wait(&qd_empty[st], ((i / NQS) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
         uint8_t* qb = smem + L::OFF_QD + st * 2 * L::QT;
         mbar_arrive_expect_tx(&qd_full[st], 2 * L::QT);
         for (int at = 0; at < ATOMS; ++at) {
@@ -842,10 +842,10 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(qb + L::QT + at * A64, &tmDO64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
         }
         issued |= 1u << st;
-        par = (par & ~(1u << st)) | ((uint32_t)((i / NST) & 1) << st);
+        par = (par & ~(1u << st)) | ((uint32_t)((i / NQS) & 1) << st);
       }
       mbar_wait(kv_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < NST; ++s)
+      for (int s = 0; s < NQS; ++s)
         if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
@@ -853,9 +853,8 @@ __global__ void __launch_bounds__(192, 1)
     bool any = false;
     for (int i = 0; ok && i <= n_it; ++i) {
       if (i < n_it) {
-        const int st = i % NST, sb = i & 1;
-        if (!warp_wait(&qd_full[st], (i / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        if (!warp_wait(&sp_empty[sb], ((i >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        const int st = i % NQS, g = i & 1;
+        if (!warp_wait(&qd_full[st], (i / NQS) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ka = smem_u32(smem + L::OFF_K), va = smem_u32(smem + L::OFF_V);
@@ -863,31 +862,29 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t offa = (kk / 4) * A128 + (kk % 4) * 32, offb = (kk / 4) * A64 + (kk % 4) * 32;
-            tc_mma_f16(tmem + sb * 128, smem_desc(ka + offa, 16, 1024, 2), smem_desc(qa + offb, 16, 1024, 2),
+            tc_mma_f16(tmem + g * 128, smem_desc(ka + offa, 16, 1024, 2), smem_desc(qa + offb, 16, 1024, 2),
                        IDESC_SP, kk > 0);
-            tc_mma_f16(tmem + sb * 128 + 64, smem_desc(va + offa, 16, 1024, 2), smem_desc(da + offb, 16, 1024, 2),
+            tc_mma_f16(tmem + g * 128 + 64, smem_desc(va + offa, 16, 1024, 2), smem_desc(da + offb, 16, 1024, 2),
                        IDESC_SP, kk > 0);
           }
-          tc_commit(&sp_full[sb]);
+          tc_commit(&sp_full[g]);
           any = true;
         }
         __syncwarp();
       }
       if (i >= 1) {
-        const int ii = i - 1, st = ii % NST;
-        if (!warp_wait(ds_full, ii & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        const int ii = i - 1, st = ii % NQS, g = ii & 1;
+        if (!warp_wait(&ds_full[g], (ii >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t pa = smem_u32(smem + L::OFF_P), dsa = smem_u32(smem + L::OFF_DS);
           const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
 #pragma unroll
           for (int kk = 0; kk < 64 / 16; ++kk) {
-            tc_mma_f16(tmem + 256, smem_desc(pa + kk * 32, 16, 1024, 2), smem_desc(da + kk * 2048, A64, 1024, 2),
-                       IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_f16(tmem + 256 + HD, smem_desc(dsa + kk * 32, 16, 1024, 2), smem_desc(qa + kk * 2048, A64, 1024, 2),
-                       IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16_ts(tmem + 256, tmem + g * 128 + kk * 8, smem_desc(da + kk * 2048, A64, 1024, 2), IDESC_ACC,
+                          (ii > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16_ts(tmem + 256 + HD, tmem + g * 128 + 64 + kk * 8, smem_desc(qa + kk * 2048, A64, 1024, 2),
+                          IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(ds_free);
           tc_commit(&qd_empty[st]);
         }
         __syncwarp();
@@ -899,22 +896,25 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;   // key row
+    const int grp = (warp - 2) >> 2;          // softmax group
+    const int quarter = warp & 3;             // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;        // key row
     const int k = k0 + r;
     const bool kvalid = k < a.S;
-    const int tid = threadIdx.x - 64;
+    const int tid = ((warp - 2) & 3) * 32 + lane;
     const uint32_t lb = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tb = tmem + lb + grp * 128;
     bool ok = k0 < a.S;
-    for (int i = 0; i < n_it && ok; ++i) {
-      const int sb = i & 1;
+    for (int i = grp; i < n_it && ok; i += 2) {
+      const int u = i >> 1;                   // this group's use count
       const int g = i / n_q, qi = qt_lo + i % n_q;
       const int h = hk * G + g;
       const int qb0 = qi * 64;
       const int64_t bh = (int64_t)b * a.H + h;
-      // double-buffered staging: buffer i&1 was last read in iteration i-2, and every
-      // thread has passed ld_full of iteration i-1 (all 128 arrivals) since then
-      float* s_lse2 = s_ld + (i & 1) * 192;
+      // staging buffer (grp, u & 1) was last read at this group's use u - 2; every
+      // thread of the group has passed ld_full of use u - 1 since then
+      const int li = grp * 2 + (u & 1);
+      float* s_lse2 = s_ld + li * 192;
       float* s_D = s_lse2 + 64;
       int* s_seg = reinterpret_cast<int*>(s_lse2 + 128);
       if (tid < 64) {
@@ -925,86 +925,82 @@ __global__ void __launch_bounds__(192, 1)
         const int qq = qb0 + tid - 64;
         s_D[tid - 64] = qq < a.S ? __ldg(a.D + bh * a.S + qq) : 0.f;
       }
-      mbar_arrive(&ld_full[i & 1]);
-      if (!warp_wait(&ld_full[i & 1], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      mbar_arrive(&ld_full[li]);
+      if (!warp_wait(&ld_full[li], (u >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
-      if (!warp_wait(&sp_full[sb], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      if (!warp_wait(&sp_full[grp], u & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[64], dr[64];
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld_32x32b_x32(tmem + lb + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&sp_empty[sb]);
-      if (i >= 1 && !warp_wait(ds_free, (i - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = smem + L::OFF_P + r * 128;
-      uint8_t* drow = smem + L::OFF_DS + r * 128;
+      // masks only on tiles that straddle the diagonal, the window edge, a
+      // packed-sequence start, or the end of the sequence
+      const bool edge = (qb0 < k0 + 128) || (qb0 + 63 >= a.S) || a.seg_start != nullptr ||
+                        (a.window > 0 && qb0 + 63 - k0 >= a.window);
+      // 16 query columns at a time: P^T / dS^T (bf16 pairs) overwrite the S^T / dP^T
+      // columns already read (chunk ch writes columns [8ch, 8ch+8), read by chunk ch/2)
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sr[16], dr[16];
+        tmem_ld_32x32b_x16(tb + ch * 16, sr);
+        tmem_ld_32x32b_x16(tb + 64 + ch * 16, dr);
+        tc_wait_ld();
+        uint32_t pw[8], dw[8];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t wp[4], wd[4];
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int x = 0; x < 8; ++x) {
           float pv[2], dv2[2];
 #pragma unroll
           for (int y = 0; y < 2; ++y) {
-            const int c = ch * 8 + 2 * x + y;
-            const int q = qb0 + c;
-            bool vis = kvalid && q < a.S && q >= k;
-            if (a.window > 0) vis = vis && (q - k < a.window);
-            if (a.seg_start != nullptr) vis = vis && s_seg[c] >= 0 && s_seg[c] <= k;
-            const float p = vis ? fast_exp2(__uint_as_float(sr[c]) * a.scale_log2 - s_lse2[c]) : 0.f;
+            const int cl = 2 * x + y, c = ch * 16 + cl;
+            bool vis = kvalid;
+            if (edge) {
+              const int q = qb0 + c;
+              vis = vis && q < a.S && q >= k;
+              if (a.window > 0) vis = vis && (q - k < a.window);
+              if (a.seg_start != nullptr) vis = vis && s_seg[c] >= 0 && s_seg[c] <= k;
+            }
+            const float p = vis ? fast_exp2(fmaf(__uint_as_float(sr[cl]), a.scale_log2, -s_lse2[c])) : 0.f;
             pv[y] = p;
-            dv2[y] = p * (__uint_as_float(dr[c]) - s_D[c]);
+            dv2[y] = p * (__uint_as_float(dr[cl]) - s_D[c]);
           }
           __nv_bfloat162 p2 = __floats2bfloat162_rn(pv[0], pv[1]);
           __nv_bfloat162 d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
-          wp[x] = *reinterpret_cast<uint32_t*>(&p2);
-          wd[x] = *reinterpret_cast<uint32_t*>(&d2);
+          pw[x] = *reinterpret_cast<uint32_t*>(&p2);
+          dw[x] = *reinterpret_cast<uint32_t*>(&d2);
         }
-        const int sw = (ch ^ (r & 7)) * 16;
-        *reinterpret_cast<uint4*>(prow + sw) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
-        *reinterpret_cast<uint4*>(drow + sw) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        tmem_st_32x32b_x8(tb + ch * 8, pw);
+        tmem_st_32x32b_x8(tb + 64 + ch * 8, dw);
       }
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[grp]);
     }
-    if (ok && n_it > 0 && warp_wait(ds_free, (n_it - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+    // all dV/dK products: the MMA warp's single-phase `done` commit; group 0
+    // writes dV, group 1 dK
+    if (ok && n_it > 0 && warp_wait(done, 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      __nv_bfloat16* dvo = a.dv + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
-      __nv_bfloat16* dko = a.dk + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
+      const int part = grp;
+      const float mul = part == 0 ? 1.0f : a.scale;
+      __nv_bfloat16* dst_row = (part == 0 ? a.dv : a.dk) + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
 #pragma unroll 1
-      for (int part = 0; part < 2; ++part) {
-        const float mul = part == 0 ? 1.0f : a.scale;
-        __nv_bfloat16* dst_row = part == 0 ? dvo : dko;
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem + lb + 256 + part * HD + c * 32, v);
-          tc_wait_ld();
-          if (kvalid) {
-            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lb + 256 + part * HD + c * 32, v);
+        tc_wait_ld();
+        if (kvalid) {
+          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
 #pragma unroll
-            for (int x = 0; x < 4; ++x) {
-              uint32_t w[4];
+          for (int x = 0; x < 4; ++x) {
+            uint32_t w[4];
 #pragma unroll
-              for (int y = 0; y < 4; ++y) {
-                __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(v[x * 8 + 2 * y]) * mul,
-                                                          __uint_as_float(v[x * 8 + 2 * y + 1]) * mul);
-                w[y] = *reinterpret_cast<uint32_t*>(&pp);
-              }
-              dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int y = 0; y < 4; ++y) {
+              __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(v[x * 8 + 2 * y]) * mul,
+                                                        __uint_as_float(v[x * 8 + 2 * y + 1]) * mul);
+              w[y] = *reinterpret_cast<uint32_t*>(&pp);
             }
+            dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -1075,19 +1071,19 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
                                      attn::DqSmem<128>::ALLOC));
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      attn::DkvSmem<128>::ALLOC));
-    attn::attn_bwd_dq_kernel<128><<<gq, 192, attn::DqSmem<128>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+    attn::attn_bwd_dq_kernel<128><<<gq, 320, attn::DqSmem<128>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
                                                                                  ds_sink);
     ZS_CUDA_TRY(cudaGetLastError());
-    attn::attn_bwd_dkv_kernel<128><<<gkv, 192, attn::DkvSmem<128>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
+    attn::attn_bwd_dkv_kernel<128><<<gkv, 320, attn::DkvSmem<128>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
   } else {
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      attn::DqSmem<64>::ALLOC));
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      attn::DkvSmem<64>::ALLOC));
-    attn::attn_bwd_dq_kernel<64><<<gq, 192, attn::DqSmem<64>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+    attn::attn_bwd_dq_kernel<64><<<gq, 320, attn::DqSmem<64>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
                                                                                ds_sink);
     ZS_CUDA_TRY(cudaGetLastError());
-    attn::attn_bwd_dkv_kernel<64><<<gkv, 192, attn::DkvSmem<64>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
+    attn::attn_bwd_dkv_kernel<64><<<gkv, 320, attn::DkvSmem<64>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
   }
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
