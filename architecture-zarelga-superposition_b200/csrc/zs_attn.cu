@@ -6,25 +6,28 @@
 // the learned per-head key sink of modeling/hca.py:138-144,264-298 (one extra
 // always-visible key whose value is zero).  Scale 1/sqrt(head_dim).
 //
-// One CTA per (query tile of 128 rows, head, batch row), 192 threads:
-//   warp 0      TMA: the Q tile once, then K/V tiles into a 2-stage ring
-//   warp 1      MMA: S_j = Q K_j^T into one of two TMEM buffers, then
-//               O += P_{j-1} V_{j-1} with P from shared memory
-//   warps 2..5  softmax: one query row per thread; read S_j from TMEM, keep
-//               the running max (log2 domain) and sum, write P_j (bf16) to
-//               shared memory in the MMA's 128-byte swizzled layout, rescale
-//               the O accumulator in TMEM only when the max grows by > 8
-//               (2^8 headroom keeps P and the sums finite); finally O / sum
-//               and the log-sum-exp.
-// TMEM columns: S buffers [0,128) and [128,256), O [256, 256+hd).
+// One CTA per (256 query rows = two 128-row tiles, head, batch row), 320
+// threads:
+//   warp 0      TMA: both Q tiles once, then K and V tiles of 128 keys into a
+//               ring of single-tile slots (K_j, V_j, K_j+1, ...)
+//   warp 1      MMA: per key tile j and query tile t, O_t += P_t V_{j-1}
+//               (P from tensor memory) then S_t = Q_t K_j^T; the two query
+//               tiles alternate, so one tile's softmax overlaps the other
+//               tile's products
+//   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1: one
+//               row per thread; read S_t from TMEM, keep the running max
+//               (log2 domain) and sum, rescale O_t in TMEM only when the max
+//               grows by > 8 (2^8 headroom keeps P and the sums finite), write
+//               P_t (bf16 pairs) over S_t's first 64 columns; finally O_t /
+//               sum and the log-sum-exp.
+// TMEM columns: S_t / P_t at t*128 (128), O_t at 256 + t*hd.
 #include "zs_common.cuh"
 
 namespace zs {
 namespace attn {
 
-constexpr int BQ = 128;      // query rows per CTA
+constexpr int BQ = 128;      // query rows per tile (two tiles per CTA in the forward)
 constexpr int BKV = 128;     // keys per tile
-constexpr int NST = 2;       // K/V ring stages
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
@@ -35,7 +38,6 @@ struct FwdArgs {
   const int* seg_start;       // nullable [B*S]: first position of the token's packed sequence (-1: padding)
   const void* k_sink;         // nullable [H, hd] (dtype of sink_dtype)
   int sink_dtype;
-  const __nv_bfloat16* q;     // [B*S, H*hd]
   __nv_bfloat16* o;           // [B*S, H*hd]
   float* lse;                 // [B, H, S] natural-log log-sum-exp
 };
@@ -43,12 +45,12 @@ struct FwdArgs {
 template <int HD>
 struct FwdSmem {
   static constexpr int TILE = 128 * HD * 2;          // one 128-row tile (Q, K or V)
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_KV = TILE;                // NST x (K, V)
-  static constexpr int OFF_P = OFF_KV + NST * 2 * TILE;
-  static constexpr int P_BYTES = 128 * 128 * 2;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int NBAR = 1 + 2 * NST + 2 + 2 + 1 + 1 + 1;
+  static constexpr int NSLOT = HD == 128 ? 5 : 8;    // K/V ring slots of one tile each
+  static constexpr int OFF_Q = 0;                    // two Q tiles
+  static constexpr int OFF_KV = 2 * TILE;
+  static constexpr int OFF_BAR = OFF_KV + NSLOT * TILE;
+  // q_full, kv_full[NSLOT], kv_empty[NSLOT], s_full[2], p_full[2], o_done[2], done
+  static constexpr int NBAR = 1 + 2 * NSLOT + 7;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -74,70 +76,85 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed f32x2 arithmetic (two lanes of a 64-bit register pair per instruction).
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  lo = __uint_as_float(a);
+  hi = __uint_as_float(b);
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
   using L = FwdSmem<HD>;
+  constexpr int NSLOT = L::NSLOT;
   constexpr int ATOMS = HD / 64;           // 128-byte swizzle atoms across head_dim
   constexpr int ATOM_BYTES = 128 * 128;    // 128 rows x 128 bytes
   extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_seg_lo[2];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + NST;
-  uint64_t* s_full = bars + 1 + 2 * NST;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* done = pv_done + 1;
+  uint64_t* kv_empty = kv_full + NSLOT;
+  uint64_t* s_full = kv_empty + NSLOT;   // [2]
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_done = p_full + 2;         // [2]
+  uint64_t* done = o_done + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (a.S + BQ - 1) / BQ;
-  const int qt = n_qt - 1 - (int)blockIdx.x;   // heaviest (latest) query tiles first
+  const int n_qb = (a.S + 2 * BQ - 1) / (2 * BQ);
+  const int qb = n_qb - 1 - (int)blockIdx.x;   // heaviest (latest) query blocks first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (a.H / a.Hkv);
-  const int q0 = qt * BQ;
+  const int q0 = qb * 2 * BQ;
   const int64_t row0 = (int64_t)b * a.S;
 
-  // key tile range [kt_lo, kt_hi] for this query tile
-  int k_first = 0;
-  if (a.window > 0) k_first = max(0, q0 - (a.window - 1));
-  if (a.seg_start != nullptr) {
-    int lo = 0x7fffffff;
-    for (int r = threadIdx.x; r < BQ; r += blockDim.x) {
-      const int q = q0 + r;
-      if (q < a.S) {
-        const int st = __ldg(a.seg_start + row0 + q);
-        if (st >= 0) lo = min(lo, st);
-      }
+  // key tile range [lo_t, hi_t] of each query tile (cnt_t = 0: the tile is past the sequence)
+  if (threadIdx.x < 2) s_seg_lo[threadIdx.x] = 0x7fffffff;
+  __syncthreads();
+  if (a.seg_start != nullptr && threadIdx.x < 2 * BQ) {
+    const int q = q0 + (int)threadIdx.x;
+    if (q < a.S) {
+      const int st = __ldg(a.seg_start + row0 + q);
+      if (st >= 0) atomicMin(&s_seg_lo[threadIdx.x / BQ], st);
     }
-    __shared__ int s_lo;
-    if (threadIdx.x == 0) s_lo = 0x7fffffff;
-    __syncthreads();
-    atomicMin(&s_lo, lo);
-    __syncthreads();
-    if (s_lo != 0x7fffffff) k_first = max(k_first, s_lo);
   }
-  const int kt_lo = k_first / BKV;
-  const int kt_hi = min(q0 + BQ - 1, a.S - 1) / BKV;
-  const int n_kv = kt_hi - kt_lo + 1;
-
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < NST; ++s) {
+    for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);   // one release per query tile
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
     mbar_init(done, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -150,76 +167,139 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  int lo[2], hi[2], cnt[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qt0 = q0 + t * BQ;
+    if (qt0 >= a.S) {
+      lo[t] = 0;
+      hi[t] = -1;
+      cnt[t] = 0;
+      continue;
+    }
+    int kf = a.window > 0 ? max(0, qt0 - (a.window - 1)) : 0;
+    if (a.seg_start != nullptr && s_seg_lo[t] != 0x7fffffff) kf = max(kf, s_seg_lo[t]);
+    lo[t] = kf / BKV;
+    hi[t] = min(qt0 + BQ - 1, a.S - 1) / BKV;
+    cnt[t] = hi[t] - lo[t] + 1;
+  }
+  const int ulo = cnt[0] > 0 ? lo[0] : lo[1];
+  const int uhi = cnt[1] > 0 ? max(hi[0], hi[1]) : hi[0];
   constexpr uint32_t IDESC_S = idesc_f16(128, 128, 1, 0, 0);
   constexpr uint32_t IDESC_PV = idesc_f16(128, HD, 1, 0, 1);
 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t issued = 0, par = 0;
-      mbar_arrive_expect_tx(q_full, L::TILE);
+      const int nq = cnt[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * L::TILE);
+      for (int t = 0; t < nq; ++t)
 #pragma unroll
-      for (int at = 0; at < ATOMS; ++at)
-        tma_load_2d(smem + L::OFF_Q + at * ATOM_BYTES, &tmQ, q_full, h * HD + at * 64, (int)(row0 + q0));
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % NST;
-        if (!mbar_wait(&kv_empty[st], ((j / NST) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
-        uint8_t* kb = smem + L::OFF_KV + st * 2 * L::TILE;
-        uint8_t* vb = kb + L::TILE;
-        const int krow = (int)(row0 + (kt_lo + j) * BKV);
-        mbar_arrive_expect_tx(&kv_full[st], 2 * L::TILE);
+        for (int at = 0; at < ATOMS; ++at)
+          tma_load_2d(smem + L::OFF_Q + t * L::TILE + at * ATOM_BYTES, &tmQ, q_full, h * HD + at * 64,
+                      (int)(row0 + q0 + t * BQ));
+      int item = 0;
+      bool ok = true;
+      for (int j = ulo; ok && j <= uhi; ++j) {
+        const bool need = (j >= lo[0] && j <= hi[0]) || (j >= lo[1] && j <= hi[1]);
+        if (!need) continue;
+        const int krow = (int)(row0 + j * BKV);
 #pragma unroll
-        for (int at = 0; at < ATOMS; ++at) {
-          tma_load_2d(kb + at * ATOM_BYTES, &tmK, &kv_full[st], hk * HD + at * 64, krow);
-          tma_load_2d(vb + at * ATOM_BYTES, &tmV, &kv_full[st], hk * HD + at * 64, krow);
+        for (int kv = 0; kv < 2; ++kv, ++item) {
+          const int st = item % NSLOT;
+          if (!mbar_wait(&kv_empty[st], ((item / NSLOT) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + L::OFF_KV + st * L::TILE;
+          mbar_arrive_expect_tx(&kv_full[st], L::TILE);
+#pragma unroll
+          for (int at = 0; at < ATOMS; ++at)
+            tma_load_2d(dst + at * ATOM_BYTES, kv == 0 ? &tmK : &tmV, &kv_full[st], hk * HD + at * 64, krow);
+          issued |= 1u << st;
+          par = (par & ~(1u << st)) | ((uint32_t)((item / NSLOT) & 1) << st);
         }
-        issued |= 1u << st;
-        par = (par & ~(1u << st)) | ((uint32_t)((j / NST) & 1) << st);
       }
       mbar_wait(q_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < NST; ++s)
+      for (int s = 0; s < NSLOT; ++s)
         if (issued & (1u << s)) mbar_wait(&kv_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
     bool ok = warp_wait(q_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
+    int u[2] = {0, 0};       // key tiles whose S MMA has been issued, per query tile
+    int vit[2] = {0, 0};     // ring item of the V tile the pending PV product reads
     bool issued_any = false;
-    for (int j = 0; ok && j <= n_kv; ++j) {
-      if (j < n_kv) {
-        const int st = j % NST, sb = j & 1;
-        if (!warp_wait(&kv_full[st], (j / NST) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        if (!warp_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+    // O_t += P_t V for the tile's previous key tile, then release that V slot for this query tile
+    auto pv = [&](int t) -> bool {
+      if (!warp_wait(&p_full[t], (u[t] - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) return false;
+      const int vi = vit[t], vs = vi % NSLOT;
+      if (!warp_wait(&kv_full[vs], (vi / NSLOT) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t va = smem_u32(smem + L::OFF_KV + vs * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          tc_mma_f16_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, smem_desc(va + kk * 2048, ATOM_BYTES, 1024, 2),
+                        IDESC_PV, (u[t] > 1 || kk > 0) ? 1u : 0u);
+        tc_commit(&kv_empty[vs]);
+      }
+      __syncwarp();
+      return true;
+    };
+    int item = 0;
+    for (int j = ulo; ok && j <= uhi; ++j) {
+      const bool in0 = j >= lo[0] && j <= hi[0], in1 = j >= lo[1] && j <= hi[1];
+      if (!in0 && !in1) continue;
+      const int ik = item, iv = item + 1;
+      item += 2;
+      const int ks = ik % NSLOT;
+      if (!warp_wait(&kv_full[ks], (ik / NSLOT) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const bool in = t == 0 ? in0 : in1;
+        if (!in) {
+          // this query tile never reads V_j: its share of the slot's release now
+          if (lane == 0) tc_commit(&kv_empty[iv % NSLOT]);
+          __syncwarp();
+          continue;
+        }
+        if (u[t] > 0 && !pv(t)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t qa = smem_u32(smem + L::OFF_Q);
-          const uint32_t ka = smem_u32(smem + L::OFF_KV + st * 2 * L::TILE);
+          const uint32_t qa = smem_u32(smem + L::OFF_Q + t * L::TILE);
+          const uint32_t ka = smem_u32(smem + L::OFF_KV + ks * L::TILE);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk / 4) * ATOM_BYTES + (kk % 4) * 32;
-            tc_mma_f16(tmem + sb * 128, smem_desc(qa + off, 16, 1024, 2), smem_desc(ka + off, 16, 1024, 2),
-                       IDESC_S, kk > 0 ? 1u : 0u);
+            tc_mma_f16(tmem + t * 128, smem_desc(qa + off, 16, 1024, 2), smem_desc(ka + off, 16, 1024, 2), IDESC_S,
+                       kk > 0 ? 1u : 0u);
           }
-          tc_commit(&s_full[sb]);
+          tc_commit(&s_full[t]);
           issued_any = true;
         }
         __syncwarp();
+        ++u[t];
+        vit[t] = iv;
       }
-      if (j >= 1) {
-        const int jj = j - 1, st = jj % NST;
-        if (!warp_wait(p_full, jj & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t pa = smem_u32(smem + L::OFF_P);
-          const uint32_t va = smem_u32(smem + L::OFF_KV + st * 2 * L::TILE + L::TILE);
+      if (!ok) break;
+      // K_j: both query tiles' S products read it
+      if (lane == 0) {
+        tc_commit(&kv_empty[ks]);
+        tc_commit(&kv_empty[ks]);
+      }
+      __syncwarp();
+    }
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint64_t ad = smem_desc(pa + (kk / 4) * ATOM_BYTES + (kk % 4) * 32, 16, 1024, 2);
-            const uint64_t bd = smem_desc(va + kk * 2048, ATOM_BYTES, 1024, 2);
-            tc_mma_f16(tmem + 256, ad, bd, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(pv_done);
-          tc_commit(&kv_empty[st]);
-        }
-        __syncwarp();
-      }
+    for (int t = 0; t < 2; ++t) {
+      if (ok && u[t] > 0) ok = pv(t);
+      if (lane == 0) tc_commit(&o_done[t]);
+      __syncwarp();
     }
     if (lane == 0 && issued_any) {
       tc_commit(done);
@@ -227,114 +307,146 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int q = q0 + r;
+    const int qt0 = q0 + t * BQ;
+    const int q = qt0 + r;
     const bool qvalid = q < a.S;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t ts = tmem + lane_base + t * 128;
+    const int n = cnt[t];
     int qseg = 0;
     if (a.seg_start != nullptr && qvalid) qseg = __ldg(a.seg_start + row0 + q);
     // running max (log2 domain, relative to which P is formed) and sum
     float m_used = -INFINITY, l = 0.f;
-    if (a.k_sink != nullptr && qvalid) {
-      const __nv_bfloat16* qr = a.q + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
-      float dot = 0.f;
-      for (int c = 0; c < HD; ++c) {
-        const float ks = a.sink_dtype == ZS_F32 ? reinterpret_cast<const float*>(a.k_sink)[h * HD + c]
-                                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[h * HD + c]);
-        dot = fmaf(__bfloat162float(qr[c]), ks, dot);
+    bool ok = n > 0;
+    if (ok && a.k_sink != nullptr) {
+      // sink logit from this row of the Q tile in shared memory (swizzled 16-byte chunks)
+      ok = warp_wait(q_full, 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE);
+      if (ok && qvalid) {
+        const uint8_t* qrow = smem + L::OFF_Q + t * L::TILE + r * 128;
+        float dot = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < HD / 8; ++ch) {
+          const uint4 v = *reinterpret_cast<const uint4*>(qrow + (ch >> 3) * ATOM_BYTES + (((ch & 7) ^ (r & 7)) * 16));
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[x]));
+            const int c = ch * 8 + 2 * x;
+            float k0, k1;
+            if (a.sink_dtype == ZS_F32) {
+              k0 = reinterpret_cast<const float*>(a.k_sink)[h * HD + c];
+              k1 = reinterpret_cast<const float*>(a.k_sink)[h * HD + c + 1];
+            } else {
+              k0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[h * HD + c]);
+              k1 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[h * HD + c + 1]);
+            }
+            dot = fmaf(f.x, k0, dot);
+            dot = fmaf(f.y, k1, dot);
+          }
+        }
+        m_used = dot * a.scale_log2;
+        l = 1.f;
       }
-      m_used = dot * a.scale_log2;
-      l = 1.f;
     }
-    bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(&s_full[sb], (j >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+    const uint64_t scale2 = pack2(__float_as_uint(a.scale_log2), __float_as_uint(a.scale_log2));
+    for (int uu = 0; uu < n && ok; ++uu) {
+      const int j = lo[t] + uu;
+      if (!warp_wait(&s_full[t], uu & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t sr[128];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld_32x32b_x32(tmem + lane_base + sb * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(ts + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-      const int k0 = (kt_lo + j) * BKV;
-      float mx = -INFINITY;
+      const int k0 = j * BKV;
+      const bool edge = (k0 + BKV - 1 > qt0) || (qt0 + BQ - 1 >= a.S) || a.seg_start != nullptr ||
+                        (a.window > 0 && qt0 + BQ - 1 - k0 >= a.window);
+      if (edge) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const int k = k0 + c;
-        bool vis = qvalid && k <= q;
-        if (a.window > 0) vis = vis && (q - k < a.window);
-        if (a.seg_start != nullptr) vis = vis && (k >= qseg) && qseg >= 0;
-        const float t = vis ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
-        sr[c] = __float_as_uint(t);
-        mx = fmaxf(mx, t);
+        for (int c = 0; c < 128; ++c) {
+          const int k = k0 + c;
+          bool vis = qvalid && k <= q;
+          if (a.window > 0) vis = vis && (q - k < a.window);
+          if (a.seg_start != nullptr) vis = vis && (k >= qseg) && qseg >= 0;
+          if (!vis) sr[c] = __float_as_uint(-INFINITY);
+        }
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+        mx0 = fmax3(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = fmax3(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = fmax3(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + 8.0f;
-      // P_{j-1} has been consumed and O holds every earlier product once PV_{j-1} completes
-      if (j >= 1 && !warp_wait(pv_done, (j - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
       float f = 1.0f;
       if (need) {
         f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
         l *= f;
         m_used = m_new;
       }
-      if (j >= 1 && __any_sync(0xffffffffu, need)) {
-        // rescale O rows in TMEM; the access is warp-wide, lanes that keep
-        // their max scale by exactly 1
-        tc_fence_after();
+      // O_t holds every earlier product (this S_t was issued after them)
+      if (uu >= 1 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t orow[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+          tmem_ld_32x32b_x32(tmem + lane_base + 256 + t * HD + c * 32, orow);
           tc_wait_ld();
 #pragma unroll
           for (int x = 0; x < 32; ++x) orow[x] = __float_as_uint(__uint_as_float(orow[x]) * f);
-          tmem_st_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+          tmem_st_32x32b_x32(tmem + lane_base + 256 + t * HD + c * 32, orow);
         }
-        tc_wait_st();
       }
-      // P = exp2(t - m_used) -> bf16, swizzled rows of 128 bytes per 64 keys
-      uint8_t* prow = smem + L::OFF_P + r * 128;
-      // a row with every key so far masked keeps m_used = -inf and all t = -inf: P = 0
+      // P = exp2(s * scale - m_used) (a row with every key so far masked keeps
+      // m_used = -inf and all s = -inf: P = 0)
       const float mu = m_used == -INFINITY ? 0.f : m_used;
-      float rs = 0.f;
+      const uint64_t negm = pack2(__float_as_uint(-mu), __float_as_uint(-mu));
+      uint64_t acc0 = 0, acc1 = 0;
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t w[4];
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pw[32];
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const float p0 = fast_exp2(__uint_as_float(sr[ch * 8 + 2 * x]) - mu);
-          const float p1 = fast_exp2(__uint_as_float(sr[ch * 8 + 2 * x + 1]) - mu);
-          __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-          const float2 back = __bfloat1622float2(pp);
-          rs += back.x + back.y;
-          w[x] = *reinterpret_cast<uint32_t*>(&pp);
+        for (int x = 0; x < 32; x += 2) {
+          const int c = hf * 64 + 2 * x;
+          float e0, e1, e2, e3;
+          unpack2(ffma2(pack2(sr[c], sr[c + 1]), scale2, negm), e0, e1);
+          unpack2(ffma2(pack2(sr[c + 2], sr[c + 3]), scale2, negm), e2, e3);
+          e0 = fast_exp2(e0);
+          e1 = fast_exp2(e1);
+          e2 = fast_exp2(e2);
+          e3 = fast_exp2(e3);
+          acc0 = fadd2(acc0, pack2(__float_as_uint(e0), __float_as_uint(e1)));
+          acc1 = fadd2(acc1, pack2(__float_as_uint(e2), __float_as_uint(e3)));
+          __nv_bfloat162 p01 = __floats2bfloat162_rn(e0, e1), p23 = __floats2bfloat162_rn(e2, e3);
+          pw[x] = *reinterpret_cast<uint32_t*>(&p01);
+          pw[x + 1] = *reinterpret_cast<uint32_t*>(&p23);
         }
-        const int atom = ch >> 3, c16 = ch & 7;
-        *reinterpret_cast<uint4*>(prow + atom * ATOM_BYTES + ((c16 ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st_32x32b_x32(ts + hf * 32, pw);
       }
-      l += rs;
-      fence_proxy_async_smem();
+      float a0, a1, a2, a3;
+      unpack2(acc0, a0, a1);
+      unpack2(acc1, a2, a3);
+      l += (a0 + a1) + (a2 + a3);
+      tc_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[t]);
     }
-    if (ok && n_kv > 0 && warp_wait(pv_done, (n_kv - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+    if (ok && warp_wait(&o_done[t], 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __nv_bfloat16* orow_g = a.o + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t orow[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 256 + c * 32, orow);
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + t * HD + c * 32, orow);
         tc_wait_ld();
         if (qvalid) {
           uint4* dst = reinterpret_cast<uint4*>(orow_g + c * 32);
@@ -395,18 +507,17 @@ extern "C" int zs_attention_forward(const void* q, const void* k, const void* v,
   a.seg_start = seg_start;
   a.k_sink = k_sink;
   a.sink_dtype = sink_dtype;
-  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
   a.o = reinterpret_cast<__nv_bfloat16*>(o);
   a.lse = lse;
-  dim3 grid((S + attn::BQ - 1) / attn::BQ, H, B);
+  dim3 grid((S + 2 * attn::BQ - 1) / (2 * attn::BQ), H, B);
   if (hd == 128) {
     using L = attn::FwdSmem<128>;
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
-    attn::attn_fwd_kernel<128><<<grid, 192, L::ALLOC, stream>>>(tq, tk, tv, a);
+    attn::attn_fwd_kernel<128><<<grid, 320, L::ALLOC, stream>>>(tq, tk, tv, a);
   } else {
     using L = attn::FwdSmem<64>;
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
-    attn::attn_fwd_kernel<64><<<grid, 192, L::ALLOC, stream>>>(tq, tk, tv, a);
+    attn::attn_fwd_kernel<64><<<grid, 320, L::ALLOC, stream>>>(tq, tk, tv, a);
   }
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;

@@ -102,10 +102,19 @@ class GatedAttention(nn.Module):
             position_ids = torch.arange(seq_len, device=hidden_states.device).expand(bsz, seq_len)
         # q, k, v and the head gate read the same input: one GEMM over the
         # concatenated weights (the input is cast once, and its gradient is one
-        # f32-accumulated product instead of a sum of four)
+        # f32-accumulated product instead of a sum of four).  Zero rows pad the
+        # output width to a multiple of 16 so every output row starts on a
+        # 32-byte boundary (an odd width sends cuBLAS to unaligned kernels).
         qd, kd = self.num_heads * self.head_dim, self.num_key_value_heads * self.head_dim
-        w_cat = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.head_gate_proj.weight], 0)
-        q, k, v, gate_logits = torch.split(F.linear(hidden_states, w_cat), [qd, kd, kd, self.num_heads], dim=-1)
+        n_out = qd + 2 * kd + self.num_heads
+        pad = -n_out % 16
+        ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.head_gate_proj.weight]
+        if pad:
+            ws.append(self.q_proj.weight.new_zeros(pad, self.hidden_size))
+        w_cat = torch.cat(ws, 0)
+        q, k, v, gate_logits = torch.split(F.linear(hidden_states, w_cat), [qd, kd, kd, self.num_heads + pad],
+                                           dim=-1)
+        gate_logits = gate_logits[..., : self.num_heads]
         q = q.reshape(bsz, seq_len, self.num_heads, self.head_dim)
         k = k.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
         v = v.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
