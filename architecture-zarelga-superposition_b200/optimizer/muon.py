@@ -15,6 +15,7 @@ has host syncs, so a whole step can be captured in a CUDA graph.
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from zs_b200 import _lib as Z
@@ -209,9 +210,41 @@ def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axi
         p.copy_(W.to(p.dtype))
 
 
-def _zeropower_many(Xs, steps):
+def _world(process_group):
+    """(world size, rank) of process_group; (1, 0) when it is None or torch.distributed is not initialised."""
+    if process_group is None or not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(process_group), dist.get_rank(process_group)
+
+
+def _ns_sharded(stack, steps, process_group, ns):
+    """Newton-Schulz of the matrices stack[0..b) split over the ranks of process_group:
+    rank r orthogonalises matrices [r*per, (r+1)*per) (per = ceil(b / world)), and one
+    all_gather_into_tensor assembles the bf16 results on every rank.  Every rank must
+    call this with the same stack shape (data-parallel ranks hold the same reduced
+    gradients, so the optimizer state and the Newton-Schulz inputs are identical)."""
+    world, rank = _world(process_group)
+    if world == 1:
+        return ns(stack, steps)
+    b = stack.size(0)
+    per = -(-b // world)
+    lo, hi = min(rank * per, b), min((rank + 1) * per, b)
+    mine = torch.zeros((per,) + tuple(stack.shape[1:]), dtype=torch.bfloat16, device=stack.device)
+    if hi > lo:
+        mine[:hi - lo].copy_(ns(stack[lo:hi], steps))
+    full = torch.empty((per * world,) + tuple(stack.shape[1:]), dtype=torch.bfloat16, device=stack.device)
+    dist.all_gather_into_tensor(full, mine, group=process_group)
+    return full[:b]
+
+
+def _zeropower_many(Xs, steps, process_group=None, ns=None):
     """zeropower_via_newtonschulz5 of every tensor in Xs; matrices of one oriented shape
-    (and step count) from different tensors share batched launches."""
+    (and step count) from different tensors share batched launches.  With a
+    process group of more than one rank, each batch is split over the ranks and
+    the orthogonalised matrices are all-gathered (_ns_sharded).  `ns` replaces the
+    Newton-Schulz function (default: the libzs kernels)."""
+    ns = zeropower_via_newtonschulz5 if ns is None else ns
+    world, _ = _world(process_group)
     out = [None] * len(Xs)
     groups = {}
     for i, (X, st) in enumerate(zip(Xs, steps)):
@@ -229,7 +262,7 @@ def _zeropower_many(Xs, steps):
                 Xo = X.mT if X.shape[-2] > X.shape[-1] else X
                 parts.append(Xo.reshape(-1, mm, nn))
             stack = parts[0] if len(parts) == 1 else torch.cat(parts, 0)
-            Y = zeropower_via_newtonschulz5(stack, st)
+            Y = _ns_sharded(stack, st, process_group, ns)
             off = 0
             for i, part in zip(chunk, parts):
                 X = Xs[i]
@@ -242,12 +275,12 @@ def _zeropower_many(Xs, steps):
 
         for i in idx:
             b = Xs[i].numel() // (mm * nn)
-            # a stack of 32+ matrices fills the GPU on its own; small ones are merged up to
-            # 64 matrices (and about 1 GiB of Newton-Schulz workspace) per launch
-            if b >= 32:
+            # a stack of 32+ matrices per rank fills the GPU on its own; small ones are merged
+            # up to 64 matrices per rank (and about 1 GiB of Newton-Schulz workspace) per launch
+            if b >= 32 * world:
                 flush([i])
                 continue
-            if chunk and (batch + b > 64 or (batch + b) * mm * (2 * mm + nn) * 2 > (1 << 30)):
+            if chunk and (batch + b > 64 * world or (batch + b) * mm * (2 * mm + nn) * 2 > (1 << 30) * world):
                 flush(chunk)
                 chunk, batch = [], 0
             chunk.append(i)
@@ -270,19 +303,147 @@ def md_decoupled_step(p, grad, state, *, lr, momentum, gain_lr, gain_betas, gain
              norm_axis=norm_axis, rescale_mode=rescale_mode)
 
 
-def md_decoupled_steps(jobs, states):
+def md_decoupled_steps(jobs, states, process_group=None):
     """md_decoupled_step for many parameters at once: jobs = [(p, hyper-parameter dict)].
     Same result per parameter; the Newton-Schulz launches are shared across parameters
-    whose matrices have the same shape."""
+    whose matrices have the same shape.  With a process group, every rank runs the
+    element-wise passes on all parameters (their state stays replicated) and the
+    Newton-Schulz batches are split over the ranks and all-gathered."""
     pre = []
     for p, hp in jobs:
         Z.require_cuda(p, p.grad)
         pre.append(_md_pre(p, p.grad, states[p], momentum=hp["momentum"], gain_mode=hp["gain_mode"],
                            norm_axis=hp["norm_axis"], capturable=hp["capturable"]))
-    Us = _zeropower_many([x for _, _, x in pre], [hp["ns_steps"] for _, hp in jobs])
+    Us = _zeropower_many([x for _, _, x in pre], [hp["ns_steps"] for _, hp in jobs], process_group)
     for (p, hp), (W, red, _), U in zip(jobs, pre, Us):
         _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
                  gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"])
+
+
+def _muon_steps(jobs, states, process_group=None):
+    """muon_update + the decoupled-weight-decay apply of the reference's Muon optimizers
+    (optimizer/muon.py:35-42, :83-93) for jobs = [(p, group)], with the Newton-Schulz
+    launches batched across same-shape matrices and, with a process group, split over
+    its ranks.  Parameters without a gradient get a zero one, as the reference does."""
+    ups = []
+    for p, group in jobs:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+        state = states[p]
+        if len(state) == 0:
+            state["momentum_buffer"] = torch.zeros_like(p)
+        buf = state["momentum_buffer"]
+        buf.lerp_(p.grad, 1 - group["momentum"])
+        u = p.grad.lerp_(buf, group["momentum"])
+        ups.append(u.view(len(u), -1) if u.ndim == 4 else u)
+    Us = _zeropower_many(ups, [5] * len(ups), process_group)
+    for (p, group), U in zip(jobs, Us):
+        U *= max(1, p.grad.size(-2) / p.grad.size(-1)) ** 0.5
+        p.mul_(1 - group["lr"] * group["weight_decay"])
+        _scaled_add_(p, U.reshape(p.shape), group["lr"])
+
+
+def _adam_steps(group, states):
+    """AdamW with decoupled weight decay for an aux-Adam group (optimizer/muon.py:226-240)."""
+    for p in group["params"]:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+        state = states[p]
+        if len(state) == 0:
+            state["exp_avg"] = torch.zeros_like(p)
+            state["exp_avg_sq"] = torch.zeros_like(p)
+            state["step"] = 0
+        state["step"] += 1
+        update = adam_update(p.grad, state["exp_avg"], state["exp_avg_sq"], state["step"], group["betas"],
+                             group["eps"])
+        p.mul_(1 - group["lr"] * group["weight_decay"])
+        _scaled_add_(p, update, group["lr"])
+
+
+def _muon_group_defaults(group):
+    group.setdefault("lr", 0.02)
+    group.setdefault("momentum", 0.95)
+    group.setdefault("weight_decay", 0)
+    assert set(group.keys()) == {"params", "lr", "momentum", "weight_decay", "use_muon"}
+
+
+def _adam_group_defaults(group):
+    group.setdefault("lr", 3e-4)
+    group.setdefault("betas", (0.9, 0.95))
+    group.setdefault("eps", 1e-10)
+    group.setdefault("weight_decay", 0)
+    assert set(group.keys()) == {"params", "lr", "betas", "eps", "weight_decay", "use_muon"}
+
+
+class SingleDeviceMuon(torch.optim.Optimizer):
+    """Muon (optimizer/muon.py:100-128): SGD-momentum with Nesterov, Newton-Schulz
+    orthogonalised update scaled by sqrt(max(1, rows/cols)), decoupled weight decay."""
+
+    process_group = None
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95):
+        super().__init__(params, dict(lr=lr, weight_decay=weight_decay, momentum=momentum))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        _muon_steps([(p, g) for g in self.param_groups for p in g["params"]], self.state, self.process_group)
+        return loss
+
+
+class Muon(SingleDeviceMuon):
+    """Distributed Muon (optimizer/muon.py:45-97), same arguments and result.  The
+    reference gives each rank every world-th parameter and all-gathers the updated
+    parameters; here every rank keeps the (replicated) momentum of all parameters,
+    the Newton-Schulz matrices are split over the ranks in equal slices, and the
+    bf16 orthogonalised updates are all-gathered (half the bytes of f32 weights).
+    Uses the default process group unless one is given."""
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95, process_group=None):
+        assert isinstance(params, list) and len(params) >= 1 and isinstance(params[0], torch.nn.Parameter)
+        params = sorted(params, key=lambda x: x.size(), reverse=True)
+        super().__init__(params, lr=lr, weight_decay=weight_decay, momentum=momentum)
+        self.process_group = dist.group.WORLD if process_group is None else process_group
+
+
+class SingleDeviceMuonWithAuxAdam(torch.optim.Optimizer):
+    """Muon for groups with use_muon=True, AdamW for the rest (optimizer/muon.py:244-336)."""
+
+    process_group = None
+
+    def __init__(self, param_groups):
+        for group in param_groups:
+            assert "use_muon" in group
+            (_muon_group_defaults if group["use_muon"] else _adam_group_defaults)(group)
+        super().__init__(param_groups, dict())
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        _muon_steps([(p, g) for g in self.param_groups if g["use_muon"] for p in g["params"]], self.state,
+                    self.process_group)
+        for group in self.param_groups:
+            if not group["use_muon"]:
+                _adam_steps(group, self.state)
+        return loss
+
+
+class MuonWithAuxAdam(SingleDeviceMuonWithAuxAdam):
+    """Distributed MuonWithAuxAdam (optimizer/muon.py:154-241): Newton-Schulz split over
+    the ranks as in Muon; the Adam groups run replicated on every rank."""
+
+    def __init__(self, param_groups, process_group=None):
+        for group in param_groups:
+            if group.get("use_muon"):
+                group["params"] = sorted(group["params"], key=lambda x: x.size(), reverse=True)
+        super().__init__(param_groups)
+        self.process_group = dist.group.WORLD if process_group is None else process_group
 
 
 _MD_KEYS = {"params", "lr", "momentum", "gain_lr", "gain_betas", "gain_eps", "gain_mode", "norm_axis", "ns_steps",
@@ -309,7 +470,7 @@ class SingleDeviceMuonMD(torch.optim.Optimizer):
                     continue
                 assert p.ndim >= 2, "MD decoupling needs a matrix or a stack of matrices (>=2D)"
                 jobs.append((p, group))
-        md_decoupled_steps(jobs, self.state)
+        md_decoupled_steps(jobs, self.state, getattr(self, "process_group", None))
         return loss
 
 
@@ -338,7 +499,8 @@ class SingleDeviceMuonMDWithAuxAdam(torch.optim.Optimizer):
             with torch.enable_grad():
                 loss = closure()
         md_decoupled_steps([(p, group) for group in self.param_groups if group["use_muon"]
-                            for p in group["params"] if p.grad is not None], self.state)
+                            for p in group["params"] if p.grad is not None], self.state,
+                           getattr(self, "process_group", None))
         for group in self.param_groups:
             for p in group["params"]:
                 if p.grad is None or group["use_muon"]:
@@ -355,3 +517,17 @@ class SingleDeviceMuonMDWithAuxAdam(torch.optim.Optimizer):
                 p.mul_(1 - group["lr"] * group["weight_decay"])
                 _scaled_add_(p, update, group["lr"])
         return loss
+
+
+class MuonMDWithAuxAdam(SingleDeviceMuonMDWithAuxAdam):
+    """Data-parallel SingleDeviceMuonMDWithAuxAdam (no counterpart in the reference,
+    which trains on one device): the ranks hold identical all-reduced gradients, so
+    each keeps the full MuonMD/Adam state and runs the element-wise passes; the
+    Newton-Schulz batches -- most of the step's cost -- are split over the ranks and
+    the bf16 orthogonalised matrices all-gathered (the ownership + all-gather pattern
+    of the reference's distributed Muon, optimizer/muon.py:82-95).  Parameters end
+    bit-identical on every rank and to the single-device optimizer."""
+
+    def __init__(self, param_groups, process_group=None):
+        super().__init__(param_groups)
+        self.process_group = dist.group.WORLD if process_group is None else process_group

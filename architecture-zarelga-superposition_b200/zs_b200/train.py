@@ -65,15 +65,17 @@ def enable_fused_weight_grad(model, enabled=True):
 
 def build_muonmd_optimizer(model, device, muon_lr=0.02, adam_lr=3e-4, momentum=0.95, gain_lr=1e-3,
                            adam_betas=(0.9, 0.95), adam_eps=1e-16, embedding_weight_decay=0.1, embedding_lr=3e-3,
-                           embedding_beta=0.9, capture_warmup_steps=5, enable_cuda_graph=True):
+                           embedding_beta=0.9, capture_warmup_steps=5, enable_cuda_graph=True, process_group=None):
     """Groups: Muon (Frobenius sphere) for matrices and expert stacks; the router
     on row spheres with column gains and the Muon shape factor; AdamW with weight
     decay for the output head; Adam for 1-D params; GramReaperSparse (unit rows)
     for the sparse input embedding.  Dense LRs are 0-dim device tensors so the
-    captured step reads scheduler updates."""
+    captured step reads scheduler updates.  With a data-parallel process group the
+    dense optimizer is MuonMDWithAuxAdam (Newton-Schulz split over the ranks and
+    all-gathered) and runs eagerly, so no CUDA graph holds the collectives."""
     from engram.GramReaperSparse import GramReaperSparse
     from optimizer.hybrid import HybridGraphOptimizer
-    from optimizer.muon import SingleDeviceMuonMDWithAuxAdam
+    from optimizer.muon import MuonMDWithAuxAdam, SingleDeviceMuonMDWithAuxAdam
 
     emb = model.embedding.weight
     muon, router, head, scalar = [], [], [], []
@@ -96,11 +98,12 @@ def build_muonmd_optimizer(model, device, muon_lr=0.02, adam_lr=3e-4, momentum=0
                            weight_decay=embedding_weight_decay, capturable=True))
     groups.append(dict(params=scalar, use_muon=False, lr=t(adam_lr), betas=adam_betas, eps=adam_eps, weight_decay=0.0,
                        capturable=True))
-    dense = SingleDeviceMuonMDWithAuxAdam(groups)
+    sharded = process_group is not None and torch.distributed.get_world_size(process_group) > 1
+    dense = MuonMDWithAuxAdam(groups, process_group) if sharded else SingleDeviceMuonMDWithAuxAdam(groups)
     sparse = GramReaperSparse([dict(params=[emb], unit_norm=True)], lr=float(embedding_lr), beta=embedding_beta,
                               unit_norm=True)
     return HybridGraphOptimizer(dense, sparse, capture_warmup_steps=capture_warmup_steps,
-                                enable_cuda_graph=enable_cuda_graph)
+                                enable_cuda_graph=enable_cuda_graph and not sharded)
 
 
 def _lr_value(lr):

@@ -527,7 +527,9 @@ def run_config4(args):
     torch.manual_seed(1234)
     model = MoEModel(cfg).to(dev)
     enable_fused_weight_grad(model)
-    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3)
+    # with N ranks the Newton-Schulz batches are split over the ranks (all-gathered)
+    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3,
+                                 process_group=dist.group.WORLD if world > 1 else None)
     reducer = None
     if world > 1:
         from zs_b200.dp import GradAllReducer
