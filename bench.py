@@ -618,6 +618,119 @@ def run_config4(args):
         dist.destroy_process_group()
 
 
+def run_config5(args):
+    """BASELINE configs[4]'s MoE layer, expert parallel: 128 routed SwiGLU experts of
+    ffn 1024 at d_model 2048, top-8, split evenly over the N ranks (16 per GPU at N=8),
+    32768 latent positions per GPU; a step = sigmoid + biased top-k routing ->
+    dispatch all-to-all -> local grouped GEMMs -> combine all-to-all, forward and
+    backward (ExpertParallelGLUMLP).  Router logits N(0,1) + bias N(0,0.1), expert
+    weights N(0,0.02), upstream gradient N(0,1), as config 2."""
+    import torch
+    import torch.distributed as dist
+
+    from modeling.moe_gate import GateTopK
+    from scattermoe.expert_parallel import ExpertParallelGLUMLP
+    from zs_b200 import _lib as Z
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo", timeout=datetime.timedelta(seconds=180),
+                            device_id=dev, init_method=None if world > 1 else f"tcp://127.0.0.1:{_free_port()}",
+                            world_size=world, rank=rank)
+    T = args.tokens or 32768
+    d, E, k, f = 2048, 128, 8, 1024
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    bf = torch.bfloat16
+    logits = torch.randn(T, E, device=dev, generator=g).to(bf)
+    bias = torch.randn(E, device=dev, generator=torch.Generator(device=dev).manual_seed(7)) * 0.1
+    x = torch.randn(T, d, device=dev, generator=g).to(bf)
+    dy = torch.randn(T, d, device=dev, generator=g).to(bf)
+    m = ExpertParallelGLUMLP(d, f, E, k).to(dev)
+    wg = torch.Generator(device=dev).manual_seed(99 + rank)
+    with torch.no_grad():
+        m.experts.weight.copy_(torch.randn(m.experts.weight.shape, device=dev, generator=wg) * 0.02)
+        m.output_experts.weight.copy_(torch.randn(m.output_experts.weight.shape, device=dev, generator=wg) * 0.02)
+    m = m.to(bf)
+    m.fuse_weight_grad = True
+    params = [m.experts.weight, m.output_experts.weight]
+
+    def step(xs, ls, dys):
+        for p_ in params:
+            p_.grad = None
+        xs.requires_grad_(True)
+        ls.requires_grad_(True)
+        idx, w = GateTopK.apply(torch.sigmoid(ls), bias, k)
+        y = m(xs, w, idx)
+        y.backward(dys)
+        return xs.grad
+
+    for _ in range(max(args.warmup, 3)):
+        step(x.detach(), logits.detach(), dy)
+    torch.cuda.synchronize()
+    dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.5)
+    Z.INSTR.events = {}
+    Z.INSTR.timing = True
+    l0 = Z.INSTR.launches
+    stream = torch.cuda.current_stream()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ht0 = time.time()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(x.detach(), logits.detach(), dy)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ht1 = time.time()
+    Z.INSTR.timing = False
+    clocks = sampler.stop(ht0, ht1)
+    ms = t0.elapsed_time(t1)
+    tt = torch.tensor([ms], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    kern = {}
+    for name, evs in Z.INSTR.events.items():
+        durs = [s.elapsed_time(e) for s, e in evs]
+        kern[name] = {"launches": len(durs), "avg_ms": sum(durs) / len(durs), "total_ms": sum(durs)}
+    gemm_ms = sum(v["total_ms"] for v in kern.values())
+    err = Z.device_error()
+    if rank == 0:
+        burst, sustained, hbm, src = measured_peaks()
+        fl = flops_per_step(T, d, E, k, f)  # per GPU: every rank's experts see T*k rows on average
+        value = world * T * args.steps / (ms * 1e-3)
+        achieved = fl * world * args.steps / (gemm_ms * 1e-3 * world) / 1e12 if gemm_ms > 0 else None
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"config5 MoE layer, expert parallel: T={T} latent positions per GPU, "
+                                       f"d=2048, E=128 ({E // world} per GPU), ffn=1024, top-8, fwd+bwd with "
+                                       "dispatch/combine all-to-all",
+                           "parallelism": f"ep{world}", "mfu_sustained_peak": value * (fl / T) / (world * sustained * 1e12)},
+                "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (rank 0's launches)",
+                             "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                             "frac": (achieved / sustained) if achieved else None, "traffic": None,
+                             "peak_source": f"{src} bf16_tflops_sustained", "kernels": kern},
+                "gpu_launches": Z.INSTR.launches - l0, "clocks": clocks, "device_error": err}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -627,7 +740,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: config 2's 16384)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4], help="BASELINE config (default 2)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5], help="BASELINE config (default 2)")
     ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
     ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
@@ -638,6 +751,8 @@ def main():
         run_config3(args)
     elif args.config == 4:
         run_config4(args)
+    elif args.config == 5:
+        run_config5(args)
     else:
         run_gpu(args)
 
