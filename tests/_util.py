@@ -1,5 +1,9 @@
+from pathlib import Path
+
 import numpy as np
 import torch
+
+GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
 
 
 def rel_err(a, b):

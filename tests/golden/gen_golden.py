@@ -153,6 +153,7 @@ def main():
     all_cases.update(gen_mcce())
     all_cases.update(gen_norm_rope())
     all_cases.update(gen_muon())
+    all_cases.update(gen_data())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
@@ -260,10 +261,6 @@ if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "norm_rope":
         print("wrote", name)
 
 
-if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") is None:
-    main()
-
-
 def gen_muon():
     """Newton-Schulz output and two MuonMD steps from the reference optimizer on CPU."""
     from optimizer import muon
@@ -298,3 +295,94 @@ if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "muon":
     for name, arrs in gen_muon().items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name)
+
+
+def _import_reference_main():
+    """The reference trainer module (main.py) with stand-ins for the two modules it
+    imports that are absent here (aim, cut_cross_entropy); only its data functions
+    are called."""
+    sys.path.insert(0, REF)
+    for name, attrs in (("aim", ("Distribution", "Run")), ("cut_cross_entropy", ("linear_cross_entropy",))):
+        if name not in sys.modules:
+            mod = types.ModuleType(name)
+            for a in attrs:
+                setattr(mod, a, None)
+            sys.modules[name] = mod
+    import main as ref_main  # noqa: E402
+    return ref_main
+
+
+def gen_data():
+    """Packed-batch and TST-batch fixtures from the reference's PackedTokenizedCollator
+    (main.py:57-129), build_token_superposition_batch (:243-352) and
+    bag_label_entropy_floor (:187-215) on seeded synthetic token lists."""
+    ref = _import_reference_main()
+    g = np.random.default_rng(11)
+    cases = {}
+    # lengths include empty, single-token, exactly max_length and over-long examples
+    for name, L, lens in (("pack_a", 64, [5, 0, 64, 30, 30, 3, 1, 70, 12, 40, 25, 2, 17, 9]),
+                          ("pack_b", 128, list(g.integers(1, 90, size=40)))):
+        examples = [{"token_ids": [int(t) for t in g.integers(2, 1000, size=n)]} for n in lens]
+        out = ref.PackedTokenizedCollator(L, 0)(examples)
+        arrs = {k: (v.numpy() if torch.is_tensor(v) else np.asarray(v)) for k, v in out.items()}
+        arrs["lens"] = np.asarray(lens)
+        arrs["tokens"] = np.concatenate([np.asarray(e["token_ids"], np.int64) for e in examples] or [np.zeros(0)])
+        arrs["L"] = np.asarray(L)
+        cases[name] = arrs
+        for sname, s_bag, latent in (("tst_a", 4, 8), ("tst_b", 3, 40)):
+            if name != "pack_b" and sname == "tst_b":
+                continue
+            tb = ref.build_token_superposition_batch(out, s_bag, latent, 0)
+            t = {k: (v.numpy() if torch.is_tensor(v) else np.asarray(v)) for k, v in tb.items()}
+            t["floor"] = ref.bag_label_entropy_floor(tb["labels"], tb["s"]).numpy()
+            t["src"] = name
+            t["s_bag"], t["latent"] = np.asarray(s_bag), np.asarray(latent)
+            cases[f"{sname}_{name}"] = t
+    return cases
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "data":
+    for name, arrs in gen_data().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name)
+
+
+CKPT_CONFIG = dict(vocab_size=128, embed_size=32, hidden_size=32, transformer_depth=2, intermediate_size=16,
+                   n_experts=5, n_shared_experts=1, n_experts_per_token=2, n_attention_heads=2, n_key_value_heads=1,
+                   attention_window_pattern=(None, None), max_position_embeddings=32, sequence_length=32,
+                   pos_rope_dims=8)
+
+
+def gen_ckpt():
+    """A checkpoint written by the reference's save_checkpoint (utils/trainutils.py:34-59)
+    for a tiny MoEModel after one step of its build_muonmd_optimizer optimizer
+    (main.py:354-465) on seeded synthetic gradients (the model's forward needs
+    flash-attn on a GPU, so the gradients are set directly)."""
+    ref = _import_reference_main()
+    from modeling.model import MoEModel
+    from modeling.model_config import ModelConfig
+    from utils.trainutils import save_checkpoint
+
+    torch.manual_seed(21)
+    model = MoEModel(ModelConfig(**CKPT_CONFIG))
+    opt = ref.build_muonmd_optimizer(model, torch.device("cpu"))
+    g = torch.Generator().manual_seed(22)
+    emb = model.embedding.weight
+    for p in model.parameters():
+        if p is emb:
+            rows = torch.tensor([[1, 5, 9, 77]])
+            p.grad = torch.sparse_coo_tensor(rows, torch.randn(4, p.size(1), generator=g), p.shape)
+        else:
+            p.grad = torch.randn(p.shape, generator=g) * 0.01
+    opt.step()
+    save_checkpoint(model, opt, str(OUT / "ckpt_ref.safetensors"), global_step=1, epoch=0)
+    print("wrote ckpt_ref.safetensors / ckpt_ref.trainer.pt")
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "ckpt":
+    gen_ckpt()
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") is None:
+    main()
+    gen_ckpt()
