@@ -183,3 +183,24 @@ class ExpertParallelGLUMLP(nn.Module):
         y_back = _AllToAll.apply(y_recv.to(x.dtype), send, recv, self.group)
         y = self._slot_sum(y_back, ssi, T, k)
         return y.view(*shape[:-1], y.size(-1))
+
+
+def shard_experts(model, process_group=None):
+    """Replace every GLUMLP in `model` by an ExpertParallelGLUMLP holding this rank's
+    slice of its experts (same module names, so parameter names are unchanged; the
+    expert weights become [E / world, ...]).  The expert weights are then rank-local:
+    a data-parallel gradient reducer must skip them.  Returns the sharded modules."""
+    from .mlp import GLUMLP
+
+    out = []
+    for parent in list(model.modules()):
+        for name, child in list(parent.named_children()):
+            if isinstance(child, GLUMLP):
+                w = child.experts.weight
+                ep = ExpertParallelGLUMLP(child.input_size, child.hidden_size, child.num_experts, child.top_k,
+                                          process_group).to(device=w.device, dtype=w.dtype)
+                ep.load_from_full(child)
+                ep.fuse_weight_grad = child.fuse_weight_grad
+                setattr(parent, name, ep)
+                out.append(ep)
+    return out

@@ -133,3 +133,51 @@ def test_expert_parallel_glumlp_matches_single_process(world, empty_rank):
         assert err is None, err
         for name, e in errs.items():
             assert e < 1e-12, f"rank {rank}: {name} differs by {e}"
+
+
+def _shard_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        from modeling.model import MoEModel
+        from modeling.model_config import ModelConfig
+        from scattermoe.expert_parallel import ExpertParallelGLUMLP, shard_experts
+
+        cfg = ModelConfig(vocab_size=64, embed_size=32, hidden_size=32, transformer_depth=2, intermediate_size=16,
+                          n_experts=9, n_shared_experts=1, n_experts_per_token=2, n_attention_heads=2,
+                          n_key_value_heads=1, attention_window_pattern=(None, None), max_position_embeddings=32,
+                          sequence_length=32, pos_rope_dims=8)
+        torch.manual_seed(0)
+        model = MoEModel(cfg)
+        full = {n: p.detach().clone() for n, p in model.named_parameters()}
+        eps = shard_experts(model)
+        ok = len(eps) == 2 and all(isinstance(l.mlp.routed_experts, ExpertParallelGLUMLP) for l in model.layers)
+        el = 8 // world
+        for n, p in model.named_parameters():
+            if "routed_experts" in n:
+                ok = ok and torch.equal(p, full[n][rank * el:(rank + 1) * el])
+            else:
+                ok = ok and torch.equal(p, full[n])
+        dist.destroy_process_group()
+        q.put((rank, ok, None))
+    except Exception:  # pragma: no cover
+        import traceback
+
+        q.put((rank, False, traceback.format_exc()))
+
+
+def test_shard_experts_module_surgery():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, err in res:
+        assert err is None, err
+        assert ok, f"rank {rank}: sharded parameters differ from the full model's slice"
