@@ -13,6 +13,10 @@
 //   md_write_kernel   reads W, U -> p = g_new * W_hat' * target / ||W_hat'||
 // Tile: 64 rows x 256 columns per block of 256 threads; warp w owns rows
 // w*8 .. w*8+7, lane owns 8 consecutive columns (two float4 per f32 operand).
+// Reductions are deterministic: each block writes its partial row / column /
+// matrix sums to a scratch slot of its own (no atomics), and md_finish_kernel
+// adds the slots in a fixed order.  Every run -- and every data-parallel
+// replica -- therefore computes bit-identical gains and projections.
 #include <initializer_list>
 #include <type_traits>
 
@@ -130,15 +134,23 @@ __device__ __forceinline__ float tile_gains(const Gains& g, int64_t l, int64_t m
 }
 
 // Pre-Newton-Schulz: buf.lerp_(g*G, 1-mom); X = lerp(g*G, buf, mom) (bf16);
-// gain gradients (before the sigmoid factor) from the old gains:
-//   red_s[l]    += sum (W/g)*G * r*c     red_r[l,i] += sum_j (W/g)*G * c*s
-//   red_c[l,j]  += sum_i (W/g)*G * r*s
+// gain gradients (before the sigmoid factor) from the old gains, as per-block
+// partial sums that md_finish_kernel adds up:
+//   red_s[l]    = sum (W/g)*G * r*c     red_r[l,i] = sum_j (W/g)*G * c*s
+//   red_c[l,j]  = sum_i (W/g)*G * r*s
+// Partial sums of one block (bx, by) of matrix l: rows [L, m, gx], columns
+// [L, gy, n], whole matrix [L, gy * gx]; md_finish_kernel reduces them.
+struct Partials {
+  float* r;
+  float* c;
+  float* s;
+};
+
 template <bool VEC>
 __global__ void __launch_bounds__(THREADS) md_pre_kernel(const float* __restrict__ W, const float* __restrict__ G,
                                                          float* __restrict__ buf, Gains gains,
-                                                         __nv_bfloat16* __restrict__ X, float* __restrict__ red_s,
-                                                         float* __restrict__ red_r, float* __restrict__ red_c,
-                                                         int64_t m, int64_t n, float mom) {
+                                                         __nv_bfloat16* __restrict__ X, Partials part, bool want_s,
+                                                         bool want_r, bool want_c, int64_t m, int64_t n, float mom) {
   __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
   const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
   const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c);
@@ -178,24 +190,36 @@ __global__ void __launch_bounds__(THREADS) md_pre_kernel(const float* __restrict
       store8<VEC>(buf + off, c, n, b);
       store8_bf16<VEC>(X + off, c, n, x);
     }
-    if (red_r != nullptr) {
+    if (want_r) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-      if (lane == 0) atomicAdd(red_r + l * m + row, racc);
+      if (lane == 0) part.r[(l * m + row) * gridDim.x + blockIdx.x] = racc;
     }
   }
-  if (red_c != nullptr) {
+  if (want_c) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) s_col[warp][lane * 8 + e] = colacc[e];
     __syncthreads();
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < THREADS / 32; ++w) t += s_col[w][threadIdx.x];
-    if (c0 + threadIdx.x < n) atomicAdd(red_c + l * n + c0 + threadIdx.x, t);
+    if (c0 + threadIdx.x < n) part.c[(l * gridDim.y + blockIdx.y) * n + c0 + threadIdx.x] = t;
   }
-  if (red_s != nullptr) {
+  if (want_s) {
     const float t = block_sum(sacc, sh);
-    if (threadIdx.x == 0) atomicAdd(red_s + l, t);
+    if (threadIdx.x == 0) part.s[l * gridDim.y * gridDim.x + blockIdx.y * gridDim.x + blockIdx.x] = t;
+  }
+}
+
+// out[i] = sum_{k < K} part[(i / inner) * K * inner + i % inner + k * inner], k ascending:
+// rows (inner 1, K = gx), whole matrices (inner 1, K = gy * gx), columns (inner n, K = gy).
+__global__ void md_finish_kernel(const float* __restrict__ part, float* __restrict__ out, int64_t count,
+                                 int64_t inner, int K) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const float* p = part + (i / inner) * K * inner + i % inner;
+    float t = 0.f;
+    for (int k = 0; k < K; ++k) t += p[k * inner];
+    out[i] = t;
   }
 }
 
@@ -213,7 +237,7 @@ __device__ __forceinline__ float lr_of(const PostArgs& a) { return a.lr_dev != n
 
 // sum of squares of W_hat' = W/g - lr * (rescale * U) per matrix / row / column
 template <bool VEC>
-__global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains gains, float* __restrict__ ss) {
+__global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains gains, Partials part) {
   __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
   const int64_t m = a.m, n = a.n;
   const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
@@ -249,7 +273,7 @@ __global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains ga
     if (a.norm_axis == 1) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-      if (lane == 0) atomicAdd(ss + l * m + row, racc);
+      if (lane == 0) part.r[(l * m + row) * gridDim.x + blockIdx.x] = racc;
     }
   }
   if (a.norm_axis == 2) {
@@ -259,10 +283,10 @@ __global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains ga
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < THREADS / 32; ++w) t += s_col[w][threadIdx.x];
-    if (c0 + threadIdx.x < n) atomicAdd(ss + l * n + c0 + threadIdx.x, t);
+    if (c0 + threadIdx.x < n) part.c[(l * gridDim.y + blockIdx.y) * n + c0 + threadIdx.x] = t;
   } else if (a.norm_axis == 0) {
     const float t = block_sum(facc, sh);
-    if (threadIdx.x == 0) atomicAdd(ss + l, t);
+    if (threadIdx.x == 0) part.s[l * gridDim.y * gridDim.x + blockIdx.y * gridDim.x + blockIdx.x] = t;
   }
 }
 
@@ -382,33 +406,73 @@ static dim3 md_grid(int64_t L, int64_t m, int64_t n) {
   return dim3((unsigned)((n + md::TC - 1) / md::TC), (unsigned)((m + md::TR - 1) / md::TR), (unsigned)L);
 }
 
+// floats of the three partial-sum arrays of one pass over [L, m, n]
+static int64_t md_partial_floats(int64_t L, int64_t m, int64_t n) {
+  const int64_t gx = (n + md::TC - 1) / md::TC, gy = (m + md::TR - 1) / md::TR;
+  return L * m * gx + L * gy * n + L * gy * gx;
+}
+
+static md::Partials md_partials(float* base, int64_t L, int64_t m, int64_t n) {
+  const int64_t gx = (n + md::TC - 1) / md::TC, gy = (m + md::TR - 1) / md::TR;
+  return md::Partials{base, base + L * m * gx, base + L * m * gx + L * gy * n};
+}
+
+// reduce the partials of one axis into out (0: whole matrix [L], 1: rows [L, m], 2: columns [L, n])
+static int md_finish(const md::Partials& p, int axis, float* out, int64_t L, int64_t m, int64_t n,
+                     cudaStream_t stream) {
+  const int64_t gx = (n + md::TC - 1) / md::TC, gy = (m + md::TR - 1) / md::TR;
+  const float* part = axis == 0 ? p.s : (axis == 1 ? p.r : p.c);
+  const int64_t count = axis == 0 ? L : (axis == 1 ? L * m : L * n);
+  const int64_t inner = axis == 2 ? n : 1;
+  const int K = (int)(axis == 0 ? gy * gx : (axis == 1 ? gx : gy));
+  int64_t blocks = (count + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  md::md_finish_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, out, count, inner, K);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" size_t zs_muonmd_pre_workspace(int64_t L, int64_t m, int64_t n) {
+  return (size_t)md_partial_floats(L, m, n) * sizeof(float) + 256;
+}
+
 extern "C" int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
                              const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col,
-                             int64_t L, int64_t m, int64_t n, float momentum, void* stream_) {
+                             int64_t L, int64_t m, int64_t n, float momentum, void* workspace,
+                             size_t workspace_bytes, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(W && G && buf && x_out, ZS_ERR_ARG);
   ZS_REQUIRE(L >= 1 && m >= 1 && n >= 1 && L < 65536 && (m + md::TR - 1) / md::TR < 65536, ZS_ERR_SHAPE);
   ZS_REQUIRE((g_scalar == nullptr) == (red_scalar == nullptr) && (g_row == nullptr) == (red_row == nullptr) &&
                  (g_col == nullptr) == (red_col == nullptr),
              ZS_ERR_ARG);
+  const bool any_red = red_scalar != nullptr || red_row != nullptr || red_col != nullptr;
+  ZS_REQUIRE(!any_red || (workspace && workspace_bytes >= zs_muonmd_pre_workspace(L, m, n)), ZS_ERR_WORKSPACE);
   ZS_BIND(W);
   md::Gains g{g_scalar, g_row, g_col};
   auto* X = reinterpret_cast<__nv_bfloat16*>(x_out);
   const dim3 grid = md_grid(L, m, n);
+  float* ws = any_red ? reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255))
+                      : nullptr;
+  const md::Partials part = any_red ? md_partials(ws, L, m, n) : md::Partials{nullptr, nullptr, nullptr};
+  const bool ws_ = red_scalar != nullptr, wr = red_row != nullptr, wc = red_col != nullptr;
   if (md_vec_ok(n, {W, G, buf, x_out}))
-    md::md_pre_kernel<true><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, red_scalar, red_row, red_col, m, n,
-                                                              momentum);
+    md::md_pre_kernel<true><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, part, ws_, wr, wc, m, n, momentum);
   else
-    md::md_pre_kernel<false><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, red_scalar, red_row, red_col, m, n,
-                                                               momentum);
+    md::md_pre_kernel<false><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, part, ws_, wr, wc, m, n, momentum);
   ZS_CUDA_TRY(cudaGetLastError());
+  int rc;
+  if (ws_ && (rc = md_finish(part, 0, red_scalar, L, m, n, stream)) != ZS_OK) return rc;
+  if (wr && (rc = md_finish(part, 1, red_row, L, m, n, stream)) != ZS_OK) return rc;
+  if (wc && (rc = md_finish(part, 2, red_col, L, m, n, stream)) != ZS_OK) return rc;
   return ZS_OK;
 }
 
 extern "C" size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n) {
   // ss + proj (up to L*max(m,n) each) + softplus old/new of scalar, row, column gains
+  // + the reduction pass's partial sums
   const int64_t mx = m > n ? m : n;
-  return (size_t)(2 * L * mx + 2 * (L + L * m + L * n)) * sizeof(float) + 8 * 256;
+  return (size_t)(2 * L * mx + 2 * (L + L * m + L * n) + md_partial_floats(L, m, n)) * sizeof(float) + 8 * 256;
 }
 
 extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
@@ -437,16 +501,20 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_
   float* sp = proj + L * mx;  // old: sc [L], row [L*m], col [L*n]; then new
   float* sp_old[3] = {sp, sp + L, sp + L + L * m};
   float* sp_new[3] = {sp_old[2] + L * n, sp_old[2] + L * n + L, sp_old[2] + L * n + L + L * m};
-  ZS_CUDA_TRY(cudaMemsetAsync(ss, 0, (size_t)n_proj * sizeof(float), stream));
+  const md::Partials part = md_partials(sp_new[2] + L * n, L, m, n);
   md::PostArgs a{W, reinterpret_cast<const __nv_bfloat16*>(U), m, n, lr_dev, lr_host, rescale, norm_axis};
   md::Gains g{g_scalar, g_row, g_col};
   const dim3 grid = md_grid(L, m, n);
   const bool vec = md_vec_ok(n, {W, U, p_out});
   if (vec)
-    md::md_reduce_kernel<true><<<grid, md::THREADS, 0, stream>>>(a, g, ss);
+    md::md_reduce_kernel<true><<<grid, md::THREADS, 0, stream>>>(a, g, part);
   else
-    md::md_reduce_kernel<false><<<grid, md::THREADS, 0, stream>>>(a, g, ss);
+    md::md_reduce_kernel<false><<<grid, md::THREADS, 0, stream>>>(a, g, part);
   ZS_CUDA_TRY(cudaGetLastError());
+  {
+    const int rc = md_finish(part, norm_axis, ss, L, m, n, stream);
+    if (rc != ZS_OK) return rc;
+  }
   md::GainArgs ga{};
   float* raws[3] = {g_scalar, g_row, g_col};
   float* m1s[3] = {m1_scalar, m1_row, m1_col};

@@ -160,13 +160,16 @@ def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
         _init_md_state(state, W, gain_mode, norm_axis, capturable)
     L = W.numel() // (m * n)
     X = torch.empty(W.shape, dtype=torch.bfloat16, device=W.device)
-    red = {k: torch.zeros_like(state[k]) for k in ("g_scalar", "g_row", "g_col") if k in state}
+    red = {k: torch.empty_like(state[k]) for k in ("g_scalar", "g_row", "g_col") if k in state}
     buf = state["momentum_buffer"]
-    Z.count(1)
+    ws = torch.empty(int(Z.lib().zs_muonmd_pre_workspace(L, m, n)) if red else 0, dtype=torch.uint8,
+                     device=W.device)
+    Z.count(1 + len(red))
     Z.check(Z.lib().zs_muonmd_pre(W.data_ptr(), G.data_ptr(), buf.data_ptr(),
                                   Z.ptr(state.get("g_scalar")), Z.ptr(state.get("g_row")), Z.ptr(state.get("g_col")),
                                   X.data_ptr(), Z.ptr(red.get("g_scalar")), Z.ptr(red.get("g_row")),
-                                  Z.ptr(red.get("g_col")), L, m, n, float(momentum), Z.stream_of(W)), "zs_muonmd_pre")
+                                  Z.ptr(red.get("g_col")), L, m, n, float(momentum), ws.data_ptr() if red else None,
+                                  ws.numel(), Z.stream_of(W)), "zs_muonmd_pre")
     return W, red, X
 
 
@@ -196,7 +199,7 @@ def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axi
     out = p if direct else W
     ws = torch.empty(int(Z.lib().zs_muonmd_post_workspace(L, m, n)), dtype=torch.uint8, device=W.device)
     g = lambda k: state.get(k)  # noqa: E731
-    Z.count(3)
+    Z.count(4)
     Z.check(Z.lib().zs_muonmd_post(
         W.data_ptr(), U.data_ptr(), out.data_ptr(), Z.dtype_code(out.dtype),
         Z.ptr(g("g_scalar")), Z.ptr(g("g_row")), Z.ptr(g("g_col")),

@@ -60,7 +60,9 @@ _SIGNATURES = {
                                     _f32, _vp]),
     "zs_attention_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                      _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp]),
-    "zs_muonmd_pre": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp]),
+    "zs_muonmd_pre_workspace": (_sz, [_i64, _i64, _i64]),
+    "zs_muonmd_pre": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _sz,
+                             _vp]),
     "zs_muonmd_post_workspace": (_sz, [_i64, _i64, _i64]),
     "zs_muonmd_post": (_i32, [_vp, _vp, _vp, _i32] + [_vp] * 12 + [_vp, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
                                                                   _f32, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),

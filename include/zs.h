@@ -396,10 +396,13 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  *
  * zs_muonmd_pre:  buf = lerp(buf, g*G, 1 - momentum);
  *                 x_out (bf16 [L, m, n]) = lerp(g*G, buf, momentum);
- *                 red_* += the gain-gradient reductions of (W/g)*G times the
+ *                 red_* = the gain-gradient reductions of (W/g)*G times the
  *                 other gains over the axes each gain does not span (red_*
- *                 f32, same shapes as the gains, zeroed by the caller; NULL
- *                 exactly where the gain is NULL).
+ *                 f32, same shapes as the gains, overwritten; NULL exactly
+ *                 where the gain is NULL).  The reductions add per-block
+ *                 partial sums in a fixed order (no atomics): results are
+ *                 bit-identical from run to run.  Workspace (only when a
+ *                 gain is present): zs_muonmd_pre_workspace bytes.
  * zs_muonmd_post: with U the orthogonalised update (bf16 [L, m, n]):
  *                 W' = W/g - lr * rescale * U, projected to target_norm
  *                 per matrix (norm_axis 0, target [L]), row (1, [L, m]) or
@@ -410,9 +413,10 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  *                 g_new * W'.  lr from lr_dev (f32 device scalar) or lr_host.
  *                 Workspace: zs_muonmd_post_workspace bytes.
  */
+size_t zs_muonmd_pre_workspace(int64_t L, int64_t m, int64_t n);
 int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
                   const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col, int64_t L,
-                  int64_t m, int64_t n, float momentum, void* stream);
+                  int64_t m, int64_t n, float momentum, void* workspace, size_t workspace_bytes, void* stream);
 size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n);
 int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
                    float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row, float* m1_col,

@@ -235,3 +235,29 @@ def test_batched_optimizer_matches_per_parameter_steps():
     # norm is reduced in a fixed order): equal up to the gain reductions' atomic order
     for p, r in zip(ps, ref):
         assert rel_err(p.detach(), r) < 1e-6
+
+
+@pytest.mark.parametrize("gain_mode,norm_axis", [("both", "frobenius"), ("col", "row"), ("row", "col"),
+                                                 ("scalar", "frobenius")])
+def test_md_step_is_deterministic(gain_mode, norm_axis):
+    """Two runs of the fused MuonMD step on the same inputs give bit-identical parameters
+    and state (fixed-order reductions), which keeps data-parallel replicas in sync."""
+    from optimizer.muon import md_decoupled_step
+
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    W0 = torch.randn(8, 384, 640, device="cuda", generator=gen) * 0.05
+    grads = [torch.randn(8, 384, 640, device="cuda", generator=gen) for _ in range(2)]
+    runs = []
+    for _ in range(2):
+        p, st = W0.clone(), {}
+        for gr in grads:
+            md_decoupled_step(p, gr.clone(), st, lr=0.02, momentum=0.95, gain_lr=1e-2, gain_betas=(0.9, 0.95),
+                              gain_eps=1e-10, gain_mode=gain_mode, norm_axis=norm_axis, ns_steps=5, capturable=True,
+                              rescale_mode="balanced")
+        torch.cuda.synchronize()
+        runs.append((p, st))
+    (pa, sa), (pb, sb) = runs
+    assert torch.equal(pa, pb)
+    for k, v in sa.items():
+        if torch.is_tensor(v):
+            assert torch.equal(v, sb[k]), k
