@@ -359,12 +359,18 @@ __device__ __forceinline__ void store_f32_chunk(float* o, const uint32_t (&r)[32
   }
 }
 
-// The gate half [swiglu_half + col0, +32) of this lane's saved row, raw.
-__device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&w)[4]) {
+// The up half [col0, +32) (h) and the gate half [swiglu_half + col0, +32) (g) of
+// this lane's saved row, raw.
+__device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, int col0, bool ok, uint4 (&h)[4],
+                                               uint4 (&g)[4]) {
   ok = ok && col0 + 32 <= a.N_out;
-  const uint4* p = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + a.swiglu_half + col0) * 2);
+  const uint4* ph = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + col0) * 2);
+  const uint4* pg = reinterpret_cast<const uint4*>(a.aux + (row * a.ld_aux + a.swiglu_half + col0) * 2);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
+  for (int q = 0; q < 4; ++q) {
+    h[q] = ok ? __ldg(ph + q) : make_uint4(0, 0, 0, 0);
+    g[q] = ok ? __ldg(pg + q) : make_uint4(0, 0, 0, 0);
+  }
 }
 
 // PAIR: a cluster of two CTAs computes 256-row MODE_ROWS tiles with one
@@ -728,8 +734,8 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           valid = false;
         }
       }
-      uint4 gcur[4];
-      if (EPI == EPI_DSWIGLU) prefetch_chunk(args, out_row, ti.nt * BN + half * (BN / 2), valid && vec, gcur);
+      uint4 hcur[4], gcur[4];
+      if (EPI == EPI_DSWIGLU) prefetch_chunk(args, out_row, ti.nt * BN + half * (BN / 2), valid && vec, hcur, gcur);
       if (!warp_wait(&tfull[buf], acc_phase, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
@@ -768,21 +774,19 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           // the saved pre-activation [h | g] into d[h | g] in one pass, with
           // the reference's rounding points:
           //   dh = round(da * round(silu(g))),  dg = round(round(da * h) * silu'(g))
-          // The gate half of the next chunk is fetched during this one.
+          // Both halves of the next chunk are fetched during this one (the first
+          // chunk's before the accumulator wait).
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
             const int lc = half * (BN / 2) + c * 32;
-            uint4 gnext[4];
-            prefetch_chunk(args, out_row, ti.nt * BN + lc + 32, valid && vec && c + 1 < BN / 64, gnext);
+            uint4 hnext[4], gnext[4];
+            prefetch_chunk(args, out_row, ti.nt * BN + lc + 32, valid && vec && c + 1 < BN / 64, hnext, gnext);
             const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
             uint4 hraw[4];
             const bool fast = vec && ncols == 32;
-            if (fast) {
-              const uint4* ph = reinterpret_cast<const uint4*>(args.aux + (out_row * args.ld_aux + col0) * 2);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) hraw[q] = valid ? __ldg(ph + q) : make_uint4(0, 0, 0, 0);
-            }
+            for (int q = 0; q < 4; ++q) hraw[q] = hcur[q];
             uint32_t r[32];
             tmem_ld_32x32b_x32(t_row + lc, r);
             tc_wait_ld();
@@ -818,7 +822,10 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, odh, vec, stg);
             emit_packed<DT>(args.out, out_row * args.ldo_m, args.swiglu_half + col0, ncols, valid, odg, vec, stg);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) gcur[q] = gnext[q];
+            for (int q = 0; q < 4; ++q) {
+              hcur[q] = hnext[q];
+              gcur[q] = gnext[q];
+            }
           }
         } else if (EPI == EPI_LSE || EPI == EPI_XENT_GRAD) {
           // Columns are vocabulary entries col_offset + col.  Labels of this
