@@ -9,7 +9,7 @@ flattened bucket is issued asynchronously on a side stream, overlapping the
 rest of the backward.  Code that writes .grad itself (the fused expert
 weight-gradient path) reports completion through notify_grad_ready.  finish()
 flushes what is left, waits for the collectives and copies the reduced values
-back.  Sparse gradients (the input embedding's COO gradient) are
+back (a bucket dtype group holding one contiguous gradient is reduced in place).  Sparse gradients (the input embedding's COO gradient) are
 all-gathered as (indices, values) and concatenated, which is the sum of the
 ranks' sparse gradients.
 
@@ -163,22 +163,26 @@ class GradAllReducer:
         with ctx:
             for dt in sorted(by_dtype, key=str):   # same order on every rank
                 group = by_dtype[dt]
-                flat = torch.cat([p.grad.reshape(-1) for p in group])
+                # a lone contiguous gradient is reduced in place (no flatten copy, no copy back)
+                in_place = len(group) == 1 and group[0].grad.is_contiguous()
+                flat = group[0].grad.view(-1) if in_place else torch.cat([p.grad.reshape(-1) for p in group])
                 work = dist.all_reduce(flat, group=self.group, async_op=True)
-                self._pending.append((work, flat, group))
+                self._pending.append((work, flat, group, in_place))
 
     def finish(self):
         """Issue the remaining buckets, wait, and write the reduced gradients back."""
         for b in range(len(self.buckets)):
             self._ready[b] = {id(p) for p in self.buckets[b]}
         self._launch_ready()
-        for work, flat, dense in self._pending:
+        for work, flat, dense, in_place in self._pending:
             work.wait()
             if self._stream is not None:
                 torch.cuda.current_stream().wait_stream(self._stream)
                 flat.record_stream(torch.cuda.current_stream())
             if self.average:
                 flat.div_(self.world)
+            if in_place:
+                continue
             off = 0
             for p in dense:
                 n = p.numel()
