@@ -7,4 +7,5 @@
 #include "zs_norm.cu"
 #include "zs_attn.cu"
 #include "zs_muon.cu"
+#include "zs_comm.cu"
 #include "zs_api.cu"

@@ -61,6 +61,12 @@ _SIGNATURES = {
     "zs_attention_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                      _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp]),
     "zs_muonmd_pre_workspace": (_sz, [_i64, _i64, _i64]),
+    "zs_ipc_handle_size": (_i32, []),
+    "zs_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "zs_ipc_open": (_i32, [_vp, _i64, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "zs_ipc_close": (_i32, [_vp]),
+    "zs_ce_allreduce_chunk": (_i64, [_i64, _i32]),
+    "zs_ce_allreduce": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp]),
     "zs_muonmd_pre": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _sz,
                              _vp]),
     "zs_muonmd_post_workspace": (_sz, [_i64, _i64, _i64]),

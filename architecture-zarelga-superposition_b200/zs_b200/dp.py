@@ -19,6 +19,11 @@ so every rank agrees), with parameters that never fire a hook at the end.
 Every rank must register the same parameters in the same order and run one
 backward pass per finish(): the collectives are issued in bucket order,
 identical on every rank.
+
+engine="ce" reduces the dense buckets (after the first step's rebuild) with
+CopyEngineAllReduce (zs_b200/ce.py): peer copies on the copy engines instead of
+NCCL kernels, so the reduction does not take SMs from the backward GEMMs it
+overlaps; the result is bit-identical on every rank.
 """
 from __future__ import annotations
 
@@ -68,10 +73,14 @@ def all_gather_sparse(grad: torch.Tensor, process_group=None) -> torch.Tensor:
 
 
 class GradAllReducer:
-    def __init__(self, params, process_group=None, bucket_mb=64.0, average=False):
+    def __init__(self, params, process_group=None, bucket_mb=64.0, average=False, engine="nccl"):
+        if engine not in ("nccl", "ce"):
+            raise ValueError(f"unknown engine {engine!r}")
         self.group = process_group
         self.world = dist.get_world_size(process_group)
         self.average = average
+        self.engine = engine
+        self._ce = {}             # (bucket, dtype) -> CopyEngineAllReduce
         self.params = [p for p in params if p.requires_grad]
         self.bucket_bytes = int(bucket_mb * (1 << 20))
         self._hooks = []
@@ -166,6 +175,17 @@ class GradAllReducer:
                 # a lone contiguous gradient is reduced in place (no flatten copy, no copy back)
                 in_place = len(group) == 1 and group[0].grad.is_contiguous()
                 flat = group[0].grad.view(-1) if in_place else torch.cat([p.grad.reshape(-1) for p in group])
+                if self.engine == "ce" and self._rebuilt and flat.is_cuda and dt in (torch.bfloat16, torch.float32):
+                    from .ce import CopyEngineAllReduce
+
+                    key = (b, dt)
+                    ce = self._ce.get(key)
+                    if ce is None or ce.count != flat.numel():
+                        ce = self._ce[key] = CopyEngineAllReduce(flat.numel(), dt, self.group, flat.device)
+                    ce(flat, scale=(1.0 / self.world) if self.average else 1.0,
+                       stream=self._stream or torch.cuda.current_stream())
+                    self._pending.append((None, flat, group, in_place))
+                    continue
                 work = dist.all_reduce(flat, group=self.group, async_op=True)
                 self._pending.append((work, flat, group, in_place))
 
@@ -175,11 +195,12 @@ class GradAllReducer:
             self._ready[b] = {id(p) for p in self.buckets[b]}
         self._launch_ready()
         for work, flat, dense, in_place in self._pending:
-            work.wait()
+            if work is not None:
+                work.wait()
             if self._stream is not None:
                 torch.cuda.current_stream().wait_stream(self._stream)
                 flat.record_stream(torch.cuda.current_stream())
-            if self.average:
+            if self.average and work is not None:
                 flat.div_(self.world)
             if in_place:
                 continue

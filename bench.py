@@ -246,7 +246,7 @@ def run_gpu(args):
     if world > 1:
         from zs_b200.dp import GradAllReducer
 
-        reducer = GradAllReducer(params, bucket_mb=1.0)
+        reducer = GradAllReducer(params, bucket_mb=1.0, engine=args.dp_engine)
 
     def step(xs, ls, dys):
         for p_ in params:
@@ -381,6 +381,9 @@ def run_gpu(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "d_model": d, "experts": E, "ffn": f, "top_k": k,
                        "parallelism": f"dp{world}", "l2": "working set ~3 GB per step, larger than the 126 MB L2",
+                       "grad_allreduce": (None if world == 1 else
+                                          "copy engines over NVLink peer memory (zs_ce_allreduce)"
+                                          if args.dp_engine == "ce" else "NCCL"),
                        "mfu_sustained_peak": mfu, "flops_per_step_per_gpu": fl},
             "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (6 launches per step: up+SwiGLU, down, "
                                                       "2 input-gradient, 2 weight-gradient)",
@@ -744,6 +747,8 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
     ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
+    ap.add_argument("--dp-engine", default="nccl", choices=["nccl", "ce"],
+                    help="config 2 with N > 1: gradient all-reduce on the copy engines (ce) or NCCL")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

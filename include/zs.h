@@ -45,6 +45,7 @@ extern "C" {
 #define ZS_DEVERR_TIMEOUT_EPILOGUE 0x04
 #define ZS_DEVERR_TIMEOUT_DRAIN 0x08
 #define ZS_DEVERR_INDEX 0x10       /* an index input was out of range; the element was skipped */
+#define ZS_DEVERR_TIMEOUT_PEER 0x20 /* a wait for a peer GPU's flag expired (zs_ce_allreduce) */
 
 /* dtype codes */
 #define ZS_F32 0
@@ -424,6 +425,34 @@ int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, floa
                    const float* step_dev, float step_host, float b1, float b2, float eps, float gain_lr,
                    const float* lr_dev, float lr_host, float rescale, int norm_axis, const float* target_norm,
                    int64_t L, int64_t m, int64_t n, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Data-parallel all-reduce over NVLink peer memory with the copy engines (no
+ * counterpart in the reference, which trains on one device; replaces the NCCL
+ * all-reduce of data-parallel gradients).  Buffers are shared between the
+ * processes of one node through CUDA IPC:
+ *   zs_ipc_export: IPC handle (zs_ipc_handle_size() bytes) of the allocation
+ *                  holding ptr, and ptr's byte offset in it;
+ *   zs_ipc_open:   map a peer's handle on `device`; *ptr_out = mapping +
+ *                  offset, *base_out = the mapping for zs_ipc_close.
+ * zs_ce_allreduce: data (count elements, bf16 or f32, 16-byte aligned) =
+ *   scale * the sum over the `world` ranks' data, bit-identical on every rank
+ *   (rank r sums chunk r in rank order in f32).  recv[p], red[p], flags[p]:
+ *   rank p's receive buffer (world * zs_ce_allreduce_chunk(count, world)
+ *   elements), reduced-chunk buffer (one chunk) and int32 flag table [3 *
+ *   world] (zeroed before the first call), as mapped in this process (own
+ *   entries local).  `step` starts at 1 and grows by one per call on the same
+ *   buffers.  Every rank makes the same calls in the same order.  The copies run
+ *   on the copy engines; waits for peers are bounded and record
+ *   ZS_DEVERR_TIMEOUT_PEER when they expire.
+ */
+int zs_ipc_handle_size(void);
+int zs_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int zs_ipc_open(const void* handle, int64_t offset, int device, void** ptr_out, void** base_out);
+int zs_ipc_close(void* base);
+int64_t zs_ce_allreduce_chunk(int64_t count, int world);
+int zs_ce_allreduce(void* data, int64_t count, int dtype, int rank, int world, void* const* recv, void* const* red,
+                    int* const* flags, int step, float scale, void* stream);
 
 #ifdef __cplusplus
 }

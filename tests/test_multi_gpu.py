@@ -9,6 +9,12 @@
   two steps, and within 1e-5 relative of the single-device optimizer (a rank's
   Newton-Schulz batch holds fewer matrices, which can change the kernels' tile
   split and so the f32 accumulation order of the bf16 GEMMs).
+* CopyEngineAllReduce (copy-engine all-reduce over CUDA IPC peer memory):
+  bit-exact against the f32 sum in rank order, rounded once, over several
+  steps, bf16 and f32, sizes that do not split evenly; GradAllReducer with
+  engine="ce" against engine="nccl" on a small model; and a peer that never
+  joins: the bounded wait expires and records ZS_DEVERR_TIMEOUT_PEER instead
+  of hanging.
 Ranks are child processes, one per GPU, with a short process-group timeout."""
 import datetime
 import os
@@ -166,3 +172,119 @@ def test_sharded_muonmd_two_gpus():
         assert tb is None, tb
         assert same, f"rank {rank}: the ranks' parameters differ"
         assert worst < 1e-5, f"rank {rank}: worst relative error {worst:.3e} against the single-device optimizer"
+
+
+def _ce_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from zs_b200.ce import CopyEngineAllReduce
+        from zs_b200 import device_error
+
+        dev = torch.device("cuda", rank)
+        ok = []
+        for dt, n in ((torch.bfloat16, 1_000_003), (torch.float32, 77_777), (torch.bfloat16, 9)):
+            ce = CopyEngineAllReduce(n, dt)
+            for step in range(3):
+                g = torch.Generator(device=dev).manual_seed(100 * step + n)
+                xs = [torch.randn(n, device=dev, generator=g).to(dt) for _ in range(world)]
+                scale = 0.5 if step == 1 else 1.0
+                acc = xs[0].float()
+                for r in range(1, world):
+                    acc = acc + xs[r].float()
+                want = (acc * scale).to(dt)
+                t = xs[rank].clone()
+                ce(t, scale=scale)
+                torch.cuda.synchronize()
+                ok.append(bool(torch.equal(t, want)))
+            ce.close()
+        err = device_error()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok, err, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def _reducer_ce_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from zs_b200.dp import GradAllReducer
+
+        dev = torch.device("cuda", rank)
+        torch.manual_seed(0)
+        nets = [torch.nn.Sequential(torch.nn.Linear(64, 128), torch.nn.GELU(), torch.nn.Linear(128, 32)).to(dev)
+                for _ in range(2)]
+        nets[1].load_state_dict(nets[0].state_dict())
+        reds = [GradAllReducer(list(nets[0].parameters()), bucket_mb=0.01, average=True, engine="nccl"),
+                GradAllReducer(list(nets[1].parameters()), bucket_mb=0.01, average=True, engine="ce")]
+        worst = 0.0
+        same_ranks = True
+        for step in range(3):
+            g = torch.Generator(device=dev).manual_seed(10 * step + rank)
+            x = torch.randn(16, 64, device=dev, generator=g)
+            for net, red in zip(nets, reds):
+                net.zero_grad(set_to_none=True)
+                net(x).square().sum().backward()
+                red.finish()
+            for a, b in zip(nets[0].parameters(), nets[1].parameters()):
+                worst = max(worst, _rel(b.grad, a.grad))
+            flat = torch.cat([p.grad.flatten() for p in nets[1].parameters()])
+            allf = [torch.empty_like(flat) for _ in range(world)]
+            dist.all_gather(allf, flat)
+            same_ranks = same_ranks and all(torch.equal(f, allf[0]) for f in allf)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, worst, same_ranks, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def _ce_timeout_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from zs_b200.ce import CopyEngineAllReduce
+        from zs_b200 import _lib as Z
+        from zs_b200 import device_error
+
+        ce = CopyEngineAllReduce(4096, torch.float32)
+        err = 0
+        if rank == 0:
+            # rank 1 never calls: the waits for its flags run out (about a second each)
+            t = torch.ones(4096, device=torch.device("cuda", rank))
+            ce(t)
+            torch.cuda.synchronize()
+            err = device_error()
+            Z.clear_device_error()
+        dist.barrier()
+        ce.close()
+        dist.destroy_process_group()
+        q.put((rank, err, None, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def test_ce_allreduce_two_gpus_bit_exact():
+    for rank, ok, err, tb in _spawn(_ce_worker):
+        assert tb is None, tb
+        assert err == 0
+        assert all(ok), f"rank {rank}: {ok}"
+
+
+def test_grad_reducer_copy_engine_two_gpus():
+    for rank, worst, same_ranks, tb in _spawn(_reducer_ce_worker):
+        assert tb is None, tb
+        assert same_ranks, f"rank {rank}: reduced gradients differ across ranks"
+        assert worst < 1e-5, f"rank {rank}: copy-engine vs NCCL gradients differ by {worst:.3e}"
+
+
+def test_ce_allreduce_peer_timeout_is_reported():
+    for rank, err, _, tb in _spawn(_ce_timeout_worker):
+        assert tb is None, tb
+        if rank == 0:
+            assert err & 0x20, f"expected ZS_DEVERR_TIMEOUT_PEER, got {err:#x}"
