@@ -196,20 +196,40 @@ __global__ void rowwise_sum_product_kernel(char* out, int out_dtype, int64_t o_s
 
 // out[t, c] = sum_j w[t, j] * in[t*k + j, c]   (w == NULL: plain sum over j)
 // f32 accumulation; one warp per token row, 8 columns per lane step.
+// rmap (optional, [T*k]): slot t*k+j reads input row rmap[t*k+j] instead of t*k+j
+// (rows stored in another order); a row outside [0, n_rows) counts as zero and
+// records ZS_DEVERR_INDEX.
 __global__ void weighted_row_sum_kernel(char* out, int64_t o_sm, const char* in, int64_t i_sm, const void* w,
-                                        int w_dtype, int64_t T, int k, int64_t C, int dtype, int vec) {
+                                        int w_dtype, int64_t T, int k, int64_t C, int dtype, int vec,
+                                        const int64_t* __restrict__ rmap, int64_t n_rows) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
     float wt[32];
-    for (int j = 0; j < k; ++j) wt[j] = w ? load_as_f32(w, t * k + j, w_dtype) : 1.0f;
+    int64_t rw[32];
+    for (int j = 0; j < k; ++j) {
+      wt[j] = w ? load_as_f32(w, t * k + j, w_dtype) : 1.0f;
+      int64_t r = t * k + j;
+      if (rmap != nullptr) {
+        r = __ldg(rmap + t * k + j);
+        if (r < 0 || r >= n_rows) {
+          if (lane == 0) zs::record_error(ZS_DEVERR_INDEX);
+          r = -1;
+        }
+      }
+      if (r < 0) {
+        wt[j] = 0.f;   // contributes nothing; row 0 keeps the load in bounds
+        r = 0;
+      }
+      rw[j] = r;
+    }
     if (vec && k <= 8) {
       // all k slot rows' vectors in flight before the accumulation (same j order)
       for (int64_t v = lane; v < C / 8; v += 32) {
         uint4 raw[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(in + ((t * k + j) * i_sm) * 2) + v);
+          if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(in + (rw[j] * i_sm) * 2) + v);
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -226,7 +246,7 @@ __global__ void weighted_row_sum_kernel(char* out, int64_t o_sm, const char* in,
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int j = 0; j < k; ++j) {
           float f[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(in + ((t * k + j) * i_sm) * 2) + v), dtype, f);
+          unpack8(__ldg(reinterpret_cast<const uint4*>(in + (rw[j] * i_sm) * 2) + v), dtype, f);
 #pragma unroll
           for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt[j], f[q], acc[q]);
         }
@@ -235,7 +255,7 @@ __global__ void weighted_row_sum_kernel(char* out, int64_t o_sm, const char* in,
     } else {
       for (int64_t c = lane; c < C; c += 32) {
         float acc = 0.f;
-        for (int j = 0; j < k; ++j) acc = fmaf(wt[j], load_as_f32(in, (t * k + j) * i_sm + c, dtype), acc);
+        for (int j = 0; j < k; ++j) acc = fmaf(wt[j], load_as_f32(in, rw[j] * i_sm + c, dtype), acc);
         store_from_f32(out, t * o_sm + c, dtype, acc);
       }
     }
@@ -290,7 +310,25 @@ extern "C" int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int6
   if (blocks > 148 * 16) blocks = 148 * 16;
   weighted_row_sum_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<char*>(out), o_sm, reinterpret_cast<const char*>(in), i_sm, weights, w_dtype, T, k, C, dtype,
-      vec);
+      vec, nullptr, T * k);
+  return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
+}
+
+extern "C" int zs_gathered_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, int64_t n_rows,
+                                   const int64_t* row_of_slot, int64_t T, int k, int64_t C, int dtype,
+                                   void* stream) {
+  ZS_REQUIRE(out && in && row_of_slot, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(T >= 0 && k >= 1 && k <= 32 && C >= 0 && n_rows >= 0, ZS_ERR_SHAPE);
+  ZS_BIND(in);
+  if (T == 0 || C == 0) return ZS_OK;
+  const int vec = C % 8 == 0 && o_sm % 8 == 0 && i_sm % 8 == 0 &&
+                  ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(in)) % 16 == 0);
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  weighted_row_sum_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<char*>(out), o_sm, reinterpret_cast<const char*>(in), i_sm, nullptr, 0, T, k, C, dtype, vec,
+      row_of_slot, n_rows);
   return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
 }
 

@@ -36,6 +36,11 @@ from torch import nn
 from .parallel_experts import ParallelExperts, flatten_sort_count
 
 
+def _all_to_all(t, out_splits, in_splits, group, world):
+    """_AllToAll, or t itself when the group has one rank (nothing to exchange)."""
+    return t if world == 1 else _AllToAll.apply(t, out_splits, in_splits, group)
+
+
 class _AllToAll(torch.autograd.Function):
     """all_to_all_single with variable splits along dim 0; backward sends the
     gradient back with the splits swapped."""
@@ -91,11 +96,20 @@ class _SlotSum(torch.autograd.Function):
 
 
 def _slot_sum(rows, ssi, T, k):
-    from .mlp import weighted_row_sum
+    """y[t] = sum_j rows[pos(t, j)] in one pass (libzs gathered row sum), pos the inverse of ssi."""
+    from zs_b200 import _lib as Z
 
-    slot_rows = torch.empty_like(rows)
-    slot_rows.index_copy_(0, ssi, rows)
-    return weighted_row_sum(slot_rows, None, T, k)
+    n = ssi.numel()
+    pos = torch.empty_like(ssi)
+    pos[ssi] = torch.arange(n, device=ssi.device, dtype=ssi.dtype)
+    rows = rows.contiguous()
+    C = rows.size(1)
+    out = torch.empty((T, C), dtype=rows.dtype, device=rows.device)
+    Z.count(1)
+    Z.check(Z.lib().zs_gathered_row_sum(out.data_ptr(), out.stride(0), rows.data_ptr(), rows.stride(0), rows.size(0),
+                                        pos.data_ptr(), T, k, C, Z.dtype_code(rows.dtype), Z.stream_of(rows)),
+            "zs_gathered_row_sum")
+    return out
 
 
 def _glu_experts(x, p, lid, W1, W2, num_local, fuse_wgrad):
@@ -150,8 +164,11 @@ class ExpertParallelGLUMLP(nn.Module):
         """(send rows per rank, receive rows per rank, receive counts [world, E_local]) from the
         inclusive per-expert offsets of this rank's slots; one all-to-all of the counts."""
         counts = torch.diff(offs, prepend=offs.new_zeros(1))
-        recv = torch.empty_like(counts)
-        dist.all_to_all_single(recv, counts.contiguous(), group=self.group)
+        if self.world == 1:
+            recv = counts
+        else:
+            recv = torch.empty_like(counts)
+            dist.all_to_all_single(recv, counts.contiguous(), group=self.group)
         both = torch.cat([counts, recv]).cpu()  # the one host read per layer: NCCL needs the split sizes
         send_c = both[:self.num_experts].view(self.world, self.num_local)
         recv_c = both[self.num_experts:].view(self.world, self.num_local)
@@ -166,8 +183,8 @@ class ExpertParallelGLUMLP(nn.Module):
         send, recv, recv_c = self._splits(offs)
         x_send = self._gather(x, ssi, k)
         p_send = expert_p.reshape(-1)[ssi]
-        x_recv = _AllToAll.apply(x_send, recv, send, self.group)
-        p_recv = _AllToAll.apply(p_send, recv, send, self.group)
+        x_recv = _all_to_all(x_send, recv, send, self.group, self.world)
+        p_recv = _all_to_all(p_send, recv, send, self.group, self.world)
         R = x_recv.size(0)
         W1, W2 = self.experts.weight, self.output_experts.weight
         if R:
@@ -180,7 +197,7 @@ class ExpertParallelGLUMLP(nn.Module):
             # received tensors stay in the graph so every rank runs the same backward
             # all-to-alls in the same order
             y_recv = x_recv.new_zeros((0, d)) + (W1.sum() + W2.sum() + x_recv.sum() + p_recv.sum()).to(x_recv.dtype) * 0
-        y_back = _AllToAll.apply(y_recv.to(x.dtype), send, recv, self.group)
+        y_back = _all_to_all(y_recv.to(x.dtype), send, recv, self.group, self.world)
         y = self._slot_sum(y_back, ssi, T, k)
         return y.view(*shape[:-1], y.size(-1))
 

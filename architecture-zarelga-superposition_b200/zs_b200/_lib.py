@@ -47,6 +47,7 @@ _SIGNATURES = {
     "zs_group": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp]),
     "zs_rowwise_sum_product": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
                                       _i64, _i64, _i64, _vp]),
+    "zs_gathered_row_sum": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _i64, _i32, _i64, _i32, _vp]),
     "zs_weighted_row_sum": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i64, _i32, _vp]),
     "zs_expert_up_swiglu": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _vp]),
     "zs_swiglu_backward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),

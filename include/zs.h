@@ -231,6 +231,17 @@ int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, c
                         int64_t T, int k, int64_t C, int dtype, void* stream);
 
 /*
+ * The same k-way sum with the slot rows stored in another order (no
+ * counterpart in the reference; the combine of the expert-parallel layer,
+ * whose output rows return in expert order):
+ *   out[t, c] = sum_j in[row_of_slot[t*k + j], c]
+ * row_of_slot int64 [T*k]; a row outside [0, n_rows) contributes zero and
+ * records ZS_DEVERR_INDEX.
+ */
+int zs_gathered_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, int64_t n_rows,
+                        const int64_t* row_of_slot, int64_t T, int k, int64_t C, int dtype, void* stream);
+
+/*
  * GLUMLP up projection with the SwiGLU activation fused into the GEMM
  * epilogue (scattermoe/mlp.py:80-87: experts(...) then chunk(2) into
  * h = first half, gates = second half, then silu(gates) * h):

@@ -9,6 +9,7 @@
   two steps, and within 1e-5 relative of the single-device optimizer (a rank's
   Newton-Schulz batch holds fewer matrices, which can change the kernels' tile
   split and so the f32 accumulation order of the bf16 GEMMs).
+* ExpertParallelGLUMLP on one rank (no exchange) against GLUMLP;
 * CopyEngineAllReduce (copy-engine all-reduce over CUDA IPC peer memory):
   bit-exact against the f32 sum in rank order, rounded once, over several
   steps, bf16 and f32, sizes that do not split evenly; GradAllReducer with
@@ -288,3 +289,40 @@ def test_ce_allreduce_peer_timeout_is_reported():
         assert tb is None, tb
         if rank == 0:
             assert err & 0x20, f"expected ZS_DEVERR_TIMEOUT_PEER, got {err:#x}"
+
+
+def _ep1_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from scattermoe.expert_parallel import ExpertParallelGLUMLP
+        from scattermoe.mlp import GLUMLP
+
+        dev = torch.device("cuda", rank)
+        T, d, E, k, f = 700, 128, 8, 3, 64
+        g = torch.Generator(device=dev).manual_seed(8)
+        x = torch.randn(T, d, device=dev, generator=g).bfloat16()
+        p, idx = torch.sigmoid(torch.randn(T, E, device=dev, generator=g)).topk(k, dim=-1)
+        p = p.bfloat16()
+        dy = torch.randn(T, d, device=dev, generator=g).bfloat16()
+        full = GLUMLP(d, f, E, k).to(dev).bfloat16()
+        ep = ExpertParallelGLUMLP(d, f, E, k).to(dev).bfloat16().load_from_full(full)
+        outs = []
+        for m in (full, ep):
+            xr, pr = x.clone().requires_grad_(True), p.clone().requires_grad_(True)
+            y = m(xr, pr, idx)
+            y.backward(dy)
+            outs.append((y, xr.grad, pr.grad, m.experts.weight.grad, m.output_experts.weight.grad))
+        res = [(_rel(a, b), _cos(a, b)) for a, b in zip(outs[1], outs[0])]
+        dist.destroy_process_group()
+        q.put((rank, res, None, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def test_expert_parallel_single_rank_equals_glumlp():
+    for rank, res, _, tb in _spawn(_ep1_worker, world=1):
+        assert tb is None, tb
+        for rel, cos in res:
+            assert rel < 1e-2 and cos > 0.999, res

@@ -305,3 +305,38 @@ def test_glumlp_fused_weight_grad_accumulation(set_to_none, wdtype):
         assert b.grad.dtype == wdtype and b.grad.is_contiguous()
         assert rel_err(b.grad, a.grad) < 5e-3 and cosine(b.grad, a.grad) > 0.99999
     assert rel_err(outs[1][0], outs[0][0]) < 1e-6 and rel_err(outs[1][1], outs[0][1]) < 1e-6
+
+
+@pytest.mark.parametrize("T,k,C", [(1000, 8, 1024), (257, 3, 72), (64, 1, 40)])
+def test_gathered_row_sum(T, k, C):
+    """out[t] = sum_j rows[pos[t*k + j]] (the expert-parallel combine): bit-exact against
+    the f32 sum in slot order rounded once; a row index out of range contributes zero
+    and is recorded as ZS_DEVERR_INDEX."""
+    from scattermoe.expert_parallel import _slot_sum
+    from zs_b200 import _lib as Z
+    from zs_b200 import clear_device_error, device_error
+
+    g = torch.Generator(device="cuda").manual_seed(T + C)
+    n = T * k
+    rows = torch.randn(n, C, device="cuda", generator=g).bfloat16()
+    ssi = torch.randperm(n, device="cuda", generator=g)
+    out = _slot_sum(rows, ssi, T, k)
+    pos = torch.empty_like(ssi)
+    pos[ssi] = torch.arange(n, device="cuda")
+    acc = torch.zeros(T, C, device="cuda")
+    for j in range(k):
+        acc = acc + rows[pos.view(T, k)[:, j]].float()
+    assert torch.equal(out, acc.bfloat16())
+    assert device_error() == 0
+    bad = pos.clone()
+    bad[0] = n + 5
+    out2 = torch.empty(T, C, device="cuda", dtype=torch.bfloat16)
+    Z.check(Z.lib().zs_gathered_row_sum(out2.data_ptr(), C, rows.data_ptr(), C, n, bad.data_ptr(), T, k, C,
+                                        Z.ZS_BF16, torch.cuda.current_stream().cuda_stream), "zs_gathered_row_sum")
+    torch.cuda.synchronize()
+    ref0 = torch.zeros(C, device="cuda")
+    for j in range(1, k):
+        ref0 = ref0 + rows[pos[j]].float()
+    assert torch.equal(out2[0], ref0.bfloat16()) and torch.equal(out2[1:], out[1:])
+    assert device_error() & 0x10
+    clear_device_error()
