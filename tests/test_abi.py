@@ -36,6 +36,11 @@ def test_host_only_entry_points():
     assert lib.zs_flatten_sort_count_workspace(131072, 64) == 32 * 65 * 4
     assert lib.zs_scatter2scatter_workspace(100, 64, 1, 1) == 0
     assert lib.zs_scatter2scatter_workspace(100, 64, 1, 0) >= 100 * 128
+    # copy-engine all-reduce chunking: ceil(count / world) rounded up to 8 elements
+    assert lib.zs_ipc_handle_size() == 64
+    assert lib.zs_ce_allreduce_chunk(9, 2) == 8 and lib.zs_ce_allreduce_chunk(1_000_003, 2) == 500_008
+    assert lib.zs_ce_allreduce_chunk(16, 4) == 8 and lib.zs_ce_allreduce_chunk(0, 2) == 0
+    assert lib.zs_muonmd_pre_workspace(64, 1536, 1536) >= 4 * (64 * 1536 * 6 + 64 * 24 * 1536 + 64 * 24 * 6)
 
 
 def test_ops_refuse_cpu_tensors():
