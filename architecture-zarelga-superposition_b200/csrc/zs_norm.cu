@@ -193,16 +193,17 @@ template <typename T, typename C>
 __global__ void rope_kernel(T* __restrict__ q, int64_t q_row_stride, T* __restrict__ k, int64_t k_row_stride,
                             const C* __restrict__ q_cos, const C* __restrict__ q_sin, const C* __restrict__ k_cos,
                             const C* __restrict__ k_sin, int64_t cos_row_stride, int64_t rows, int seq_len,
-                            int cos_bs, int n_qh, int n_kh, int hd, int backward) {
+                            int cos_bs, int n_qh, int n_kh, int hd, int backward, int rot) {
+  // rot <= hd/2: only pairs p < rot are rotated (the others have cos 1, sin 0)
   const int half = hd / 2;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int64_t b = r / seq_len, s = r % seq_len;
     const int64_t crow = (cos_bs == 1 ? s : b * seq_len + s) * cos_row_stride;
-    const int total = (n_qh + n_kh) * half;
+    const int total = (n_qh + n_kh) * rot;
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
-      const bool isq = i < n_qh * half;
-      const int j = isq ? i : i - n_qh * half;
-      const int h = j / half, p = j - h * half;
+      const bool isq = i < n_qh * rot;
+      const int j = isq ? i : i - n_qh * rot;
+      const int h = j / rot, p = j - h * rot;
       T* base = isq ? q + r * q_row_stride + (int64_t)h * hd : k + r * k_row_stride + (int64_t)h * hd;
       const float c = to_f32<C>((isq ? q_cos : k_cos)[crow + p]);
       const float sn = to_f32<C>((isq ? q_sin : k_sin)[crow + p]);
@@ -320,14 +321,16 @@ extern "C" int zs_zrmsnorm_backward(const void* dy, const void* x, const void* w
   return ZS_OK;
 }
 
-extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos,
-                       const void* q_sin, const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch,
-                       int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim, int dtype,
-                       int table_dtype, int backward, void* stream_) {
+extern "C" int zs_rope_partial(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos,
+                               const void* q_sin, const void* k_cos, const void* k_sin, int64_t cos_row_stride,
+                               int batch, int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim,
+                               int rot_pairs, int dtype, int table_dtype, int backward, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(q && k && q_cos && q_sin && k_cos && k_sin, ZS_ERR_ARG);
   ZS_REQUIRE(batch >= 0 && seq_len >= 1 && n_q_heads >= 1 && n_kv_heads >= 1 && head_dim >= 2 && head_dim % 2 == 0,
              ZS_ERR_SHAPE);
+  ZS_REQUIRE(rot_pairs >= 0 && rot_pairs <= head_dim / 2, ZS_ERR_SHAPE);
+  if (rot_pairs == 0) return ZS_OK;
   ZS_REQUIRE(cos_batch == 1 || cos_batch == batch, ZS_ERR_SHAPE);
   ZS_BIND(q);
   const int64_t rows = (int64_t)batch * seq_len;
@@ -339,7 +342,7 @@ extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_str
       reinterpret_cast<T*>(q), q_row_stride, reinterpret_cast<T*>(k), k_row_stride,                            \
       reinterpret_cast<const C*>(q_cos), reinterpret_cast<const C*>(q_sin), reinterpret_cast<const C*>(k_cos), \
       reinterpret_cast<const C*>(k_sin), cos_row_stride, rows, seq_len, cos_batch, n_q_heads, n_kv_heads,      \
-      head_dim, backward)
+      head_dim, backward, rot_pairs)
   if (dtype == ZS_BF16 && table_dtype == ZS_F32)
     ZS_ROPE(__nv_bfloat16, float);
   else if (dtype == ZS_BF16 && table_dtype == ZS_BF16)
@@ -353,4 +356,13 @@ extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_str
 #undef ZS_ROPE
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
+}
+
+extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos,
+                       const void* q_sin, const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch,
+                       int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim, int dtype,
+                       int table_dtype, int backward, void* stream) {
+  return zs_rope_partial(q, q_row_stride, k, k_row_stride, q_cos, q_sin, k_cos, k_sin, cos_row_stride, batch,
+                         seq_len, cos_batch, n_q_heads, n_kv_heads, head_dim, head_dim / 2, dtype, table_dtype,
+                         backward, stream);
 }

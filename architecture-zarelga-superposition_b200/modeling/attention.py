@@ -19,7 +19,7 @@ import torch.nn.functional as F
 
 from zs_b200.attn import attention as attention_core
 
-from .liger_rope import LigerRopeFunction
+from .liger_rope import LigerRopeFunction, PartialRopeFunction  # noqa: F401
 from .zRMSNorm import ZeroCenteredRMSNorm
 
 
@@ -120,10 +120,13 @@ class GatedAttention(nn.Module):
         v = v.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
         q = self.q_norm(q)
         k = self.k_norm(k)
-        if self.do_rope:
-            cos = self.pos_cos_cache[position_ids]
-            sin = self.pos_sin_cache[position_ids]
-            q, k = LigerRopeFunction.apply(q, k, cos, sin, cos, sin)
+        if self.do_rope and self.pos_rope_pairs > 0:
+            # only the first pos_rope_pairs pairs rotate (the tables are the identity
+            # beyond them), so only those columns of the tables are gathered and touched
+            rp = self.pos_rope_pairs
+            cos = self.pos_cos_cache[:, :rp][position_ids]
+            sin = self.pos_sin_cache[:, :rp][position_ids]
+            q, k = PartialRopeFunction.apply(q, k, cos, sin, rp)
         seq_ids = None
         if cu_seqlens is not None:
             seq_ids = _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len)

@@ -13,7 +13,7 @@ import torch
 from zs_b200 import _lib as Z
 
 
-def _launch(q, k, q_cos, q_sin, k_cos, k_sin, backward):
+def _launch(q, k, q_cos, q_sin, k_cos, k_sin, backward, rot_pairs=None):
     Z.require_cuda(q, k, q_cos, q_sin, k_cos, k_sin)
     bsz, seq_len, n_qh, hd = q.shape
     n_kh = k.shape[2]
@@ -25,10 +25,14 @@ def _launch(q, k, q_cos, q_sin, k_cos, k_sin, backward):
     qc, qs, kc, ks = tables
     if qc.shape != kc.shape:
         raise ValueError(f"q_cos and k_cos must share a shape, got {tuple(qc.shape)} vs {tuple(kc.shape)}")
+    rot = hd // 2 if rot_pairs is None else int(rot_pairs)
+    if rot_pairs is not None and qc.shape[-1] != rot:
+        raise ValueError(f"partial RoPE tables must hold {rot} pairs per row, got {qc.shape[-1]}")
     Z.count(1)
-    Z.check(Z.lib().zs_rope(q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), qc.data_ptr(), qs.data_ptr(),
-                            kc.data_ptr(), ks.data_ptr(), qc.stride(-2), bsz, seq_len, qc.shape[0], n_qh, n_kh, hd,
-                            Z.dtype_code(q.dtype), Z.dtype_code(qc.dtype), int(backward), Z.stream_of(q)), "zs_rope")
+    Z.check(Z.lib().zs_rope_partial(q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), qc.data_ptr(),
+                                    qs.data_ptr(), kc.data_ptr(), ks.data_ptr(), qc.stride(-2), bsz, seq_len,
+                                    qc.shape[0], n_qh, n_kh, hd, rot, Z.dtype_code(q.dtype), Z.dtype_code(qc.dtype),
+                                    int(backward), Z.stream_of(q)), "zs_rope_partial")
     return q, k
 
 
@@ -53,3 +57,24 @@ class LigerRopeFunction(torch.autograd.Function):
         q_cos, q_sin, k_cos, k_sin = ctx.saved_tensors
         dq, dk = rope_backward(dq, dk, q_cos, q_sin, k_cos, k_sin)
         return dq, dk, None, None, None, None
+
+
+class PartialRopeFunction(torch.autograd.Function):
+    """RoPE on the first `rot_pairs` pairs (i, i + head_dim/2) of every head only, in
+    place: what LigerRopeFunction computes when the tables' remaining pairs are the
+    identity (cos 1, sin 0), as GatedAttention's partial position RoPE builds them
+    (modeling/attention.py:85-104), without touching the identity pairs.  Tables
+    [1 or bsz, seq, rot_pairs]."""
+
+    @staticmethod
+    def forward(ctx, q, k, cos, sin, rot_pairs):
+        q, k = _launch(q, k, cos, sin, cos, sin, backward=False, rot_pairs=rot_pairs)
+        ctx.save_for_backward(cos, sin)
+        ctx.rot = rot_pairs
+        return q, k
+
+    @staticmethod
+    def backward(ctx, dq, dk):
+        cos, sin = ctx.saved_tensors
+        dq, dk = _launch(dq, dk, cos, sin, cos, sin, backward=True, rot_pairs=ctx.rot)
+        return dq, dk, None, None, None

@@ -311,6 +311,14 @@ int zs_zrmsnorm_backward(const void* dy, const void* x, const void* weight, cons
 int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos, const void* q_sin,
             const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch, int seq_len, int cos_batch,
             int n_q_heads, int n_kv_heads, int head_dim, int dtype, int table_dtype, int backward, void* stream);
+/* zs_rope restricted to the first rot_pairs pairs of every head (0 <= rot_pairs
+ * <= head_dim/2; the tables hold rot_pairs entries per row, cos_row_stride
+ * apart): the partial RoPE of GatedAttention, whose remaining pairs have cos 1
+ * and sin 0 (modeling/attention.py:85-104), so they are left untouched. */
+int zs_rope_partial(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* q_cos,
+                    const void* q_sin, const void* k_cos, const void* k_sin, int64_t cos_row_stride, int batch,
+                    int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim, int rot_pairs, int dtype,
+                    int table_dtype, int backward, void* stream);
 
 /* ------------------------------------------------ attention core (a13, a15) */
 

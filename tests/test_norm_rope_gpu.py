@@ -103,3 +103,34 @@ def test_rope_reference_fixture(golden):
                            sin)
     np.testing.assert_allclose(dq.cpu().numpy(), gd["dq_out"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(dk.cpu().numpy(), gd["dk_out"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("rot", [8, 16, 32, 64])
+def test_partial_rope_equals_full_rope_with_identity_tail(rot):
+    """PartialRopeFunction (rotates the first `rot` pairs only) gives bit-identical
+    outputs and gradients to LigerRopeFunction on tables whose pairs beyond `rot` are
+    the identity (cos 1, sin 0), as GatedAttention builds them."""
+    from modeling.liger_rope import LigerRopeFunction, PartialRopeFunction
+
+    g = torch.Generator(device="cuda").manual_seed(rot)
+    B, S, H, Hk, hd = 2, 96, 6, 2, 128
+    q = torch.randn(B, S, H, hd, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, S, Hk, hd, device="cuda", generator=g).bfloat16()
+    ang = torch.rand(B, S, rot, device="cuda", generator=g) * 6.0
+    cos_full = torch.ones(B, S, hd // 2, device="cuda")
+    sin_full = torch.zeros(B, S, hd // 2, device="cuda")
+    cos_full[..., :rot], sin_full[..., :rot] = ang.cos(), ang.sin()
+    dq = torch.randn_like(q)
+    dk = torch.randn_like(k)
+    outs = []
+    for partial in (False, True):
+        qq, kk = q.clone().requires_grad_(True), k.clone().requires_grad_(True)
+        if partial:
+            a, b = PartialRopeFunction.apply(qq * 1, kk * 1, ang.cos(), ang.sin(), rot)
+        else:
+            a, b = LigerRopeFunction.apply(qq * 1, kk * 1, cos_full, sin_full, cos_full, sin_full)
+        # the backward rotates the incoming gradients in place: give each run its own copy
+        gq, gk = torch.autograd.grad((a, b), (qq, kk), (dq.clone(), dk.clone()))
+        outs.append((a.detach(), b.detach(), gq, gk))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
