@@ -151,8 +151,19 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, const 
     ti.mt = i;
     ti.nt = i + local;
   } else {
-    ti.mt = local / a.n_tiles;
-    ti.nt = local - ti.mt * a.n_tiles;
+    // Row tiles of a group whose output is wider than it is tall (N > rows, e.g. the
+    // classifier GEMM of the cut cross entropy) go column by column: the CTAs in flight
+    // then share a few column tiles of B and revisit the (smaller) A from L2, so B
+    // streams from DRAM once instead of once per row tile.  Otherwise row by row.
+    const int rows_g = rstart[lo + 1] - rstart[lo];
+    const int n_mt = (rows_g + TM - 1) / TM;
+    if (a.mode == MODE_ROWS && n_mt > 1 && (int64_t)a.n_tiles * BN > (int64_t)rows_g) {
+      ti.nt = local / n_mt;
+      ti.mt = local - ti.nt * n_mt;
+    } else {
+      ti.mt = local / a.n_tiles;
+      ti.nt = local - ti.mt * a.n_tiles;
+    }
   }
   if (a.mode == MODE_ROWS) {
     ti.r0 = rstart[lo] + ti.mt * TM;
