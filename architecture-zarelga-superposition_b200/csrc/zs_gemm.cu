@@ -913,13 +913,36 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             if (tgt != 0.f) atomicAdd(args.target_sum + row, tgt);
           }
         } else if (EPI == EPI_AXPBY) {
+          // the aux row's next 32 columns are fetched (raw) while this chunk is combined
+          auto fetch_aux = [&](int cc, uint4 (&w)[4]) {
+            const int c0 = ti.nt * BN + half * (BN / 2) + cc * 32;
+            const bool ok = valid && vec && cc < BN / 64 && c0 + 32 <= args.N_out;
+            const uint4* p = reinterpret_cast<const uint4*>(args.aux + (out_row * args.ld_aux + c0) * 2);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) w[q] = ok ? __ldg(p + q) : make_uint4(0, 0, 0, 0);
+          };
+          uint4 acur[4];
+          fetch_aux(0, acur);
 #pragma unroll 1
           for (int c = 0; c < BN / 64; ++c) {
             const int lc = half * (BN / 2) + c * 32;
             const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
+            uint4 anext[4];
+            fetch_aux(c + 1, anext);
             float av[32];
-            if (ncols > 0) load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, av, DT, vec);
+            if (vec && ncols == 32) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const float2 f = unpk<DT>(word_of(acur, jj));
+                av[2 * jj] = valid ? f.x : 0.f;
+                av[2 * jj + 1] = valid ? f.y : 0.f;
+              }
+            } else if (ncols > 0) {
+              load_chunk(args.aux, out_row * args.ld_aux, col0, ncols, valid, av, DT, vec);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acur[q] = anext[q];
             uint32_t r[32];
             tmem_ld_32x32b_x32(t_row + lc, r);
             tc_wait_ld();
