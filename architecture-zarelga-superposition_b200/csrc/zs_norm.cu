@@ -180,6 +180,148 @@ __global__ void __launch_bounds__(256) zrmsnorm_bwd_vec_kernel(const T* __restri
   }
 }
 
+// Residual add fused with the norm, for an f32 residual stream x and a bf16
+// branch r (the transformer block's `x + branch` followed by a norm whose output
+// feeds bf16 GEMMs):  h = x + r (f32, stored when h_out is given), y = bf16 of
+// zRMSNorm(h).  Without r it is the norm of x with a bf16 output.  Rows of
+// d = 128 * NV f32 values; warp per row, lane holds NV chunks of 4 columns.
+template <int NV>
+__global__ void __launch_bounds__(256) add_zrmsnorm_fwd_kernel(const float* __restrict__ x,
+                                                               const __nv_bfloat16* __restrict__ r,
+                                                               const float* __restrict__ w,
+                                                               float* __restrict__ h_out,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               float* __restrict__ rstd, int64_t rows, float eps) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+    float hv[NV][4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 a = __ldg(xr + j * 32 + lane);
+      hv[j][0] = a.x; hv[j][1] = a.y; hv[j][2] = a.z; hv[j][3] = a.w;
+    }
+    if (r != nullptr) {
+      const uint2* rr = reinterpret_cast<const uint2*>(r + row * D);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        float b[4];
+        Vec4<__nv_bfloat16>::unpack(__ldg(rr + j * 32 + lane), b);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) hv[j][v] = hv[j][v] + b[v];
+      }
+      if (h_out != nullptr) {
+        float4* hr = reinterpret_cast<float4*>(h_out + row * D);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) hr[j * 32 + lane] = make_float4(hv[j][0], hv[j][1], hv[j][2], hv[j][3]);
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) ss = fmaf(hv[j][v], hv[j][v], ss);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float rs = rsqrtf(ss / (float)D + eps);
+    if (lane == 0 && rstd != nullptr) rstd[row] = rs;
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    uint2* yr = reinterpret_cast<uint2*>(y + row * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 wv = __ldg(wr + j * 32 + lane);
+      const float o[4] = {(hv[j][0] * rs) * (1.0f + wv.x), (hv[j][1] * rs) * (1.0f + wv.y),
+                          (hv[j][2] * rs) * (1.0f + wv.z), (hv[j][3] * rs) * (1.0f + wv.w)};
+      yr[j * 32 + lane] = Vec4<__nv_bfloat16>::pack(o);
+    }
+  }
+}
+
+// Backward of add_zrmsnorm_fwd_kernel: dy bf16, h (the saved f32 norm input),
+// dh_in (optional f32: the gradient reaching h from its other use, the residual
+// path); dx = dh_in + the norm's input gradient (f32, the gradient of x), dr =
+// bf16 of dx (optional, the gradient of the bf16 branch r); dweight partials per
+// block as zrmsnorm_bwd_vec_kernel.
+template <int NV>
+__global__ void __launch_bounds__(256) add_zrmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                               const float* __restrict__ h,
+                                                               const float* __restrict__ w,
+                                                               const float* __restrict__ rstd,
+                                                               const float* __restrict__ dh_in,
+                                                               float* __restrict__ dx,
+                                                               __nv_bfloat16* __restrict__ dr,
+                                                               float* __restrict__ dw_part, int64_t rows) {
+  constexpr int D = 128 * NV;
+  extern __shared__ float sdw[];  // [8][D] per-warp dw, then [D] of (1 + w)
+  float* swp = sdw + 8 * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) swp[c] = 1.0f + w[c];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[j][v] = 0.f;
+  const int64_t warps = (int64_t)gridDim.x * 8;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += warps) {
+    const float4* hr = reinterpret_cast<const float4*>(h + row * D);
+    const uint2* gr = reinterpret_cast<const uint2*>(dy + row * D);
+    const float rs = __ldg(rstd + row);
+    float xv[NV][4], gv[NV][4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 a = __ldg(hr + j * 32 + lane);
+      xv[j][0] = a.x; xv[j][1] = a.y; xv[j][2] = a.z; xv[j][3] = a.w;
+      Vec4<__nv_bfloat16>::unpack(__ldg(gr + j * 32 + lane), gv[j]);
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int c = (j * 32 + lane) * 4 + v;
+        const float n = xv[j][v] * rs;
+        dot = fmaf(gv[j][v] * swp[c], n, dot);
+        acc[j][v] = fmaf(gv[j][v], n, acc[j][v]);
+      }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / (float)D;
+    const float4* ehr = dh_in != nullptr ? reinterpret_cast<const float4*>(dh_in + row * D) : nullptr;
+    float4* dxr = reinterpret_cast<float4*>(dx + row * D);
+    uint2* drr = dr != nullptr ? reinterpret_cast<uint2*>(dr + row * D) : nullptr;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      float o[4];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int c = (j * 32 + lane) * 4 + v;
+        const float n = xv[j][v] * rs;
+        o[v] = rs * (gv[j][v] * swp[c] - n * mean);
+      }
+      if (ehr != nullptr) {
+        const float4 e = __ldg(ehr + j * 32 + lane);
+        o[0] = e.x + o[0]; o[1] = e.y + o[1]; o[2] = e.z + o[2]; o[3] = e.w + o[3];
+      }
+      dxr[j * 32 + lane] = make_float4(o[0], o[1], o[2], o[3]);
+      if (drr != nullptr) drr[j * 32 + lane] = Vec4<__nv_bfloat16>::pack(o);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) sdw[warp * D + (j * 32 + lane) * 4 + v] = acc[j][v];
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t += sdw[q * D + c];
+    dw_part[(int64_t)blockIdx.x * D + c] = t;
+  }
+}
+
 __global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int d, float* __restrict__ out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
@@ -318,6 +460,92 @@ extern "C" int zs_zrmsnorm_backward(const void* dy, const void* x, const void* w
   ZS_CUDA_TRY(cudaGetLastError());
   sum_rows_kernel<<<(d + 255) / 256, 256, 0, stream>>>(part, (int)blocks, d, dweight);
   ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+static bool addnorm_nv_ok(int d) {
+  const int nv = d % 128 == 0 ? d / 128 : 0;
+  return nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 12 || nv == 16;
+}
+
+template <int NV>
+static int launch_add_zrmsnorm_fwd(const float* x, const void* r, const float* weight, float* h_out, void* y,
+                                   float* rstd, int64_t rows, float eps, cudaStream_t stream) {
+  int64_t blocks = (rows + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  add_zrmsnorm_fwd_kernel<NV><<<(unsigned)blocks, 256, 0, stream>>>(
+      x, reinterpret_cast<const __nv_bfloat16*>(r), weight, h_out, reinterpret_cast<__nv_bfloat16*>(y), rstd, rows,
+      eps);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+template <int NV>
+static int launch_add_zrmsnorm_bwd(const void* dy, const float* h, const float* weight, const float* rstd,
+                                   const float* dh_in, float* dx, void* dr, float* part, int64_t blocks,
+                                   int64_t rows, cudaStream_t stream) {
+  const size_t shv = (size_t)9 * 128 * NV * sizeof(float);
+  if (shv > 48 * 1024)
+    ZS_CUDA_TRY(cudaFuncSetAttribute(add_zrmsnorm_bwd_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)shv));
+  add_zrmsnorm_bwd_kernel<NV><<<(unsigned)blocks, 256, shv, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy), h, weight, rstd, dh_in, dx, reinterpret_cast<__nv_bfloat16*>(dr),
+      part, rows);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" int zs_add_zrmsnorm_forward(const float* x, const void* r, const float* weight, float* h_out, void* y,
+                                       float* rstd, int64_t rows, int d, float eps, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(x && weight && y, ZS_ERR_ARG);
+  ZS_REQUIRE(rows >= 0 && addnorm_nv_ok(d), ZS_ERR_SHAPE);
+  ZS_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(weight) |
+               reinterpret_cast<uintptr_t>(h_out) | reinterpret_cast<uintptr_t>(y)) & 15) == 0,
+             ZS_ERR_ALIGN);
+  ZS_BIND(x);
+  if (rows == 0) return ZS_OK;
+  switch (d / 128) {
+    case 1: return launch_add_zrmsnorm_fwd<1>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+    case 2: return launch_add_zrmsnorm_fwd<2>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+    case 4: return launch_add_zrmsnorm_fwd<4>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+    case 8: return launch_add_zrmsnorm_fwd<8>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+    case 12: return launch_add_zrmsnorm_fwd<12>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+    default: return launch_add_zrmsnorm_fwd<16>(x, r, weight, h_out, y, rstd, rows, eps, stream);
+  }
+}
+
+extern "C" int zs_add_zrmsnorm_backward(const void* dy, const float* h, const float* weight, const float* rstd,
+                                        const float* dh_in, float* dx, void* dr, float* dweight, int64_t rows, int d,
+                                        void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(dy && h && weight && rstd && dx && dweight, ZS_ERR_ARG);
+  ZS_REQUIRE(rows >= 0 && addnorm_nv_ok(d), ZS_ERR_SHAPE);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_zrmsnorm_backward_workspace(rows, d), ZS_ERR_WORKSPACE);
+  ZS_REQUIRE(((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(dh_in) |
+               reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dr)) & 15) == 0,
+             ZS_ERR_ALIGN);
+  ZS_BIND(h);
+  int64_t blocks = (rows + 7) / 8;
+  if (blocks > 296) blocks = 296;
+  if (blocks < 1) blocks = 1;
+  float* part = reinterpret_cast<float*>(workspace);
+  int rc;
+  switch (d / 128) {
+    case 1: rc = launch_add_zrmsnorm_bwd<1>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+    case 2: rc = launch_add_zrmsnorm_bwd<2>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+    case 4: rc = launch_add_zrmsnorm_bwd<4>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+    case 8: rc = launch_add_zrmsnorm_bwd<8>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+    case 12: rc = launch_add_zrmsnorm_bwd<12>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+    default: rc = launch_add_zrmsnorm_bwd<16>(dy, h, weight, rstd, dh_in, dx, dr, part, blocks, rows, stream); break;
+  }
+  if (rc != ZS_OK) return rc;
+  if (rows > 0) {
+    sum_rows_kernel<<<(d + 255) / 256, 256, 0, stream>>>(part, (int)blocks, d, dweight);
+    ZS_CUDA_TRY(cudaGetLastError());
+  } else {
+    ZS_CUDA_TRY(cudaMemsetAsync(dweight, 0, (size_t)d * sizeof(float), stream));
+  }
   return ZS_OK;
 }
 

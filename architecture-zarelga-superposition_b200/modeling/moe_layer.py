@@ -35,7 +35,9 @@ class MoELayer(nn.Module):
         nn.init.normal_(self.routed_experts.experts.weight, mean=0.0, std=std)
         nn.init.normal_(self.routed_experts.output_experts.weight, mean=0.0, std=std)
 
-    def forward(self, hidden_states, unpad_indices=None):
+    def forward(self, hidden_states, unpad_indices=None, out_dtype=None):
+        """(out, topk_idx); out in the input's dtype, or out_dtype when given (a block whose
+        norm already produced the bf16 input passes its f32 residual dtype)."""
         if unpad_indices is not None:
             bsz, seq_len, d = hidden_states.shape
             x = hidden_states.reshape(bsz * seq_len, d).index_select(0, unpad_indices).unsqueeze(0)
@@ -44,7 +46,7 @@ class MoELayer(nn.Module):
         k = self.n_experts_per_token
         se = self.shared_experts
         E, f = self.gate.weight.size(0), se.gate_proj.weight.size(0)
-        in_dtype = x.dtype
+        in_dtype = x.dtype if out_dtype is None else out_dtype
         if torch.is_autocast_enabled() and x.dtype == torch.float32:
             x = x.to(torch.get_autocast_dtype("cuda"))
         d = x.size(-1)

@@ -55,6 +55,8 @@ _SIGNATURES = {
     "zs_zrmsnorm_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _i32, _i32, _vp]),
     "zs_zrmsnorm_backward_workspace": (_sz, [_i64, _i32]),
     "zs_zrmsnorm_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "zs_add_zrmsnorm_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "zs_add_zrmsnorm_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _sz, _vp]),
     "zs_rope_partial": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64] + [_i32] * 10 + [_vp]),
     "zs_rope": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                        _i32, _vp]),

@@ -294,6 +294,25 @@ int zs_zrmsnorm_forward(const void* x, const void* weight, void* y, float* rstd,
  * d <= 12288; workspace: zs_zrmsnorm_backward_workspace(rows, d) bytes.
  */
 size_t zs_zrmsnorm_backward_workspace(int64_t rows, int d);
+/*
+ * The transformer block's residual add fused with the next zRMSNorm (no
+ * counterpart as one function in the reference; it computes
+ * modeling/transformer_block.py:19-46's `h = x + branch` and the norm of
+ * modeling/zRMSNorm.py:13-17 with the output cast that the following autocast
+ * GEMM applies).  x f32 [rows, d], r bf16 [rows, d] or NULL, d = 128 * {1, 2, 4,
+ * 8, 12, 16}, 16-byte aligned:
+ *   forward:  h = x + r (f32, written to h_out when both are given), y = bf16 of
+ *             zRMSNorm(h) (or of x without r), rstd as zs_zrmsnorm_forward;
+ *   backward: dy bf16 (gradient of y), h the saved norm input, dh_in f32 or NULL
+ *             (gradient reaching h from the residual path); dx = dh_in + the
+ *             norm's input gradient (f32), dr = bf16 of dx (or NULL), dweight
+ *             f32 [d]; workspace zs_zrmsnorm_backward_workspace(rows, d) bytes.
+ */
+int zs_add_zrmsnorm_forward(const float* x, const void* r, const float* weight, float* h_out, void* y, float* rstd,
+                            int64_t rows, int d, float eps, void* stream);
+int zs_add_zrmsnorm_backward(const void* dy, const float* h, const float* weight, const float* rstd,
+                             const float* dh_in, float* dx, void* dr, float* dweight, int64_t rows, int d,
+                             void* workspace, size_t workspace_bytes, void* stream);
 int zs_zrmsnorm_backward(const void* dy, const void* x, const void* weight, const float* rstd, void* dx,
                          float* dweight, int64_t rows, int d, int x_dtype, int w_dtype, void* workspace,
                          size_t workspace_bytes, void* stream);

@@ -49,3 +49,41 @@ def test_untrained_loss_is_near_log_vocab_and_matches_materialised_ce():
                                             t.view(-1))
     assert abs(loss.item() - ref.item()) / ref.item() < 2e-2
     assert abs(loss.item() - math.log(cfg.vocab_size)) < 2.0
+
+
+def test_fused_add_norm_block_matches_reference_op_sequence():
+    """The block's fused residual-add + zRMSNorm path (bf16 norm outputs under autocast)
+    against the reference op sequence (add, f32 norm, autocast casts): block output,
+    input gradient and every parameter gradient agree to reduction-order rounding."""
+    from modeling.transformer_block import TransformerBlock
+
+    cfg, m = _tiny(layers=1)
+    blk = m.layers[0]
+    with torch.no_grad():
+        for n in (blk.input_layernorm, blk.post_attention_layernorm):
+            n.weight.normal_(0, 0.1)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x0 = torch.randn(2, 256, 256, device="cuda", generator=g)
+    dy = torch.randn(2, 256, 256, device="cuda", generator=g)
+    outs = []
+    for fused in (False, True):
+        TransformerBlock.fused_add_norm = fused
+        try:
+            blk.zero_grad(set_to_none=True)
+            x = x0.clone().requires_grad_(True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y, _ = blk(x)
+            y.backward(dy)
+            torch.cuda.synchronize()
+            outs.append((y.detach().float(), x.grad.clone(),
+                         {n: p.grad.detach().float().clone() for n, p in blk.named_parameters() if p.grad is not None}))
+        finally:
+            TransformerBlock.fused_add_norm = True
+    (ya, xa, ga), (yb, xb, gb) = outs
+    assert yb.dtype == ya.dtype
+    assert ((ya - yb).norm() / ya.norm()).item() < 5e-3
+    cos = lambda a, b: (a.flatten() @ b.flatten() / (a.norm() * b.norm())).item()  # noqa: E731
+    assert cos(xa, xb) > 0.9999
+    assert ga.keys() == gb.keys()
+    for n in ga:
+        assert cos(ga[n], gb[n]) > 0.999, n
