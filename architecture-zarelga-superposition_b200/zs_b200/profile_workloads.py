@@ -7,7 +7,8 @@ attention: config 4's attention shape (B=8, S=4096, H=12, Hkv=4, hd=128, causal,
 two warm-up forward+backward passes, then one more.
 muonmd:    one md_decoupled_step on config 4's W1 expert stack [64, 1536, 1536] f32 (gain
 mode "both", Frobenius sphere) after one warm-up step.
-norm_rope: zRMSNorm forward + backward on config 4's residual rows [32768, 1536] f32 and
+norm_rope: zRMSNorm forward + backward on config 4's residual rows [32768, 1536] f32, the
+           fused residual add + zRMSNorm (bf16 branch, bf16 output) forward + backward, and
            partial RoPE forward + backward on q [8, 4096, 12, 128] / k [8, 4096, 4, 128] bf16
            (8 of 64 pairs rotated, config 4's pos_rope_dims = 16), two warm-up passes, then one more.
 routing:   config 2 routing: sigmoid + biased top-8 of [16384, 64] bf16 probabilities,
@@ -63,7 +64,7 @@ def muonmd(passes: int = 2) -> None:
 
 def norm_rope(passes: int = 3) -> None:
     from modeling.liger_rope import PartialRopeFunction
-    from modeling.zRMSNorm import ZRMSNormFunction
+    from modeling.zRMSNorm import AddZRMSNormFunction, ZRMSNormFunction
 
     g = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(32768, 1536, device="cuda", generator=g).requires_grad_(True)
@@ -74,9 +75,14 @@ def norm_rope(passes: int = 3) -> None:
     # config 4 keeps ModelConfig's pos_rope_dims = 16: the first 8 of 64 pairs rotate
     ang = torch.arange(4096, device="cuda", dtype=torch.float32)[:, None] * torch.logspace(0, -4, 8, device="cuda")
     cos, sin = ang.cos().expand(8, 4096, 8).contiguous(), ang.sin().expand(8, 4096, 8).contiguous()
+    br = torch.randn(32768, 1536, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    dyb = dy.bfloat16()
     for _ in range(passes):
         y = ZRMSNormFunction.apply(x, w, 1e-6)
         torch.autograd.grad(y, (x, w), dy)
+        # the block's fused residual add + norm with a bf16 output (f32 stream, bf16 branch)
+        h, yb = AddZRMSNormFunction.apply(x, br, w, 1e-6)
+        torch.autograd.grad((h, yb), (x, br, w), (dy, dyb))
         qq, kk = q.clone().requires_grad_(True), k.clone().requires_grad_(True)
         qo, ko = PartialRopeFunction.apply(qq * 1, kk * 1, cos, sin, 8)
         torch.autograd.grad((qo, ko), (qq, kk), (torch.ones_like(qo), torch.ones_like(ko)))
