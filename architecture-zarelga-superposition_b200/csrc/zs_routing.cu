@@ -510,9 +510,8 @@ extern "C" int zs_moe_gate_topk_backward(const void* gate_probs, int probs_dtype
 // ----------------------------------------------- allocation-free variant --
 //
 // Some callers cannot allocate device memory at the point where they route
-// tokens: code running inside a CUDA stream capture that must not add
-// allocation nodes, runtimes that own a fixed memory pool and forbid
-// cudaMalloc after start-up, or plain C callers without an allocator.  For
+// tokens: runtimes that own a fixed memory pool and forbid cudaMalloc after
+// start-up, or plain C callers without an allocator.  For
 // them zs_flatten_sort_count_noalloc keeps its scratch (the per-chunk expert
 // histograms) in the fixed device array below instead of a caller workspace.
 //

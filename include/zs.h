@@ -109,9 +109,8 @@ int zs_flatten_sort_count(const int64_t* expert_idxs, int64_t n, int num_experts
 /*
  * Allocation-free variant of zs_flatten_sort_count.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory where
- * they route tokens (inside a CUDA stream capture that must not add
- * allocation nodes, runtimes with a fixed memory pool, C callers without an
- * allocator).  Same inputs, outputs and results as zs_flatten_sort_count; the
+ * they route tokens (runtimes that own a fixed device memory pool and forbid
+ * cudaMalloc after start-up, C callers without an allocator).  Same inputs, outputs and results as zs_flatten_sort_count; the
  * scratch lives in a fixed 1 MiB device array inside the library (held on
  * every GPU that loads the library until the process exits), so the problem
  * must satisfy ceil(n / 4096) * (num_experts + 1) <= 262144 (the value of

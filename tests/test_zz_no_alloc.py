@@ -1,8 +1,8 @@
 """The allocation-free flatten_sort_count entry point, called through the C ABI.
 
-Callers that cannot allocate device memory where they route tokens (inside a
-CUDA stream capture, under a fixed memory pool, or from C without an
-allocator) use zs_flatten_sort_count_noalloc, whose scratch is a fixed array
+Callers that cannot allocate device memory where they route tokens (runtimes
+with a fixed memory pool that forbid cudaMalloc after start-up, or C callers
+without an allocator) use zs_flatten_sort_count_noalloc, whose scratch is a fixed array
 inside the library.  Its results must equal those of the workspace-taking
 zs_flatten_sort_count, call after call (the shared array keeps the previous
 call's contents).  This file is collected last so that a failing run that
