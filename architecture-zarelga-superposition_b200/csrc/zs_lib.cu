@@ -8,4 +8,5 @@
 #include "zs_attn.cu"
 #include "zs_muon.cu"
 #include "zs_comm.cu"
+#include "zs_sparse.cu"
 #include "zs_api.cu"

@@ -24,6 +24,19 @@ NS_COEFFS = (3.4445, -4.7750, 2.0315)
 _RAW_GAIN_INIT = 0.5413248546129181  # softplus^-1(1): every gain starts at exactly 1
 
 
+def newton_schulz_flops(batch, m, n, steps):
+    """Tensor FLOPs the kernels execute for `steps` iterations on `batch` m x n matrices
+    (m <= n): X X^T and A A on 256-row pair tiles compute only the upper triangle of tiles
+    when m is a multiple of 256; B X is a full product."""
+    if m % 256 == 0:
+        t = m // 256
+        sym = t * (t + 1) // 2 * 256 * 256
+        per = 2.0 * sym * n + 2.0 * sym * m + 2.0 * m * m * n
+    else:
+        per = 4.0 * m * m * n + 2.0 * m * m * m
+    return per * batch * steps
+
+
 def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int) -> torch.Tensor:
     """Quintic Newton-Schulz orthogonalisation of the trailing two dims of G
     (batched over leading dims), in bf16; returns a bf16 tensor of G's shape."""
@@ -51,7 +64,7 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int) -> torch.Tensor:
                      device=G.device)
     a, b, c = NS_COEFFS
     Z.count(1 + 3 * int(steps))
-    with Z.timed("newton_schulz5"):
+    with Z.timed("newton_schulz5", newton_schulz_flops(batch, mp, np_, steps)):
         Z.check(Z.lib().zs_newton_schulz5(Xc.data_ptr(), out.data_ptr(), batch, mp, np_, int(steps), a, b, c,
                                           ws.data_ptr(), ws.numel(), Z.ZS_BF16, Z.stream_of(Xc)),
                 "zs_newton_schulz5")

@@ -97,7 +97,7 @@ def _launch_scatter2scatter(output, W, X, k, sei, ssi, b, x_grouped, y_grouped, 
     ws_bytes = Z.lib().zs_scatter2scatter_workspace(n, K, code, int(bool(x_grouped)))
     ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=X.device)
     Z.count(1 if x_grouped else 2)
-    with Z.timed(tag):
+    with Z.timed(tag, 2.0 * n * K * N):
       Z.check(Z.lib().zs_scatter2scatter(
         out.data_ptr(), out.stride(0), Wc.data_ptr(), E, K, N, Wc.stride(0), Wc.stride(1), Wc.stride(2),
         Xc.data_ptr(), Xc.size(0), Xc.stride(0),
@@ -128,7 +128,7 @@ def group_bwd_W(DY, X, expert_offsets, E, has_bias=False, tag="groupXtY"):
     DWt = torch.empty((E, DY.size(-1), X.size(-1)), device=DY.device, dtype=DY.dtype)
     DW = DWt.permute(0, 2, 1)
     Db = torch.empty((E, DY.size(-1)), device=DY.device, dtype=DY.dtype) if has_bias else None
-    with Z.timed(tag):
+    with Z.timed(tag, 2.0 * DY.size(0) * DY.size(-1) * X.size(-1)):
         groupXtY_compileable(E, DW, Db, DY, X, expert_offsets)
     return DW, Db
 

@@ -46,7 +46,7 @@ def up_swiglu(xg, W1, sorted_expert_idxs, expert_offsets):
     act = torch.empty((n, f), dtype=xg.dtype, device=xg.device)
     hfull = torch.empty((n, f2), dtype=xg.dtype, device=xg.device)
     Z.count(1)
-    with Z.timed("up_swiglu"):
+    with Z.timed("up_swiglu", 4.0 * n * d * f):
         Z.check(Z.lib().zs_expert_up_swiglu(act.data_ptr(), hfull.data_ptr(), W1.data_ptr(), E, d, f,
                                             xg.data_ptr(), xg.stride(0), sorted_expert_idxs.data_ptr(),
                                             expert_offsets.data_ptr(), n, Z.dtype_code(xg.dtype), Z.stream_of(xg)),
@@ -61,7 +61,7 @@ def down_dswiglu(dyg, W2, hfull, sorted_expert_idxs, expert_offsets):
     E, _, f = W2.shape
     dh = torch.empty((n, 2 * f), dtype=dyg.dtype, device=dyg.device)
     Z.count(1)
-    with Z.timed("down_dx"):
+    with Z.timed("down_dx", 2.0 * n * d * f):
         Z.check(Z.lib().zs_expert_down_dswiglu(dh.data_ptr(), hfull.data_ptr(), W2.data_ptr(), E, d, f,
                                                dyg.data_ptr(), dyg.stride(0), sorted_expert_idxs.data_ptr(),
                                                expert_offsets.data_ptr(), n, Z.dtype_code(dyg.dtype),
@@ -95,13 +95,13 @@ def accumulate_weight_grad(W, DY, X, offs, tag):
         if g is None:
             g = W.grad = torch.empty_like(W, memory_format=torch.contiguous_format)
             acc = 0
-        with Z.timed(tag):
+        with Z.timed(tag, 2.0 * X.size(0) * K * N):
             Z.check(Z.lib().zs_group_xty_f32(E, g.data_ptr(), N * K, 1, K, DY.data_ptr(), DY.stride(0),
                                              X.data_ptr(), X.stride(0), X.size(0), K, N, offs.data_ptr(),
                                              Z.dtype_code(X.dtype), acc, Z.stream_of(X)), "zs_group_xty_f32")
     else:
         out = torch.empty_like(W, memory_format=torch.contiguous_format) if g is None else torch.empty_like(g)
-        with Z.timed(tag):
+        with Z.timed(tag, 2.0 * X.size(0) * K * N):
             Z.check(Z.lib().zs_group_xty(E, out.data_ptr(), N * K, 1, K, None, 0, 0, DY.data_ptr(), DY.stride(0),
                                          X.data_ptr(), X.stride(0), X.size(0), K, N, offs.data_ptr(),
                                          Z.dtype_code(X.dtype), Z.stream_of(X)), "zs_group_xty")

@@ -81,6 +81,11 @@ _SIGNATURES = {
     "zs_xent_forward_workspace": (_sz, [_i64, _i64]),
     "zs_xent_forward": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                _i32, _vp]),
+    "zs_embedding_bag_forward": (_i32, [_vp, _i64, _i64, _vp, _i64, _i32, _f32, _vp, _vp]),
+    "zs_embedding_bag_backward": (_i32, [_vp, _i64, _i32, _i64, _f32, _vp, _vp]),
+    "zs_sparse_rmsprop_workspace": (_sz, [_i64, _i64]),
+    "zs_sparse_rmsprop_step": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _f32,
+                                      ctypes.c_double, _f32, _i32, _vp, _sz, _vp]),
     "zs_xent_backward_workspace": (_sz, [_i64, _i64, _i32]),
     "zs_xent_backward": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                 _i64, _vp, _sz, _i32, _vp]),
@@ -159,8 +164,9 @@ def clear_device_error(device=None) -> None:
 
 class _Instr:
     launches = 0          # kernels of libzs.so launched through these bindings
-    timing = False        # record CUDA events around the grouped GEMM launches
-    events = {}           # name -> [(start_event, end_event), ...]
+    timing = False        # record CUDA events around the instrumented launches
+    events = {}           # name -> [(start_event, end_event, flops), ...] of eager launches
+    graph_events = {}     # the same for launches recorded into a CUDA graph (re-recorded by every replay)
 
 
 INSTR = _Instr()
@@ -171,23 +177,31 @@ def count(n: int = 1) -> None:
 
 
 class timed:
-    """Record a CUDA event pair around a launch when INSTR.timing is set."""
+    """Record a CUDA event pair around a launch when INSTR.timing is set.
 
-    __slots__ = ("name", "s")
+    `flops` is the launch's algorithmic work (tensor-core FLOPs) for the roofline.  Inside a
+    CUDA-graph capture the events are external event-record nodes of the graph, so every
+    replay re-records them; they are kept in INSTR.graph_events (the last replay's times)."""
 
-    def __init__(self, name):
+    __slots__ = ("name", "s", "flops", "graph")
+
+    def __init__(self, name, flops=0.0):
         self.name = name
         self.s = None
+        self.flops = float(flops)
+        self.graph = False
 
     def __enter__(self):
         if INSTR.timing:
-            self.s = torch.cuda.Event(enable_timing=True)
+            self.graph = torch.cuda.is_current_stream_capturing()
+            self.s = torch.cuda.Event(enable_timing=True, external=self.graph)
             self.s.record()
         return self
 
     def __exit__(self, *exc):
         if self.s is not None:
-            e = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True, external=self.graph)
             e.record()
-            INSTR.events.setdefault(self.name, []).append((self.s, e))
+            (INSTR.graph_events if self.graph else INSTR.events).setdefault(self.name, []).append(
+                (self.s, e, self.flops))
         return False

@@ -24,6 +24,16 @@ import torch
 from . import _lib as Z
 
 
+def attention_flops(B, S, H, hd, window=0):
+    """Algorithmic tensor FLOPs of the causal forward (S = QK^T and O = PV over the
+    visible key positions of every query: i+1, or min(i+1, window))."""
+    if window and window < S:
+        visible = window * (window + 1) // 2 + (S - window) * window
+    else:
+        visible = S * (S + 1) // 2
+    return 4.0 * B * H * hd * visible
+
+
 def seg_start_from_seq_ids(seq_ids: torch.Tensor) -> torch.Tensor:
     """int32 [B, S]: first row position of each token's sequence, -1 on padding (no host sync)."""
     B, S = seq_ids.shape
@@ -43,7 +53,7 @@ class _Attention(torch.autograd.Function):
         o = torch.empty_like(q)
         lse = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
         L = Z.lib()
-        with Z.timed("attention_fwd"):
+        with Z.timed("attention_fwd", attention_flops(B, S, H, hd, window)):
             Z.check(L.zs_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                                            B, S, H, Hkv, hd, window, Z.ptr(seg_start), Z.ptr(k_sink),
                                            Z.dtype_code(k_sink.dtype) if k_sink is not None else 0, scale,
@@ -65,7 +75,7 @@ class _Attention(torch.autograd.Function):
         D = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
         ds_sink = torch.empty(B, H, S, dtype=torch.float32, device=q.device) if k_sink is not None else None
         L = Z.lib()
-        with Z.timed("attention_bwd"):
+        with Z.timed("attention_bwd", 2.5 * attention_flops(B, S, H, hd, ctx.window)):
             Z.check(L.zs_attention_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
                                             lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                             D.data_ptr(), B, S, H, Hkv, hd, ctx.window, Z.ptr(seg_start),

@@ -53,8 +53,9 @@ def all_reduce_counts(counts: torch.Tensor, process_group=None) -> torch.Tensor:
 def all_gather_sparse(grad: torch.Tensor, process_group=None) -> torch.Tensor:
     """Sum of every rank's sparse COO gradient (same dense shape), as one uncoalesced COO tensor."""
     world = dist.get_world_size(process_group)
-    g = grad.coalesce() if not grad.is_coalesced() else grad
-    idx, val = g.indices(), g.values()
+    # duplicates need no coalescing here: the sum over ranks is the concatenation of the
+    # ranks' entries, and the sparse-row optimizer sums duplicates itself
+    idx, val = grad._indices(), grad._values()
     n = torch.tensor([idx.size(1)], device=idx.device, dtype=torch.long)
     sizes = [torch.zeros_like(n) for _ in range(world)]
     dist.all_gather(sizes, n, group=process_group)

@@ -30,7 +30,7 @@ class FusedLinearCrossEntropy(torch.autograd.Function):
         denom = torch.empty((), dtype=torch.float32, device=dev)
         ws = torch.empty(int(Z.lib().zs_xent_forward_workspace(T, V)), dtype=torch.uint8, device=dev)
         Z.count(4)
-        with Z.timed("xent_fwd"):
+        with Z.timed("xent_fwd", 2.0 * T * V * D):
             Z.check(Z.lib().zs_xent_forward(h.data_ptr(), T, D, h.stride(0), c.data_ptr(), V, c.stride(0),
                                             lab.data_ptr(), lab.size(1), sc.data_ptr(), lse.data_ptr(),
                                             row_loss.data_ptr(), loss.data_ptr(), denom.data_ptr(), ws.data_ptr(),
@@ -57,7 +57,7 @@ class FusedLinearCrossEntropy(torch.autograd.Function):
                          device=dev)
         nchunks = (V + vch - 1) // vch
         Z.count(nchunks * (1 + int(need_h) + int(need_c)))
-        with Z.timed("xent_bwd"):
+        with Z.timed("xent_bwd", 2.0 * T * V * D * (1 + int(need_h) + int(need_c))):
             Z.check(Z.lib().zs_xent_backward(h.data_ptr(), T, D, h.stride(0), c.data_ptr(), V, c.stride(0),
                                              lab.data_ptr(), lab.size(1), sc.data_ptr(), lse.data_ptr(), g.data_ptr(),
                                              denom.data_ptr(), Z.ptr(dh), Z.ptr(dc), vch, ws.data_ptr(), ws.numel(),

@@ -301,7 +301,7 @@ def run_gpu(args):
     # per-kernel durations of the grouped GEMM launches (same stream, same region)
     kern = {}
     for name, evs in Z.INSTR.events.items():
-        durs = [s.elapsed_time(e) for s, e in evs]
+        durs = [s.elapsed_time(e) for s, e, *_ in evs]
         kern[name] = {"launches": len(durs), "avg_ms": sum(durs) / len(durs), "total_ms": sum(durs)}
     gemm_ms = sum(v["total_ms"] for v in kern.values())
 
@@ -462,7 +462,7 @@ def run_config3(args):
     ms = t0.elapsed_time(t1)
     kern = {}
     for name, evs in Z.INSTR.events.items():
-        durs = [a.elapsed_time(b) for a, b in evs]
+        durs = [a.elapsed_time(b) for a, b, *_ in evs]
         kern[name] = {"launches": len(durs), "avg_ms": sum(durs) / len(durs)}
     _, sustained, _, src = measured_peaks()
     fl = 3 * 2 * T * V * D  # algorithmic: forward logits, dH, dW (the backward's logit recompute excluded)
@@ -482,6 +482,77 @@ def run_config3(args):
                          "traffic": None, "peak_source": f"{src} bf16_tflops_sustained", "kernels": kern},
             "gpu_launches": Z.INSTR.launches - l0, "clocks": clocks, "device_error": Z.device_error()}
     print(json.dumps(line), flush=True)
+
+
+KERNEL_FAMILIES = {
+    # grouped_gemm_kernel (csrc/zs_gemm.cu): every tcgen05 GEMM launch of the step
+    "grouped_gemm_kernel": ("newton_schulz5", "up_swiglu", "down_dx", "down_fwd", "down_dw", "up_dw", "up_dx",
+                            "xent_fwd", "xent_bwd", "scatter2scatter", "groupXtY"),
+    # attn_fwd_kernel / attn_bwd_* (csrc/zs_attn.cu)
+    "attention": ("attention_fwd", "attention_bwd"),
+}
+
+
+def _family(name):
+    for fam, keys in KERNEL_FAMILIES.items():
+        if any(name.startswith(k) for k in keys):
+            return fam
+    return None
+
+
+def kernel_table(steps):
+    """Per instrumented region: launches per step, ms per step and achieved TFLOP/s, from the
+    CUDA events recorded in the timed region (eager launches: every step; launches inside
+    the recorded optimizer graph: the last replay, which is one step)."""
+    from zs_b200 import _lib as Z
+
+    out = {}
+    for name, evs in Z.INSTR.events.items():
+        durs = [s.elapsed_time(e) for s, e, _ in evs]
+        fl = sum(f for _, _, f in evs)
+        out[name] = {"launches_per_step": len(durs) / steps, "ms_per_step": sum(durs) / steps,
+                     "tflop_per_step": fl / steps / 1e12, "graph": False}
+    for name, evs in Z.INSTR.graph_events.items():
+        durs = [s.elapsed_time(e) for s, e, _ in evs]
+        fl = sum(f for _, _, f in evs)
+        row = {"launches_per_step": len(durs), "ms_per_step": sum(durs), "tflop_per_step": fl / 1e12, "graph": True}
+        prev = out.get(name)
+        if prev is not None:  # both eager and recorded launches of one region
+            row = {k: (prev[k] + row[k]) if k != "graph" else True for k in row}
+        out[name] = row
+    for r in out.values():
+        r["achieved_tflops"] = (r["tflop_per_step"] / (r["ms_per_step"] * 1e-3)) if r["ms_per_step"] > 0 else None
+    return out
+
+
+def roofline_from_table(table, clocks):
+    """Roofline of the dominant kernel family (largest share of the instrumented time):
+    achieved = its algorithmic FLOPs / its summed CUDA-event time.  The peak is the burst
+    cuBLAS figure when the timed region ran at the maximum SM clock, else the sustained one
+    (the power-capped clock the sustained figure was measured at)."""
+    burst, sustained, _, src = measured_peaks()
+    fams = {}
+    for name, r in table.items():
+        fam = _family(name)
+        if fam is None:
+            continue
+        f = fams.setdefault(fam, {"ms_per_step": 0.0, "tflop_per_step": 0.0, "regions": []})
+        f["ms_per_step"] += r["ms_per_step"]
+        f["tflop_per_step"] += r["tflop_per_step"]
+        f["regions"].append(name)
+    if not fams:
+        return None
+    for f in fams.values():
+        f["achieved_tflops"] = f["tflop_per_step"] / (f["ms_per_step"] * 1e-3) if f["ms_per_step"] > 0 else None
+    dom = max(fams, key=lambda k: fams[k]["ms_per_step"])
+    at_max = bool(clocks and clocks.get("sm_max_mhz") and clocks["sm_mhz"] >= 0.95 * clocks["sm_max_mhz"])
+    peak = burst if at_max else sustained
+    ach = fams[dom]["achieved_tflops"]
+    return {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+            "frac": (ach / peak) if ach else None, "traffic": None,
+            "peak_source": (f"{src} bf16_tflops (burst: the timed region ran at the maximum SM clock)" if at_max else
+                            f"{src} bf16_tflops_sustained (the timed region ran below the maximum SM clock)"),
+            "families": fams}
 
 
 def config4_model_config(layers=16):
@@ -506,16 +577,24 @@ def model_flops_per_token(cfg, seq_len):
     return 6 * active + 6 * cfg.transformer_depth * cfg.n_attention_heads * hd * seq_len
 
 
+WORKLOAD4 = ("config4: full MoE LM training step (forward, cut cross entropy, backward, MuonMD + AdamW + "
+             "sparse-embedding optimizer, aux-loss-free bias update); L={L} d=1536 H=12/4 hd=128 gated sink "
+             "attention, E=64+1 shared ffn=768 top-6, V=65536, seq 4096 x micro-batch {B} per GPU, bf16")
+
+
 def run_config4(args):
-    """the full MoE LM training step (forward, CCE loss,
-    backward, MuonMD + AdamW + sparse embedding optimizer step, aux-loss-free
-    bias update), micro-batch 8 x 4096 tokens per GPU, data parallel."""
+    """BASELINE configs[3], the headline: the full MoE LM training step (forward, CCE loss,
+    backward, MuonMD + AdamW + sparse embedding optimizer step, aux-loss-free bias update),
+    micro-batch 8 x 4096 tokens per GPU, data parallel over N GPUs (weak scaling).  Every
+    step draws fresh uniform token ids.  `value` times the step with the ids already in HBM;
+    `e2e` times the same step with the ids and attention mask uploaded from pinned host
+    memory every step and the loss read back to the host every step."""
     import torch
     import torch.distributed as dist
 
     from cut_cross_entropy import linear_cross_entropy
-    from modeling.model import MoEModel
     from zs_b200 import _lib as Z
+    from zs_b200.lm import MoELM
     from zs_b200.train import (auxillary_loss_free_update, build_muonmd_optimizer, build_next_token_loss_inputs,
                                enable_fused_weight_grad)
 
@@ -526,13 +605,13 @@ def run_config4(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pg = dist.group.WORLD if world > 1 else None
     cfg = config4_model_config(args.layers)
     torch.manual_seed(1234)
-    model = MoEModel(cfg).to(dev)
+    model = MoELM(cfg).to(dev)
     enable_fused_weight_grad(model)
     # with N ranks the Newton-Schulz batches are split over the ranks (all-gathered)
-    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3,
-                                 process_group=dist.group.WORLD if world > 1 else None)
+    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3, process_group=pg)
     reducer = None
     if world > 1:
         from zs_b200.dp import GradAllReducer
@@ -541,32 +620,36 @@ def run_config4(args):
         # batch, so the average is the gradient of the global batch mean
         reducer = GradAllReducer(list(model.parameters()), bucket_mb=64.0, average=True)
     B, S = args.micro_batch, 4096
+    warmup = max(args.warmup, 5)
     g = torch.Generator(device=dev).manual_seed(77 + rank)
-    nb = max(args.warmup, 5) + args.steps
-    # a fresh batch of uniform token ids for every step (a fixed batch is
-    # memorised within a few steps by a model this size)
+    nb = 4
+    # fresh uniform token ids every step: a ring of device batches, each refilled after use
     batches = torch.randint(0, cfg.vocab_size, (nb, B, S), device=dev, generator=g)
     mask = torch.ones(B, S, dtype=torch.long, device=dev)
     it = [0]
 
-    def step():
-        ids = batches[it[0] % nb]
-        it[0] += 1
+    def train_step(ids, am):
         opt.zero_grad(set_to_none=False)
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             emb, all_topk = model.headless_forward(ids)
-            le, labels = build_next_token_loss_inputs(emb, ids, mask)
+            le, labels = build_next_token_loss_inputs(emb, ids, am)
             loss = linear_cross_entropy(le, model.get_classifier_weights(), labels, ignore_index=-100)
-        with Z.timed("backward"):
-            loss.backward()
+        loss.backward()
         if reducer is not None:
             reducer.finish()
-        with Z.timed("optimizer_step"):
-            opt.step()
-        auxillary_loss_free_update(model, all_topk, 1e-3, mask, process_group=dist.group.WORLD if world > 1 else None)
+        opt.step()
+        auxillary_loss_free_update(model, all_topk, 1e-3, am, process_group=pg)
         return loss
 
-    for _ in range(max(args.warmup, 5)):
+    def step():
+        i = it[0] % nb
+        it[0] += 1
+        loss = train_step(batches[i], mask)
+        batches[i].random_(0, cfg.vocab_size, generator=g)
+        return loss
+
+    Z.INSTR.timing = True  # the optimizer graph recorded in warm-up carries its event nodes
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -575,50 +658,126 @@ def run_config4(args):
     sampler.start()
     time.sleep(0.5)
     Z.INSTR.events = {}
-    Z.INSTR.timing = True
     l0 = Z.INSTR.launches
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     ht0 = time.time()
     t0.record()
     for _ in range(args.steps):
         loss = step()
     t1.record()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     ht1 = time.time()
     Z.INSTR.timing = False
     clocks = sampler.stop(ht0, ht1)
+    launches = Z.INSTR.launches - l0
     ms = t0.elapsed_time(t1)
     if world > 1:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
-    kern = {}
-    for name, evs in Z.INSTR.events.items():
-        durs = [a.elapsed_time(b) for a, b in evs]
-        kern[name] = {"launches_per_step": len(durs) / args.steps, "ms_per_step": sum(durs) / args.steps}
+    table = kernel_table(args.steps)
+    loss_v = float(loss.item())
+
+    # End to end through the public API with host buffers: every step uploads its ids and
+    # attention mask from pinned host memory and reads the loss back into pinned memory.
+    e_steps = 0 if args.no_e2e else max(1, min(args.steps, args.e2e_steps))
+    ids_h = torch.randint(0, cfg.vocab_size, (nb, B, S), generator=torch.Generator().manual_seed(5 + rank))
+    ids_h = ids_h.pin_memory()
+    mask_h = torch.ones(B, S, dtype=torch.long).pin_memory()
+    loss_h = torch.empty(max(e_steps, 1), dtype=torch.float32).pin_memory()
+    ids_d = torch.empty(B, S, dtype=torch.long, device=dev)
+    mask_d = torch.empty(B, S, dtype=torch.long, device=dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e_steps):
+        ids_d.copy_(ids_h[i % nb], non_blocking=True)
+        mask_d.copy_(mask_h, non_blocking=True)
+        lo = train_step(ids_d, mask_d)
+        loss_h[i:i + 1].copy_(lo.detach().reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = max(e0.elapsed_time(e1), 1e-9)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    err = Z.device_error()
     if rank == 0:
-        _, sustained, _, src = measured_peaks()
+        burst, sustained, _, src = measured_peaks()
         fpt = model_flops_per_token(cfg, S)
         value = world * B * S * args.steps / (ms * 1e-3)
-        mfu = value * fpt / (world * sustained * 1e12)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": max(args.warmup, 5), "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "warmup": warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": f"config4: MoE LM L={cfg.transformer_depth} d=1536 H=12/4 hd=128 E=64+1 "
-                                       f"ffn=768 top-6 V=65536, gated sink attention, seq 4096 x micro-batch {B}, full step incl. "
-                                       "MuonMD/AdamW/sparse-embedding optimizer",
-                           "parallelism": f"dp{world}", "model_gflop_per_token": fpt / 1e9, "mfu": mfu,
-                           "loss": float(loss.item())},
-                "roofline": {"bound": "tensor", "achieved": value * fpt / world / 1e12, "peak": sustained,
-                             "unit": "TFLOP/s", "frac": mfu, "traffic": None,
-                             "peak_source": f"{src} bf16_tflops_sustained; achieved = model FLOPs only",
-                             "kernels": kern},
-                "gpu_launches": Z.INSTR.launches - l0, "clocks": clocks, "device_error": Z.device_error()}
+                "config": {"workload": WORKLOAD4.format(L=cfg.transformer_depth, B=B),
+                           "model": "config4 MoE LM (3.98 B total / 0.60 B active matmul parameters)",
+                           "global_batch": world * B, "seq_len": S, "tokens_per_gpu_step": B * S,
+                           "parallelism": f"dp{world}", "model_gflop_per_token": fpt / 1e9,
+                           "mfu_of_sustained_peak": value * fpt / (world * sustained * 1e12),
+                           "mfu_of_burst_peak": value * fpt / (world * burst * 1e12),
+                           "l2": "working set per step tens of GB (weights alone 16 GB), far larger than the 126 MB L2",
+                           "ids": "fresh uniform token ids every step", "loss": loss_v},
+                "roofline": roofline_from_table(table, clocks),
+                "kernels": table,
+                "cpu_baseline": None,
+                "e2e": None if not e_steps else {
+                    "value": world * B * S * e_steps / (e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": ids_d.numel() * 8 + mask_d.numel() * 8, "d2h_bytes_per_step": 4,
+                    "steps": e_steps,
+                    "path": "MoELM.headless_forward + cut_cross_entropy.linear_cross_entropy + backward + "
+                            "optimizer.step + auxillary_loss_free_update; ids/mask H2D and loss D2H every step",
+                    "last_loss": float(loss_h[e_steps - 1])},
+                "gpu_launches": launches,
+                "gpu_launches_note": "libzs kernels launched by eager calls in the timed region; the kernels of "
+                                     "the replayed optimizer graphs are not counted",
+                "clocks": clocks, "device_error": err}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_config4(cfg)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def cpu_baseline_config4(cfg):
+    """The reference's step restated on the CPU (oracle/model_step.py), on the box's host cores."""
+    try:
+        from oracle.model_step import time_config4_sample
+    except ImportError as exc:
+        return {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"unavailable: {exc}"}
+    return time_config4_sample(cfg_fields(cfg), budget_s=25.0)
+
+
+def run_reference_config4(args):
+    """--impl reference for config 4: the CPU restatement of the reference's step, timed on a
+    bounded sample on the host cores (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    try:
+        from oracle.model_step import reference_arm
+    except ImportError as exc:
+        print(json.dumps({"impl": "reference", "unavailable": f"oracle/model_step.py missing: {exc}"}), flush=True)
+        return
+    line = reference_arm(cfg_fields(config4_model_config(args.layers)), args.steps, args.warmup,
+                         micro_batch=args.micro_batch)
+    line.update({"impl": "reference", "metric": METRIC, "unit": UNIT, "n_gpus": args.gpus,
+                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"})
+    print(json.dumps(line), flush=True)
+
+
+def cfg_fields(cfg):
+    keys = ("vocab_size", "hidden_size", "transformer_depth", "intermediate_size", "n_routed_experts",
+            "n_shared_experts", "n_experts_per_token", "n_attention_heads", "n_key_value_heads", "rms_norm_eps",
+            "rope_theta", "pos_rope_dims", "max_position_embeddings", "initializer_range")
+    return {k: getattr(cfg, k) for k in keys}
 
 
 def run_config5(args):
@@ -700,7 +859,7 @@ def run_config5(args):
     ms = float(tt.item())
     kern = {}
     for name, evs in Z.INSTR.events.items():
-        durs = [s.elapsed_time(e) for s, e in evs]
+        durs = [s.elapsed_time(e) for s, e, *_ in evs]
         kern[name] = {"launches": len(durs), "avg_ms": sum(durs) / len(durs), "total_ms": sum(durs)}
     gemm_ms = sum(v["total_ms"] for v in kern.values())
     err = Z.device_error()
@@ -737,21 +896,28 @@ def _free_port():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (default: 20 for config 4, 200 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="zs", choices=["zs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
-    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: config 2's 16384)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5], help="BASELINE config (default 2)")
+    ap.add_argument("--e2e-steps", type=int, default=10, help="config 4: steps of the end-to-end loop")
+    ap.add_argument("--tokens", type=int, default=0, help="config 2/3/5: tokens per GPU")
+    ap.add_argument("--config", type=int, default=4, choices=[2, 3, 4, 5],
+                    help="BASELINE config (default 4, the full training step the metric is quoted on)")
     ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
     ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
     ap.add_argument("--dp-engine", default="nccl", choices=["nccl", "ce"],
                     help="config 2 with N > 1: gradient all-reduce on the copy engines (ce) or NCCL")
     args = ap.parse_args()
+    if not args.steps:
+        args.steps = 20 if args.config == 4 else 200
     if args.impl == "reference":
-        run_reference(args)
+        if args.config == 4:
+            run_reference_config4(args)
+        else:
+            run_reference(args)
     elif args.config == 3:
         run_config3(args)
     elif args.config == 4:

@@ -491,6 +491,43 @@ int64_t zs_ce_allreduce_chunk(int64_t count, int world);
 int zs_ce_allreduce(void* data, int64_t count, int dtype, int rank, int world, void* const* recv, void* const* red,
                     int* const* flags, int step, float scale, void* stream);
 
+/*
+ * Sparse input embedding (modeling/model.py:71-86: nn.Embedding(sparse=True),
+ * bag mean in f32 for token-superposition ids, x sqrt(d) when untied):
+ *   zs_embedding_bag_forward:  out[t, :] = scale * mean_{j < bag} table[ids[t*bag + j], :]
+ *     table f32 [num_rows, d] (row stride d), ids int64 [num_bags * bag],
+ *     out f32 [num_bags, d]; bag = 1 is the plain lookup.  Out-of-range ids
+ *     contribute nothing and record ZS_DEVERR_INDEX.
+ *   zs_embedding_bag_backward: the COO values of the table gradient, one row
+ *     per lookup in lookup order: values[t*bag + j, :] = (dy[t, :] * scale) / bag
+ *     (the indices are the ids themselves).  d % 4 == 0, 16-byte aligned rows.
+ */
+int zs_embedding_bag_forward(const float* table, int64_t num_rows, int64_t d, const int64_t* ids, int64_t num_bags,
+                             int bag, float scale, float* out, void* stream);
+int zs_embedding_bag_backward(const float* dy, int64_t num_bags, int bag, int64_t d, float scale, float* values,
+                              void* stream);
+
+/*
+ * GramReaperSparse.step (engram/GramReaperSparse.py:18-66) on one table: the
+ * COO gradient (rows int64 [n], values f32 [n, d], duplicates allowed, in any
+ * order) is summed per distinct row in lookup order (coalesce), then for each
+ * touched row r:
+ *   v[r] = beta * v[r] + (1 - beta) * sum(g_r^2)
+ *   p[r] -= lr / (sqrt(v[r] / (1 - beta^t)) + eps) * g_r
+ *   p[r] /= max(||p[r]||, eps)                       (unit_norm != 0)
+ * t is the device counter *step_counter, incremented once per call with n > 0
+ * (n == 0 leaves everything untouched, as the reference skips).  lr is *lr_ptr
+ * when lr_ptr is not NULL (a device f32, read when the kernels run), else lr.
+ * No host synchronisation; deterministic (a stable radix sort by row, one CTA
+ * per distinct row).  d <= 4096, d % 4 == 0.  Rows outside [0, num_rows) are
+ * skipped and record ZS_DEVERR_INDEX.
+ */
+size_t zs_sparse_rmsprop_workspace(int64_t n, int64_t num_rows);
+int zs_sparse_rmsprop_step(float* param, int64_t num_rows, int64_t d, int64_t ld_param, float* v_state,
+                           long long* step_counter, const int64_t* rows, const float* values, int64_t ld_values,
+                           int64_t n, const float* lr_ptr, float lr, double beta, float eps, int unit_norm,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

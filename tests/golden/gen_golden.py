@@ -154,6 +154,7 @@ def main():
     all_cases.update(gen_norm_rope())
     all_cases.update(gen_muon())
     all_cases.update(gen_data())
+    all_cases.update(gen_sparse())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
@@ -343,6 +344,44 @@ def gen_data():
 
 if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "data":
     for name, arrs in gen_data().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name)
+
+
+def gen_sparse():
+    """Three GramReaperSparse steps (engram/GramReaperSparse.py:18-66) of the reference on
+    seeded COO gradients with duplicate rows, with and without the unit-norm projection;
+    the middle step's gradient touches no row."""
+    sys.path.insert(0, REF)
+    from engram.GramReaperSparse import GramReaperSparse
+
+    cases = {}
+    g = torch.Generator().manual_seed(71)
+    for name, unit in (("sparse_unit", True), ("sparse_plain", False)):
+        V, d = 50, 16
+        W0 = torch.randn(V, d, generator=g)
+        if unit:
+            W0 = W0 / W0.norm(dim=1, keepdim=True)
+        p = torch.nn.Parameter(W0.clone())
+        opt = GramReaperSparse([dict(params=[p], unit_norm=unit)], lr=3e-2, beta=0.9, unit_norm=unit)
+        out = dict(W0=_np(W0).copy())
+        for k, n in enumerate((40, 0, 25)):
+            rows = torch.randint(0, V, (n,), generator=g)
+            if n:
+                rows[: n // 4] = rows[0]                      # a row hit several times
+            vals = torch.randn(n, d, generator=g)
+            p.grad = torch.sparse_coo_tensor(rows.view(1, -1), vals, (V, d))
+            opt.step()
+            # copies: the parameter keeps changing in place
+            out[f"rows{k}"], out[f"vals{k}"], out[f"W{k + 1}"] = _np(rows), _np(vals), _np(p).copy()
+        st = opt.state[p]
+        out["v"], out["t"] = _np(st["v"]).copy(), np.asarray(st["t"])
+        cases[name] = out
+    return cases
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "sparse":
+    for name, arrs in gen_sparse().items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name)
 

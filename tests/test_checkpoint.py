@@ -19,7 +19,7 @@ CKPT_CONFIG = dict(vocab_size=128, embed_size=32, hidden_size=32, transformer_de
 
 
 def _model_opt(device="cpu"):
-    from modeling.model import MoEModel
+    from zs_b200.lm import MoELM as MoEModel
     from modeling.model_config import ModelConfig
     from zs_b200.train import build_muonmd_optimizer
 

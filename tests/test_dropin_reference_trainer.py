@@ -1,7 +1,8 @@
 """The drop-in boundary seen from the reference's own trainer: with this package's
 import root in front of a reference checkout, the reference's main.py imports
-unchanged and builds its model, optimizer and checkpoint helpers from this
-package's modules (the reference's other helpers, e.g. utils/tokenizer.py, stay
+unchanged; its own modeling/model.py builds the model from this package's
+modules (attention, MoE layer, experts, norms), and its optimizer and
+checkpoint helpers come from this package (the reference's other helpers, e.g. utils/tokenizer.py, stay
 reachable).  Runs in a subprocess; skipped where no reference checkout exists
 (the GPU box has none).  No GPU work: the model and optimizer are only built."""
 import os
@@ -39,6 +40,8 @@ where = {{
     "mcce": main.mcce_raw_token_mean_v2.__code__.co_filename,
     "zRMSNorm": main.ZeroCenteredRMSNorm.__init__.__code__.co_filename,
 }}
+# the reference's own model.py builds the model, on this package's modules
+assert where.pop("MoEModel").startswith({ref!r}), type(model)
 bad = {{k: v for k, v in where.items() if not v.startswith(pkg)}}
 assert not bad, bad
 import utils.tokenizer  # the reference's own helper, still importable
@@ -62,7 +65,7 @@ def test_reference_trainer_imports_and_builds_on_this_package(tmp_path):
     stub.mkdir()
     (stub / "aim.py").write_text("Distribution = Run = None\n")
     env["PYTHONPATH"] = os.pathsep.join([env["PYTHONPATH"], str(stub)])
-    r = subprocess.run([sys.executable, "-c", SCRIPT.format(pkg=str(PKG))], cwd=tmp_path, env=env,
+    r = subprocess.run([sys.executable, "-c", SCRIPT.format(pkg=str(PKG), ref=str(REF))], cwd=tmp_path, env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert r.stdout.strip().startswith("ok")

@@ -141,7 +141,7 @@ def _shard_worker(rank, world, port, q):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world,
                                 timeout=__import__("datetime").timedelta(seconds=60))
-        from modeling.model import MoEModel
+        from zs_b200.lm import MoELM as MoEModel
         from modeling.model_config import ModelConfig
         from scattermoe.expert_parallel import ExpertParallelGLUMLP, shard_experts
 

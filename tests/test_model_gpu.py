@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 def _tiny(layers=2, window=None):
     from modeling.model_config import ModelConfig
-    from modeling.model import MoEModel
+    from zs_b200.lm import MoELM as MoEModel
 
     cfg = ModelConfig(vocab_size=8192, embed_size=256, hidden_size=256, transformer_depth=layers,
                       intermediate_size=512, n_experts=9, n_shared_experts=1, n_experts_per_token=2,
