@@ -15,6 +15,7 @@ from __future__ import annotations
 import os
 import sys
 import types
+import zlib
 from pathlib import Path
 
 os.environ.setdefault("TRITON_INTERPRET", "1")
@@ -155,6 +156,7 @@ def main():
     all_cases.update(gen_muon())
     all_cases.update(gen_data())
     all_cases.update(gen_sparse())
+    all_cases.update(gen_step())
     for name, arrs in all_cases.items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name, sorted(arrs.keys()))
@@ -384,6 +386,129 @@ if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "sparse":
     for name, arrs in gen_sparse().items():
         np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
         print("wrote", name)
+
+
+def _sdpa_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, dropout_p=0.0, causal=True,
+                 window_size=(-1, -1), **_):
+    """CPU stand-in for flash_attn_varlen_func (CUDA only): exact causal GQA softmax
+    attention per packed sequence (q head h reads kv head h // (H / Hkv))."""
+    assert causal and tuple(window_size) == (-1, -1)
+    out = torch.empty_like(q)
+    rep = q.size(1) // k.size(1)
+    cu = cu_seqlens_q.tolist()
+    for a, b in zip(cu[:-1], cu[1:]):
+        qq = q[a:b].transpose(0, 1)
+        kk = k[a:b].repeat_interleave(rep, dim=1).transpose(0, 1)
+        vv = v[a:b].repeat_interleave(rep, dim=1).transpose(0, 1)
+        out[a:b] = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True).transpose(0, 1)
+    return out
+
+
+STEP_SAMPLES = 4096
+
+
+def _sample_idx(name, numel, rows=None, width=None):
+    """Seeded flat indices (sorted) of up to STEP_SAMPLES elements of a parameter; for the
+    embedding only inside the touched rows."""
+    g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+    if rows is not None:
+        r = rows[torch.randint(0, rows.numel(), (STEP_SAMPLES,), generator=g)]
+        c = torch.randint(0, width, (STEP_SAMPLES,), generator=g)
+        return torch.unique(r * width + c)
+    if numel <= STEP_SAMPLES:
+        return torch.arange(numel)
+    return torch.unique(torch.randint(0, numel, (STEP_SAMPLES,), generator=g))
+
+
+def gen_step():
+    """One full training step of the reference at BASELINE config 1's shapes on the CPU
+    (main.py:723-815 with s == 1): its own MoEModel, build_muonmd_optimizer and
+    auxillary_loss_free_update, on weights from oracle.model_step.canonical_params (N(0, 0.02),
+    unit-norm embedding rows, zero norm gains and biases) and seeded ids [4, 256].  The
+    reference's scattermoe and Liger RoPE Triton kernels run under Triton's interpreter,
+    flash_attn_varlen_func is replaced by exact SDPA (_sdpa_varlen), linear_cross_entropy by
+    F.cross_entropy over h @ W^T.  Stored: the loss, every layer's routing and gate
+    probabilities, layer outputs, and for every parameter the gradient and the weights after
+    the optimizer step at up to 4096 seeded positions plus their full norms and sums."""
+    ref = _import_reference_main()
+    sys.path.insert(0, str(OUT.parents[1]))
+    from oracle.model_step import canonical_ids, canonical_params, config1
+    import modeling.attention as ref_attn
+    from modeling.model import MoEModel
+    from modeling.model_config import ModelConfig
+
+    ref_attn.flash_attn_varlen_func = _sdpa_varlen
+    c1 = config1()
+    cfg = ModelConfig(vocab_size=c1["vocab_size"], embed_size=c1["hidden_size"], hidden_size=c1["hidden_size"],
+                      transformer_depth=c1["transformer_depth"], intermediate_size=c1["intermediate_size"],
+                      n_experts=c1["n_routed_experts"] + 1, n_shared_experts=1,
+                      n_experts_per_token=c1["n_experts_per_token"], n_attention_heads=c1["n_attention_heads"],
+                      n_key_value_heads=c1["n_key_value_heads"], attention_window_pattern=(None, None),
+                      max_position_embeddings=c1["max_position_embeddings"], sequence_length=256,
+                      pos_rope_dims=c1["pos_rope_dims"])
+    torch.manual_seed(0)
+    model = MoEModel(cfg)
+    P = canonical_params(c1, 0)
+    sd = model.state_dict()
+    missing = set(P) ^ {k for k in sd if not k.endswith("expert_biases")}
+    assert not missing, missing
+    with torch.no_grad():
+        for k, v in P.items():
+            sd[k].copy_(v)
+    ids = canonical_ids(c1, 4, 256, 1)
+    mask = torch.ones_like(ids)
+    opt = ref.build_muonmd_optimizer(model, torch.device("cpu"))
+    keep = {}
+    hooks = []
+    for i, layer in enumerate(model.layers):
+        hooks.append(layer.self_attn.register_forward_hook(
+            lambda m, a, o, i=i: keep.__setitem__(f"attn{i}", o.detach().clone())))
+        hooks.append(layer.mlp.register_forward_hook(
+            lambda m, a, o, i=i: keep.update({f"moe{i}": o[0].detach().clone(),
+                                              f"probs{i}": torch.sigmoid(a[0].reshape(-1, a[0].size(-1))
+                                                                         @ m.gate.weight.T).detach().clone()})))
+        hooks.append(layer.register_forward_hook(lambda m, a, o, i=i: keep.__setitem__(f"out{i}", o[0].detach().clone())))
+    opt.zero_grad(set_to_none=False)
+    emb, topk = model.headless_forward(ids)
+    le, labels = ref.build_next_token_loss_inputs(emb, ids, mask)
+    loss = torch.nn.functional.cross_entropy(le.reshape(-1, le.size(-1)) @ model.get_classifier_weights().T,
+                                             labels.reshape(-1), ignore_index=-100)
+    loss.backward()
+    for h in hooks:
+        h.remove()
+    grads = {n: (p.grad.to_dense() if p.grad.is_sparse else p.grad).detach().clone()
+             for n, p in model.named_parameters()}
+    before = {n: p.detach().clone() for n, p in model.named_parameters()}
+    opt.step()
+    ref.auxillary_loss_free_update(model, topk, 1e-3, mask)
+    out = dict(loss=_np(loss), ids=_np(ids))
+    touched = torch.unique(ids)
+    for n, p in model.named_parameters():
+        rows = touched if n == "embedding.weight" else None
+        idx = _sample_idx(n, p.numel(), rows, p.size(-1))
+        out[f"idx:{n}"] = idx.numpy().astype(np.int64)
+        out[f"grad:{n}"] = _np(grads[n].reshape(-1)[idx]).copy()
+        out[f"after:{n}"] = _np(p.detach().reshape(-1)[idx]).copy()
+        out[f"delta:{n}"] = _np((p.detach() - before[n]).reshape(-1)[idx]).copy()
+        out[f"gnorm:{n}"] = np.asarray(float(grads[n].norm()))
+        out[f"dnorm:{n}"] = np.asarray(float((p.detach() - before[n]).norm()))
+    for i, layer in enumerate(model.layers):
+        out[f"topk{i}"] = _np(topk[i]).copy()
+        out[f"probs{i}"] = _np(keep[f"probs{i}"]).copy()
+        out[f"bias_after{i}"] = _np(layer.mlp.gate.expert_biases).copy()
+        for key in ("attn", "moe", "out"):
+            t = keep[f"{key}{i}"].reshape(-1)
+            sel = _sample_idx(f"{key}{i}", t.numel())
+            out[f"{key}{i}"] = _np(t[sel]).copy()
+            out[f"{key}{i}_idx"] = sel.numpy().astype(np.int64)
+            out[f"{key}{i}_norm"] = np.asarray(float(t.norm()))
+    return {"step_cfg1": out}
+
+
+if __name__ == "__main__" and os.environ.get("ZS_GOLDEN_ONLY") == "step":
+    for name, arrs in gen_step().items():
+        np.savez_compressed(OUT / f"{name}.npz", **{kk: np.asarray(v) for kk, v in arrs.items()})
+        print("wrote", name, len(arrs))
 
 
 CKPT_CONFIG = dict(vocab_size=128, embed_size=32, hidden_size=32, transformer_depth=2, intermediate_size=16,
