@@ -82,6 +82,7 @@ class GradAllReducer:
         self.average = average
         self.engine = engine
         self._ce = {}             # (bucket, dtype) -> CopyEngineAllReduce
+        self._ce_used = False     # a copy-engine all-reduce ran since the last finish()
         self.params = [p for p in params if p.requires_grad]
         self.bucket_bytes = int(bucket_mb * (1 << 20))
         self._hooks = []
@@ -130,10 +131,33 @@ class GradAllReducer:
         self._pending = []        # (work, flat, params) of dense buckets
         self._sparse = []         # (param, reduced grad)
 
+    def _close_ce(self):
+        for ce in self._ce.values():
+            ce.close()
+        self._ce = {}
+
+    def _check_peers(self):
+        """A copy-engine all-reduce whose wait for a peer expired reduced stale or partial
+        chunks: raise instead of handing those gradients to the optimizer, and drop the
+        copy-engine state (its step flags no longer agree with the peers')."""
+        from . import _lib as Z
+
+        self._ce_used = False
+        if torch.cuda.is_available():
+            torch.cuda.current_stream().synchronize()
+        err = Z.device_error()
+        if err & 0x20:  # ZS_DEVERR_TIMEOUT_PEER
+            Z.clear_device_error()
+            self._close_ce()
+            self._reset()
+            raise RuntimeError("copy-engine gradient all-reduce: a peer rank did not signal in time "
+                               "(ZS_DEVERR_TIMEOUT_PEER); the reduced gradients are invalid")
+
     def remove(self):
         for h in self._hooks:
             h.remove()
         self._hooks = []
+        self._close_ce()
         for p in self.params:
             if _READY.get(id(p)) == self._on_grad:
                 del _READY[id(p)]
@@ -181,8 +205,15 @@ class GradAllReducer:
 
                     key = (b, dt)
                     ce = self._ce.get(key)
-                    if ce is None or ce.count != flat.numel():
+                    if ce is not None and ce.count != flat.numel():
+                        # the bucket changed size: release the old buffers and peer mappings once
+                        # the copies that use them have finished
+                        (self._stream or torch.cuda.current_stream()).synchronize()
+                        ce.close()
+                        ce = None
+                    if ce is None:
                         ce = self._ce[key] = CopyEngineAllReduce(flat.numel(), dt, self.group, flat.device)
+                    self._ce_used = True
                     ce(flat, scale=(1.0 / self.world) if self.average else 1.0,
                        stream=self._stream or torch.cuda.current_stream())
                     self._pending.append((None, flat, group, in_place))
@@ -210,6 +241,8 @@ class GradAllReducer:
                 n = p.numel()
                 p.grad.copy_(flat[off:off + n].view_as(p.grad))
                 off += n
+        if self._ce_used:
+            self._check_peers()
         for p, g in self._sparse:
             p.grad = g / self.world if self.average else g
         self._reset()

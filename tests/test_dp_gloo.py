@@ -167,3 +167,30 @@ def test_routing_counts_all_reduce_two_ranks():
     out = _run(_counts_worker)
     assert all(ok_counts and ok_bias for _, ok_counts, ok_bias, _ in out)
     assert out[0][3] == out[1][3]   # identical bias on both ranks
+
+
+def test_copy_engine_peer_timeout_raises_and_drops_state(monkeypatch):
+    """finish() after a copy-engine all-reduce reads the device error word: an expired
+    peer wait (ZS_DEVERR_TIMEOUT_PEER) raises, and the copy-engine instances (whose step
+    flags no longer agree with the peers') are closed and dropped (fake error word)."""
+    from zs_b200 import _lib, dp
+
+    r = dp.GradAllReducer.__new__(dp.GradAllReducer)
+    closed = []
+
+    class FakeCE:
+        def close(self):
+            closed.append(True)
+
+    r._ce = {(0, torch.float32): FakeCE(), (1, torch.float32): FakeCE()}
+    r._ce_used = True
+    r.buckets = [[], []]
+    monkeypatch.setattr(_lib, "device_error", lambda device=None: 0x20)
+    monkeypatch.setattr(_lib, "clear_device_error", lambda device=None: None)
+    with pytest.raises(RuntimeError, match="TIMEOUT_PEER"):
+        r._check_peers()
+    assert len(closed) == 2 and r._ce == {} and not r._ce_used
+    # a clean error word passes
+    r._ce_used = True
+    monkeypatch.setattr(_lib, "device_error", lambda device=None: 0)
+    r._check_peers()

@@ -65,3 +65,23 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
                                                dummy.data_ptr(), Z.stream_of(dummy))
     assert rc == 8  # ZS_ERR_SCRATCH_LIMIT
     assert b"scratch" in Z.lib().zs_error_string(rc)
+
+
+def test_noalloc_at_its_limit_matches_workspace_entry_point():
+    """The largest problem the fixed scratch accepts (256 chunks x 1024 buckets = all of
+    it): the histogram scan no longer fits shared memory and runs in place in the fixed
+    array; two calls in a row, each equal to the workspace entry point."""
+    from zs_b200 import _lib as Z
+
+    E, n = 1023, 256 * 4096
+    assert Z.lib().zs_flatten_sort_count_workspace(n, E) // 4 == Z.lib().zs_flatten_sort_count_noalloc_max_scratch_ints()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    for _ in range(2):
+        w = torch.softmax(torch.randn(E, device="cuda", generator=g) * 3, 0)
+        ids = torch.multinomial(w, n, replacement=True, generator=g)
+        ref = _workspace_entry_point(Z, ids, E)
+        got = _noalloc_entry_point(Z, ids, E)
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+    assert Z.device_error() == 0
