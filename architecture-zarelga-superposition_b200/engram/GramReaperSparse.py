@@ -113,6 +113,13 @@ class GramReaperSparse(Optimizer):
                     continue
                 yield group, p, rows, vals
 
+    def state_dict(self):
+        """The reference's layout: "t" as a Python int (read from the device counter)."""
+        sd = super().state_dict()
+        sd["state"] = {k: ({**v, "t": int(v["t"])} if torch.is_tensor(v.get("t")) else v)
+                       for k, v in sd["state"].items()}
+        return sd
+
     # ------------------------------------------------------------------ eager
     @torch.no_grad()
     def step(self, closure=None):

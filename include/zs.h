@@ -15,6 +15,12 @@
  * that ran out, an index out of range) never trap: they set bits in a
  * device-global error word read with zs_device_error_get().
  *
+ * Current device: an entry point makes the device that owns its data current
+ * on the calling thread (cudaSetDevice) before it launches, and leaves it
+ * current when it returns.  A multi-GPU caller in one process that relies on
+ * the current device afterwards (allocations without an explicit device) sets
+ * it again itself.
+ *
  * Each declaration names the reference function it replaces
  * (CoffeeVampir3/Architecture-Zarelga-Superposition, path:line).
  */

@@ -176,9 +176,10 @@ def moe(P, p, cfg, x, bias, routing=None, keep=None):
     g = xt @ P[p + "shared_experts.gate_proj.weight"].T
     u = xt @ P[p + "shared_experts.up_proj.weight"].T
     shared = (F.silu(g) * u) @ P[p + "shared_experts.down_proj.weight"].T
-    W1 = P[p + "routed_experts.experts.weight"]
-    W2 = P[p + "routed_experts.output_experts.weight"]
-    f = W2.shape[-1]
+    # one view per expert (unbind: the backward stacks the experts' gradients once)
+    W1 = P[p + "routed_experts.experts.weight"].unbind(0)
+    W2 = P[p + "routed_experts.output_experts.weight"].unbind(0)
+    f = W2[0].shape[-1]
     routed = torch.zeros_like(xt)
     flat = idx.reshape(-1)
     for e in range(E):
@@ -384,7 +385,7 @@ def _sample_cfg(cfg):
     return c
 
 
-def config4_sample_step(cfg, tokens, ns_rows=1):
+def config4_sample_step(cfg, tokens, ns_rows=1, t_opt=None):
     """Seconds of the config-4 step extrapolated from a bounded sample on the CPU:
       * one transformer layer forward + backward on `tokens` tokens (one sequence), times
         L layers and 32768 / tokens (the per-GPU micro-batch);
@@ -411,6 +412,10 @@ def config4_sample_step(cfg, tokens, ns_rows=1):
     t_layer = max(t_fb - t_head, 0.0)
     L = cfg["transformer_depth"]
     scale = 32768 / tokens
+    total = t_layer * L * scale + t_head * scale
+    if t_opt is not None:  # the optimizer's cost measured by an earlier sample
+        return total + t_opt, {"layer_fwd_bwd_s": t_layer, "head_fwd_bwd_s": t_head,
+                               "optimizer_s_extrapolated": t_opt}
     # optimizer sample
     t_opt = 0.0
     shapes = {}
@@ -437,12 +442,12 @@ def time_config4_sample(cfg, budget_s=25.0):
     """cpu_baseline for bench.py: the config-4 step's tokens/s on the host cores, from one
     bounded sample (config4_sample_step), sized to stay near budget_s."""
     cores = _threads()
-    tokens = 4096
+    tokens = 512
     t0 = time.perf_counter()
-    est, parts = config4_sample_step(cfg, 512)           # calibration on a small sample
-    if time.perf_counter() - t0 > budget_s / 8:
-        tokens = 1024
-    est, parts = config4_sample_step(cfg, tokens)
+    est, parts = config4_sample_step(cfg, 512)
+    if time.perf_counter() - t0 < budget_s / 6:        # a fast host: a longer sequence
+        tokens = 2048
+        est, parts = config4_sample_step(cfg, tokens)
     return {"value": 32768 / est, "unit": "tokens/s", "cores": cores, "kind": "port",
             "ms_per_step_extrapolated": est * 1e3, "parts": parts,
             "sample": f"config 4 widths, one layer + head forward/backward on {tokens} tokens and MuonMD on one "
@@ -456,15 +461,15 @@ def reference_arm(cfg, steps, warmup, micro_batch=8):
     """--impl reference: per step one bounded config-4 sample on the host cores; value =
     config-4 tokens/s from the mean extrapolated step time."""
     cores = _threads()
-    t0 = time.perf_counter()
-    config4_sample_step(cfg, 512)
-    tokens = 4096 if time.perf_counter() - t0 < 3.0 else 1024
+    tokens = 256
+    _, parts = config4_sample_step(cfg, tokens)          # also measures the optimizer, once
+    t_opt = parts["optimizer_s_extrapolated"]
     for _ in range(max(0, warmup)):
-        config4_sample_step(cfg, tokens)
+        config4_sample_step(cfg, tokens, t_opt=t_opt)
     ests = []
     wall = time.perf_counter()
     for _ in range(max(1, steps)):
-        ests.append(config4_sample_step(cfg, tokens)[0])
+        ests.append(config4_sample_step(cfg, tokens, t_opt=t_opt)[0])
     wall = time.perf_counter() - wall
     est = sum(ests) / len(ests)
     value = micro_batch * 4096 / est
@@ -472,6 +477,7 @@ def reference_arm(cfg, steps, warmup, micro_batch=8):
             "config": {"workload": "config4 full training step (CPU restatement, extrapolated from samples)",
                        "sample_tokens_per_step": tokens, "sample_wall_s": wall},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"each step: one config-4 layer + head fwd/bwd on {tokens} tokens and "
-                                       "MuonMD on one matrix per weight shape, extrapolated to the full step"},
+                             "sample": f"each step: one config-4 layer + head fwd/bwd on {tokens} tokens, "
+                                       "extrapolated to 16 layers x 8 x 4096 tokens, plus the optimizer's time "
+                                       "extrapolated once from MuonMD on one matrix per weight shape"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
