@@ -6,8 +6,9 @@ window, and a per-head sigmoid output gate.  An optional learned sink logit
 per head (the key-sink of modeling/hca.py:138-144, value 0) is off by default
 so the state dict matches the reference's.
 
-QK-norm, RoPE and the attention core (tcgen05 flash attention, forward and
-backward) run in libzs.so; the projections are cuBLAS linears.
+Everything runs in libzs.so: the q/k/v/head-gate projections as one grouped-GEMM
+product over the concatenated weights, QK-norm, RoPE, the attention core
+(tcgen05 flash attention, forward and backward) and the output projection.
 """
 from __future__ import annotations
 
@@ -18,6 +19,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from zs_b200.attn import attention as attention_core
+from zs_b200.dense import dense_linear
 
 from .liger_rope import LigerRopeFunction, PartialRopeFunction  # noqa: F401
 from .zRMSNorm import ZeroCenteredRMSNorm
@@ -109,11 +111,8 @@ class GatedAttention(nn.Module):
         n_out = qd + 2 * kd + self.num_heads
         pad = -n_out % 16
         ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.head_gate_proj.weight]
-        if pad:
-            ws.append(self.q_proj.weight.new_zeros(pad, self.hidden_size))
-        w_cat = torch.cat(ws, 0)
-        q, k, v, gate_logits = torch.split(F.linear(hidden_states, w_cat), [qd, kd, kd, self.num_heads + pad],
-                                           dim=-1)
+        qkvg = dense_linear(hidden_states, ws, tag="proj_qkvg", pad=pad)
+        q, k, v, gate_logits = torch.split(qkvg, [qd, kd, kd, self.num_heads + pad], dim=-1)
         gate_logits = gate_logits[..., : self.num_heads]
         q = q.reshape(bsz, seq_len, self.num_heads, self.head_dim)
         k = k.reshape(bsz, seq_len, self.num_key_value_heads, self.head_dim)
@@ -133,4 +132,5 @@ class GatedAttention(nn.Module):
         attn = attention_core(q, k, v, window=self.window_size, seq_ids=seq_ids, k_sink=self.k_sink)
         gate = torch.sigmoid(gate_logits)
         attn = attn * gate.unsqueeze(-1)
-        return self.o_proj(attn.reshape(bsz, seq_len, self.num_heads * self.head_dim))
+        return dense_linear(attn.reshape(bsz, seq_len, self.num_heads * self.head_dim), [self.o_proj.weight],
+                            tag="proj_o")

@@ -1,8 +1,14 @@
 """ExpertMLP (the shared expert): down(silu(gate(x)) * up(x)) with bias-free
-linears named gate_proj / up_proj / down_proj (modeling/expert_layer.py:6-24)."""
+linears named gate_proj / up_proj / down_proj (modeling/expert_layer.py:6-24).
+The forward runs on the grouped tcgen05 GEMM as a one-group expert: the up and
+gate products in one launch with the SwiGLU in its epilogue, the down product in
+a second; the backward fuses the SwiGLU derivative into the down product's
+input-gradient epilogue (zs_b200.dense.dense_swiglu)."""
 from __future__ import annotations
 
 import torch.nn as nn
+
+from zs_b200.dense import dense_swiglu
 
 
 class ExpertMLP(nn.Module):
@@ -23,4 +29,5 @@ class ExpertMLP(nn.Module):
             nn.init.normal_(lin.weight, mean=0.0, std=self.initializer_range)
 
     def forward(self, x):
-        return self.down_proj(self.act_fn(self.gate_proj(x)) * self.up_proj(x))
+        # one-group grouped GEMMs with the SwiGLU fused into their epilogues (zs_b200.dense)
+        return dense_swiglu(x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight)

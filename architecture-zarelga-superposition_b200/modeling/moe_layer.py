@@ -1,11 +1,9 @@
 """MoELayer: router + shared expert + routed GLU experts (modeling/moe_layer.py:11-58).
 Parameter names match the reference (gate, shared_experts, routed_experts).
 
-The router and the shared expert's gate/up projections read the same input, so
-they run as one GEMM over their concatenated weights; the input is cast to the
-autocast dtype once and shared with the routed experts.  Same products as the
-reference's separate autocast linears (the input gradient is accumulated in f32
-inside one GEMM instead of summing bf16 gradients)."""
+The input is cast to the autocast dtype once and shared by the router (a
+T x E cuBLAS product, 2*T*d*E flops), the shared expert (one-group grouped
+GEMMs with the SwiGLU fused, modeling/expert_layer.py) and the routed experts."""
 from __future__ import annotations
 
 import torch
@@ -45,15 +43,13 @@ class MoELayer(nn.Module):
             x = hidden_states
         k = self.n_experts_per_token
         se = self.shared_experts
-        E, f = self.gate.weight.size(0), se.gate_proj.weight.size(0)
         in_dtype = x.dtype if out_dtype is None else out_dtype
         if torch.is_autocast_enabled() and x.dtype == torch.float32:
             x = x.to(torch.get_autocast_dtype("cuda"))
         d = x.size(-1)
-        w_cat = torch.cat([self.gate.weight, se.gate_proj.weight, se.up_proj.weight], 0)
-        logits, g, u = torch.split(F.linear(x.reshape(-1, d), w_cat), [E, f, f], dim=-1)
+        logits = F.linear(x.reshape(-1, d), self.gate.weight)   # the router: T x E, tiny
         topk_idx, topk_weight = self.gate.route(logits)
-        shared = se.down_proj(se.act_fn(g) * u).view(x.shape)
+        shared = se(x)
         routed = self.routed_experts(x, topk_weight, topk_idx)
         # the reference adds a bf16 shared output to f32 routed rows: the sum in f32
         out = shared.to(in_dtype) + routed

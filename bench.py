@@ -487,7 +487,7 @@ def run_config3(args):
 KERNEL_FAMILIES = {
     # grouped_gemm_kernel (csrc/zs_gemm.cu): every tcgen05 GEMM launch of the step
     "grouped_gemm_kernel": ("newton_schulz5", "up_swiglu", "down_dx", "down_fwd", "down_dw", "up_dw", "up_dx",
-                            "xent_fwd", "xent_bwd", "scatter2scatter", "groupXtY"),
+                            "xent_fwd", "xent_bwd", "scatter2scatter", "groupXtY", "proj_", "shared_expert"),
     # attn_fwd_kernel / attn_bwd_* (csrc/zs_attn.cu)
     "attention": ("attention_fwd", "attention_bwd"),
 }
