@@ -664,11 +664,15 @@ def run_config4(args):
     if world > 1:
         dist.barrier()
     ht0 = time.time()
+    if args.profile_timed:
+        torch.cuda.profiler.start()   # a profiler started with --profile-from-start off records from here
     t0.record()
     for _ in range(args.steps):
         loss = step()
     t1.record()
     torch.cuda.synchronize()
+    if args.profile_timed:
+        torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     ht1 = time.time()
@@ -902,6 +906,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) loop")
     ap.add_argument("--e2e-steps", type=int, default=10, help="config 4: steps of the end-to-end loop")
+    ap.add_argument("--profile-timed", action="store_true",
+                    help="config 4: bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--tokens", type=int, default=0, help="config 2/3/5: tokens per GPU")
     ap.add_argument("--config", type=int, default=4, choices=[2, 3, 4, 5],
                     help="BASELINE config (default 4, the full training step the metric is quoted on)")
