@@ -80,6 +80,7 @@ struct GemmArgs {
   const float* grad_loss;              // EPI_XENT_GRAD: device scalar dL/dloss
   const float* denom;                  // EPI_XENT_GRAD: device scalar N (total active labels)
   int accumulate;                      // EPI_F32: out += acc instead of out = acc
+  const float* f32_scale;              // EPI_F32 (nullable): device scalar multiplying the accumulator
   int64_t group_rows;                  // > 0: uniform groups (batched GEMM), group e = rows [e*g, (e+1)*g)
   float alpha, beta;                   // EPI_AXPBY: out = alpha * acc + beta * aux
   int sym_upper;                       // uniform square groups (pair tiles): the product is symmetric,
@@ -855,8 +856,11 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           float run_m = -INFINITY, run_s = 0.f, tgt = 0.f;
           float alpha = 0.f, scale = 0.f, lrow = 0.f;
           if (EPI == EPI_XENT_GRAD) {
-            scale = __ldg(args.grad_loss) / __ldg(args.denom);
-            alpha = scale * (float)si;
+            // G = s * softmax - counts, unscaled: grad_loss / N is applied in f32 by the dH and
+            // dW products (a bf16 G of (softmax - 1) / N would round every row's target entry
+            // the same way and scale the whole gradient by up to 2^-8)
+            scale = 1.0f;
+            alpha = (float)si;
             lrow = valid ? __ldg(args.lse + row) : 0.f;
           }
 #pragma unroll 1
@@ -970,6 +974,11 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             const int col0 = ti.nt * BN + lc;
             const int ncols = min(32, args.N_out - col0);
             if (ncols <= 0 || !valid) continue;
+            if (args.f32_scale != nullptr) {
+              const float sc = __ldg(args.f32_scale);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * sc);
+            }
             float* o = reinterpret_cast<float*>(args.out) + out_row * args.ldo_m + col0;
             store_f32_chunk(o, r, ncols, args.accumulate != 0, vec);
           }
@@ -1021,6 +1030,11 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
           if (ncols <= 0) continue;
           if (EPI == EPI_F32) {
             if (mvalid) {
+              if (args.f32_scale != nullptr) {
+                const float sc = __ldg(args.f32_scale);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * sc);
+              }
               float* o = reinterpret_cast<float*>(args.out) + ti.e * args.out_se + (int64_t)m * args.ldo_m + col0;
               store_f32_chunk(o, r, ncols, args.accumulate != 0, vec);
             }
@@ -1626,8 +1640,16 @@ extern "C" int zs_xent_forward(const void* hidden, int64_t T, int64_t D, int64_t
 
 extern "C" size_t zs_xent_backward_workspace(int64_t T, int64_t v_chunk, int dtype) {
   const int64_t pitch = ((v_chunk * elem_size(dtype) + 15) / 16) * 16;
-  return (size_t)(T * pitch + 256);
+  return (size_t)(T * pitch + 512);
 }
+
+namespace zs {
+__global__ void xent_grad_scale_kernel(const float* __restrict__ grad_loss, const float* __restrict__ denom,
+                                       float* __restrict__ out) {
+  const float n = __ldg(denom);
+  out[0] = n > 0.f ? __ldg(grad_loss) / n : 0.f;
+}
+}  // namespace zs
 
 extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_t h_sm, const void* classifier,
                                 int64_t V, int64_t c_sm, const int64_t* labels, int s_max, const int* s_count,
@@ -1648,6 +1670,9 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
   constexpr int BN = 256;
   const int64_t pitch = ((v_chunk * es + 15) / 16) * 16 / es;
   char* G = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  float* gscale = reinterpret_cast<float*>(G + ((T * pitch * es + 255) / 256) * 256);   // grad_loss / N
+  xent_grad_scale_kernel<<<1, 1, 0, stream>>>(grad_loss, denom, gscale);
+  ZS_CUDA_TRY(cudaGetLastError());
   CUtensorMap tmH_k, tmC_k, tmC_mn, tmH_mn;
   int rc = make_tmap(&tmH_k, hidden, dtype, (uint64_t)D, (uint64_t)T, (uint64_t)h_sm * es, 64, 128);
   if (rc != ZS_OK) return rc;
@@ -1706,6 +1731,7 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
       h.vec_ok = (reinterpret_cast<uintptr_t>(d_hidden) % 16) == 0;
       h.b_row_offset = v0;
       h.accumulate = v0 > 0;
+      h.f32_scale = gscale;
       rc = launch_gemm<BN, 4, false, true, EPI_F32>(tmG_k, tmC_mn, h, ((T + BM - 1) / BM) * h.n_tiles, stream);
       if (rc != ZS_OK) return rc;
     }
@@ -1726,6 +1752,7 @@ extern "C" int zs_xent_backward(const void* hidden, int64_t T, int64_t D, int64_
       w.out_se = 0;
       w.vec_ok = (reinterpret_cast<uintptr_t>(d_classifier) % 16) == 0;
       w.accumulate = 0;
+      w.f32_scale = gscale;
       rc = launch_gemm<BN, 4, true, true, EPI_F32>(tmG_mn, tmH_mn, w, (int64_t)w.m_tiles_xty * w.n_tiles, stream);
       if (rc != ZS_OK) return rc;
     }

@@ -889,6 +889,166 @@ def run_config5(args):
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------ kernel workloads
+# Fixed single-kernel workloads at the configs' shapes, for timing with CUDA events and for
+# capturing one kernel under a profiler (one process, one GPU):  bench.py --kernel NAME
+# [--batch B].  Each runs `--warmup` passes, then `--steps` timed passes, and prints one JSON
+# line of mean milliseconds per pass (forward and backward separately where both exist).
+
+def _kernel_attention(args, g):
+    """config 4 attention: B x 4096, H=12, Hkv=4, hd=128, causal, sink key; forward and backward."""
+    import torch
+
+    from zs_b200.attn import attention, attention_flops
+
+    B, S, H, Hkv, hd = args.batch or 8, 4096, 12, 4, 128
+    q = torch.randn(B, S, H, hd, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    k = torch.randn(B, S, Hkv, hd, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    v = torch.randn(B, S, Hkv, hd, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    ks = (torch.randn(H, hd, device="cuda", generator=g) * 0.5).requires_grad_(True)
+    do = torch.randn(B, S, H, hd, device="cuda", generator=g).bfloat16()
+    holder = {}
+
+    def fwd():
+        holder["o"] = attention(q, k, v, k_sink=ks)
+
+    def bwd():
+        torch.autograd.grad(holder["o"], (q, k, v, ks), do, retain_graph=True)
+
+    fl = attention_flops(B, S, H, hd)
+    return {"shape": [B, S, H, Hkv, hd]}, [("fwd", fwd, fl), ("bwd", bwd, 2.5 * fl)]
+
+
+def _kernel_newton_schulz(args, g):
+    """zeropower_via_newtonschulz5 on config 4's expert stacks [64, 1536, 1536] and [64, 1536, 768]."""
+    import torch
+
+    from optimizer.muon import newton_schulz_flops, zeropower_via_newtonschulz5
+
+    a = torch.randn(64, 1536, 1536, device="cuda", generator=g).bfloat16()
+    b = torch.randn(64, 1536, 768, device="cuda", generator=g).bfloat16()
+    return {"shapes": [[64, 1536, 1536], [64, 1536, 768]]}, [
+        ("w1_stack", lambda: zeropower_via_newtonschulz5(a, 5), newton_schulz_flops(64, 1536, 1536, 5)),
+        ("w2_stack", lambda: zeropower_via_newtonschulz5(b, 5), newton_schulz_flops(64, 768, 1536, 5))]
+
+
+def _kernel_xent(args, g):
+    """config 3 cut cross entropy: hidden [16384, 2048], classifier [131072, 2048], 5 % ignored."""
+    import torch
+
+    from cut_cross_entropy import linear_cross_entropy
+
+    T, D, V = args.tokens or 16384, 2048, 131072
+    h = torch.randn(T, D, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    c = (torch.randn(V, D, device="cuda", generator=g) * 0.02).bfloat16().requires_grad_(True)
+    t = torch.randint(0, V, (T,), device="cuda", generator=g)
+    t[torch.rand(T, device="cuda", generator=g) < 0.05] = -100
+    holder = {}
+
+    def fwd():
+        holder["l"] = linear_cross_entropy(h, c, t, ignore_index=-100)
+
+    def bwd():
+        torch.autograd.grad(holder["l"], (h, c), retain_graph=True)
+
+    return {"shape": [T, D, V]}, [("fwd", fwd, 2.0 * T * V * D), ("bwd", bwd, 6.0 * T * V * D)]
+
+
+def _kernel_muonmd(args, g):
+    """One md_decoupled_step on config 4's W1 expert stack [64, 1536, 1536] f32 (gains "both")."""
+    import torch
+
+    from optimizer.muon import md_decoupled_step
+
+    p = torch.randn(64, 1536, 1536, device="cuda", generator=g) * 0.02
+    grad = torch.randn(64, 1536, 1536, device="cuda", generator=g) * 1e-3
+    state = {}
+    lr = torch.tensor(0.02, device="cuda")
+
+    def step():
+        md_decoupled_step(p, grad, state, lr=lr, momentum=0.95, gain_lr=1e-3, gain_betas=(0.9, 0.95),
+                          gain_eps=1e-10, gain_mode="both", norm_axis="frobenius", ns_steps=5, capturable=True,
+                          rescale_mode="balanced")
+
+    return {"shape": [64, 1536, 1536]}, [("step", step, 0.0)]
+
+
+def _kernel_norm_rope(args, g):
+    """zRMSNorm and the fused residual add + zRMSNorm on [32768, 1536], partial RoPE on config 4's q/k."""
+    import torch
+
+    from modeling.liger_rope import PartialRopeFunction
+    from modeling.zRMSNorm import AddZRMSNormFunction, ZRMSNormFunction
+
+    x = torch.randn(32768, 1536, device="cuda", generator=g).requires_grad_(True)
+    w = (torch.randn(1536, device="cuda", generator=g) * 0.1).requires_grad_(True)
+    dy = torch.randn(32768, 1536, device="cuda", generator=g)
+    br = torch.randn(32768, 1536, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    q = torch.randn(8, 4096, 12, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(8, 4096, 4, 128, device="cuda", generator=g).bfloat16()
+    ang = torch.arange(4096, device="cuda", dtype=torch.float32)[:, None] * torch.logspace(0, -4, 8, device="cuda")
+    cos, sin = ang.cos().expand(8, 4096, 8).contiguous(), ang.sin().expand(8, 4096, 8).contiguous()
+
+    def norm():
+        y = ZRMSNormFunction.apply(x, w, 1e-6)
+        torch.autograd.grad(y, (x, w), dy)
+
+    def add_norm():
+        h, yb = AddZRMSNormFunction.apply(x, br, w, 1e-6)
+        torch.autograd.grad((h, yb), (x, br, w), (dy, dy.bfloat16()))
+
+    def rope():
+        qq, kk = q.clone().requires_grad_(True), k.clone().requires_grad_(True)
+        qo, ko = PartialRopeFunction.apply(qq * 1, kk * 1, cos, sin, 8)
+        torch.autograd.grad((qo, ko), (qq, kk), (torch.ones_like(qo), torch.ones_like(ko)))
+
+    return {"rows": [32768, 1536]}, [("zrmsnorm", norm, 0.0), ("add_zrmsnorm", add_norm, 0.0), ("rope", rope, 0.0)]
+
+
+def _kernel_routing(args, g):
+    """config 2 routing: sigmoid + biased top-8 of [16384, 64] bf16, flatten_sort_count, gate backward."""
+    import torch
+
+    from modeling.moe_gate import GateTopK
+    from scattermoe.parallel_experts import flatten_sort_count
+
+    logits = torch.randn(16384, 64, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    bias = torch.randn(64, device="cuda", generator=g) * 0.1
+
+    def route():
+        idx, w = GateTopK.apply(torch.sigmoid(logits), bias, 8)
+        flatten_sort_count(idx, 64)
+        torch.autograd.grad(w, logits, torch.ones_like(w))
+
+    return {"shape": [16384, 64, 8]}, [("route", route, 0.0)]
+
+
+KERNEL_WORKLOADS = {"attention": _kernel_attention, "newton_schulz": _kernel_newton_schulz, "xent": _kernel_xent,
+                    "muonmd": _kernel_muonmd, "norm_rope": _kernel_norm_rope, "routing": _kernel_routing}
+
+
+def run_kernel(args):
+    import torch
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    meta, parts = KERNEL_WORKLOADS[args.kernel](args, g)
+    out = {"kernel_workload": args.kernel, **meta, "passes": args.steps}
+    for name, fn, fl in parts:
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        out[name] = {"ms": ms, **({"tflops": fl / ms / 1e9} if fl else {})}
+    print(json.dumps(out), flush=True)
+
+
 def _free_port():
     import socket
 
@@ -914,11 +1074,17 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
     ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
+    ap.add_argument("--kernel", default=None, choices=sorted(KERNEL_WORKLOADS),
+                    help="time one fixed kernel workload instead of a config (for profiling)")
+    ap.add_argument("--batch", type=int, default=0, help="--kernel attention: sequences of 4096 (default 8)")
     ap.add_argument("--dp-engine", default="nccl", choices=["nccl", "ce"],
                     help="config 2 with N > 1: gradient all-reduce on the copy engines (ce) or NCCL")
     args = ap.parse_args()
     if not args.steps:
-        args.steps = 20 if args.config == 4 else 200
+        args.steps = 10 if args.kernel else (20 if args.config == 4 else 200)
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.impl == "reference":
         if args.config == 4:
             run_reference_config4(args)
