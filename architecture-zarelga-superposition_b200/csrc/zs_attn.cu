@@ -1126,95 +1126,91 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-// ---------------------------------------------------------- fused backward (hd 128)
+// ------------------------------------------- fused backward, 64-query ping-pong (hd 128)
 //
-// One kernel for dQ, dK and dV: one CTA per (128-key tile, kv head, batch row),
-// looping over the GQA group's query heads and 128-row query tiles.  Per
-// iteration (128 keys x 128 queries), on tcgen05 with every product in TMEM:
-//   S^T = K Q^T -> [0, 128),  dP^T = V dO^T -> [128, 256)            (MMA warp)
-//   P^T = exp2(S^T scale log2e - lse2), dS^T = P^T (dP^T - D)         (8 softmax warps)
-//        P^T (bf16 pairs) over S^T's columns [0, 64), dS^T over [128, 192), and dS
-//        to shared memory (MN-major, the A operand of dQ)
-//   dV += P^T dO -> [256, 384),  dK += dS^T Q -> [384, 512)           (A from TMEM)
-//   dQ  = dS K   -> [64, 128) (head columns 0..63), [192, 256) (64..127), the
-//        columns the softmax left free
-//   4 dQ warps add dQ into an f32 accumulator [B*S, H*hd] with vector reductions
-//   (red.global.add.v4.f32); attn_bwd_dq_finish_kernel then scales it, adds the
-//   sink term and writes bf16 dQ.
-// The two softmax warpgroups split the 128 query columns (64 each) over the same
-// key rows (TMEM lane quarters); the first group reads its upper 64 columns
-// first and releases them (named barrier per quarter) before the second group
-// writes its packed halves there.  The next S^T / dP^T into [0, 256) waits for
-// the dQ warps to have read dQ out; everything else is ordered by the tensor
-// pipe executing this CTA's MMAs in issue order.
-struct FusedBwdSmem {
-  static constexpr int TILE = 128 * 128 * 2;        // 128 rows x hd 128, bf16 (two 64-column atoms)
-  static constexpr int ATOM = 128 * 128;            // one 64-column atom of 128 rows (bytes)
+// dK, dV and dQ in one kernel: one CTA per (128-key tile, kv head, batch row),
+// looping over the GQA group's query heads and 64-row query tiles, the
+// iterations alternating between two TMEM buffers so the softmax of one overlaps
+// the products of the other.  Buffer g (128 columns at g*128), per iteration:
+//   S^T = K Q^T -> [0, 64), dP^T = V dO^T -> [64, 128)           (MMA warp)
+//   softmax group g: P^T (bf16 pairs) -> [0, 32), dS^T -> [32, 64), and dS to
+//       shared buffer g (the B operand of dQ^T)
+//   dV += P^T dO, dK += dS^T Q                   -> [256, 384), [384, 512)
+//   dQ^T = K^T dS                                -> [64, 128): head dim on the lanes,
+//       the 64 queries on the columns
+//   4 dQ warps read dQ^T and add it into the f32 accumulator: each warp
+//       instruction adds 32 consecutive head columns of one query row (128 bytes).
+// The next products into buffer g wait until its dQ^T has been read out.
+struct PingPongBwdSmem {
+  static constexpr int KT = 128 * 128 * 2;          // K, V tiles (128 keys, two 64-column atoms)
+  static constexpr int A128 = 128 * 128;            // one atom of a 128-row tile
+  static constexpr int QT = 64 * 128 * 2;           // Q, dO tiles of 64 rows
+  static constexpr int A64 = 64 * 128;              // one atom of a 64-row tile
+  static constexpr int NQS = 3;                     // Q/dO ring stages
+  static constexpr int DST = 128 * 128;             // dS buffer: 128 keys x 64 queries bf16 (one atom)
   static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = TILE;
-  static constexpr int OFF_QD = 2 * TILE;           // 2 stages x (Q, dO)
-  static constexpr int OFF_DS = OFF_QD + 4 * TILE;  // dS (bf16, MN-major: [2 atoms][128 keys][128 B])
-  static constexpr int OFF_LD = OFF_DS + TILE;      // lse2[128], D[128] (f32) of the current iteration
-  static constexpr int OFF_BAR = OFF_LD + 256 * 4;
-  // kv_full, qd_full[2], qd_empty[2], ld_full, sp_full, ds_full, dq_full, dq_empty, done, half_read[4]
-  static constexpr int NBAR = 15;
+  static constexpr int OFF_V = KT;
+  static constexpr int OFF_QD = 2 * KT;
+  static constexpr int OFF_DS = OFF_QD + NQS * 2 * QT;
+  static constexpr int OFF_LD = OFF_DS + 2 * DST;   // [2 groups][2] x (lse2[64], D[64])
+  static constexpr int OFF_BAR = OFF_LD + 4 * 128 * 4;
+  // kv_full, qd_full[NQS], qd_empty[NQS], sp_full[2], ds_full[2], dq_full[2], dq_empty[2], done, ld_full[4]
+  static constexpr int NBAR = 1 + 2 * NQS + 8 + 1 + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int TOTAL = OFF_MISC + 16;
-  static constexpr int ALLOC = TOTAL + 1024;
+  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
 };
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+__device__ __forceinline__ void red_add_f32(float* addr, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
 __global__ void __launch_bounds__(512, 1)
-    attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                          const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
-                          const BwdArgs a, float* __restrict__ dq_acc) {
-  using L = FusedBwdSmem;
+    attn_bwd_pingpong_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                             const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmDO64,
+                             const BwdArgs a, float* __restrict__ dq_acc) {
+  using L = PingPongBwdSmem;
   constexpr int HD = 128;
+  constexpr int NQS = L::NQS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;      // [2]
-  uint64_t* qd_empty = bars + 3;     // [2]
-  uint64_t* ld_full = bars + 5;
-  uint64_t* sp_full = bars + 6;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* dq_full = bars + 8;
-  uint64_t* dq_empty = bars + 9;
-  uint64_t* done = bars + 10;
-  uint64_t* half_read = bars + 11;   // [4]: per lane quarter, group 0 has read columns [32, 64)
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = qd_full + NQS;
+  uint64_t* sp_full = qd_empty + NQS;   // [2]
+  uint64_t* ds_full = sp_full + 2;      // [2]
+  uint64_t* dq_full = ds_full + 2;      // [2]
+  uint64_t* dq_empty = dq_full + 2;     // [2]
+  uint64_t* done = dq_empty + 2;
+  uint64_t* ld_full = done + 1;         // [4]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  float* s_lse2 = reinterpret_cast<float*>(smem + L::OFF_LD);
-  float* s_D = s_lse2 + 128;
+  float* s_ld = reinterpret_cast<float*>(smem + L::OFF_LD);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = a.H / a.Hkv;
   const int k0 = kt * 128;
   const int64_t row0 = (int64_t)b * a.S;
-  const int qt_lo = k0 / 128;
+  const int qt_lo = k0 / 64;
   int q_last = a.S - 1;
   if (a.window > 0) q_last = min(q_last, k0 + 127 + a.window - 1);
-  const int qt_hi = q_last / 128;
+  const int qt_hi = q_last / 64;
   const int n_q = qt_hi - qt_lo + 1;
   const int n_it = k0 < a.S ? G * n_q : 0;
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NQS; ++s) {
       mbar_init(&qd_full[s], 1);
       mbar_init(&qd_empty[s], 1);
     }
-    mbar_init(ld_full, 32);
-    mbar_init(sp_full, 1);
-    mbar_init(ds_full, 256);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sp_full[s], 1);
+      mbar_init(&ds_full[s], 128);
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_empty[s], 128);
+    }
     mbar_init(done, 1);
-    for (int x = 0; x < 4; ++x) mbar_init(&half_read[x], 32);
+    for (int s = 0; s < 4; ++s) mbar_init(&ld_full[s], 128);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -1226,102 +1222,86 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  constexpr uint32_t IDESC_SP = idesc_f16(128, 128, 1, 0, 0);
+  constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
   constexpr uint32_t IDESC_ACC = idesc_f16(128, HD, 1, 0, 1);
-  constexpr uint32_t IDESC_DQ = idesc_f16(128, 64, 1, 1, 1);
+  constexpr uint32_t IDESC_DQT = idesc_f16(128, 64, 1, 1, 1);
   if (warp == 0) {
-    // TMA for K, V (once) and the Q / dO ring (lane 0); lse2 / D of each iteration
-    // (all lanes) once the softmax of the previous one has finished reading them
-    uint32_t issued = 0, par = 0;
-    bool ok = n_it > 0;
-    if (ok && lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * L::TILE);
+    if (lane == 0 && n_it > 0) {
+      uint32_t issued = 0, par = 0;
+      mbar_arrive_expect_tx(kv_full, 2 * L::KT);
       for (int at = 0; at < 2; ++at) {
-        tma_load_2d(smem + L::OFF_K + at * L::ATOM, &tmK, kv_full, hk * HD + at * 64, (int)(row0 + k0));
-        tma_load_2d(smem + L::OFF_V + at * L::ATOM, &tmV, kv_full, hk * HD + at * 64, (int)(row0 + k0));
+        tma_load_2d(smem + L::OFF_K + at * L::A128, &tmK, kv_full, hk * HD + at * 64, (int)(row0 + k0));
+        tma_load_2d(smem + L::OFF_V + at * L::A128, &tmV, kv_full, hk * HD + at * 64, (int)(row0 + k0));
       }
-    }
-    for (int i = 0; ok && i < n_it; ++i) {
-      const int st = i & 1;
-      const int g = i / n_q, qi = qt_lo + i % n_q;
-      const int h = hk * G + g;
-      const int q0 = qi * 128;
-      if (!warp_wait(&qd_empty[st], ((i >> 1) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) {
-        uint8_t* qb = smem + L::OFF_QD + st * 2 * L::TILE;
-        mbar_arrive_expect_tx(&qd_full[st], 2 * L::TILE);
+      for (int i = 0; i < n_it; ++i) {
+        const int st = i % NQS;
+        const int g = i / n_q, qi = qt_lo + i % n_q;
+        const int h = hk * G + g;
+        if (!mbar_wait(&qd_empty[st], ((i / NQS) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
+        uint8_t* qb = smem + L::OFF_QD + st * 2 * L::QT;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * L::QT);
         for (int at = 0; at < 2; ++at) {
-          tma_load_2d(qb + at * L::ATOM, &tmQ, &qd_full[st], h * HD + at * 64, (int)(row0 + q0));
-          tma_load_2d(qb + L::TILE + at * L::ATOM, &tmDO, &qd_full[st], h * HD + at * 64, (int)(row0 + q0));
+          tma_load_2d(qb + at * L::A64, &tmQ64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
+          tma_load_2d(qb + L::QT + at * L::A64, &tmDO64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
         }
         issued |= 1u << st;
-        par = (par & ~(1u << st)) | ((uint32_t)((i >> 1) & 1) << st);
+        par = (par & ~(1u << st)) | ((uint32_t)((i / NQS) & 1) << st);
       }
-      if (i > 0 && !warp_wait(ds_full, (i - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) {
-        ok = false;
-        break;
-      }
-      const int64_t bh = (int64_t)b * a.H + h;
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const int qq = q0 + x * 32 + lane;
-        s_lse2[x * 32 + lane] = qq < a.S ? __ldg(a.lse + bh * a.S + qq) * LOG2E : INFINITY;
-        s_D[x * 32 + lane] = qq < a.S ? __ldg(a.D + bh * a.S + qq) : 0.f;
-      }
-      mbar_arrive(ld_full);
-    }
-    if (lane == 0 && n_it > 0) {
       mbar_wait(kv_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < 2; ++s)
+      for (int s = 0; s < NQS; ++s)
         if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
     }
-    __syncwarp();
   } else if (warp == 1) {
     bool ok = n_it > 0 && warp_wait(kv_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
     bool any = false;
     const uint32_t ka = smem_u32(smem + L::OFF_K), va = smem_u32(smem + L::OFF_V);
-    const uint32_t dsa = smem_u32(smem + L::OFF_DS);
-    for (int i = 0; ok && i < n_it; ++i) {
-      const int st = i & 1;
-      if (!warp_wait(&qd_full[st], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-      if (i > 0 && !warp_wait(dq_empty, (i - 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-      tc_fence_after();
-      const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::TILE), da = qa + L::TILE;
-      if (lane == 0) {
+    for (int i = 0; ok && i <= n_it; ++i) {
+      if (i < n_it) {
+        const int st = i % NQS, g = i & 1;
+        if (!warp_wait(&qd_full[st], (i / NQS) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        // buffer g's dQ^T of iteration i - 2 has been read out
+        if (i >= 2 && !warp_wait(&dq_empty[g], ((i - 2) >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk / 4) * L::ATOM + (kk % 4) * 32;
-          tc_mma_f16(tmem, smem_desc(ka + off, 16, 1024, 2), smem_desc(qa + off, 16, 1024, 2), IDESC_SP, kk > 0);
-          tc_mma_f16(tmem + 128, smem_desc(va + off, 16, 1024, 2), smem_desc(da + off, 16, 1024, 2), IDESC_SP,
-                     kk > 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t offa = (kk / 4) * L::A128 + (kk % 4) * 32, offb = (kk / 4) * L::A64 + (kk % 4) * 32;
+            tc_mma_f16(tmem + g * 128, smem_desc(ka + offa, 16, 1024, 2), smem_desc(qa + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+            tc_mma_f16(tmem + g * 128 + 64, smem_desc(va + offa, 16, 1024, 2), smem_desc(da + offb, 16, 1024, 2),
+                       IDESC_SP, kk > 0);
+          }
+          tc_commit(&sp_full[g]);
+          any = true;
         }
-        tc_commit(sp_full);
-        any = true;
+        __syncwarp();
       }
-      __syncwarp();
-      if (!warp_wait(ds_full, i & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-      tc_fence_after();
-      if (lane == 0) {
+      if (i >= 1) {
+        const int ii = i - 1, st = ii % NQS, g = ii & 1;
+        if (!warp_wait(&ds_full[g], (ii >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
+          const uint32_t dsa = smem_u32(smem + L::OFF_DS + g * L::DST);
 #pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          tc_mma_f16_ts(tmem + 256, tmem + kk * 8, smem_desc(da + kk * 2048, L::ATOM, 1024, 2), IDESC_ACC,
-                        (i > 0 || kk > 0) ? 1u : 0u);
-          tc_mma_f16_ts(tmem + 384, tmem + 128 + kk * 8, smem_desc(qa + kk * 2048, L::ATOM, 1024, 2), IDESC_ACC,
-                        (i > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+          for (int kk = 0; kk < 64 / 16; ++kk) {
+            tc_mma_f16_ts(tmem + 256, tmem + g * 128 + kk * 8, smem_desc(da + kk * 2048, L::A64, 1024, 2),
+                          IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16_ts(tmem + 384, tmem + g * 128 + 32 + kk * 8, smem_desc(qa + kk * 2048, L::A64, 1024, 2),
+                          IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
+          }
+          // dQ^T [hd x 64 queries] = K^T dS^T-as-B: A = K (MN-major, head dim on M),
+          // B = dS (MN-major, queries on N), contraction over the 128 keys
 #pragma unroll
           for (int kk = 0; kk < 128 / 16; ++kk)
-            tc_mma_f16(tmem + (hh == 0 ? 64 : 192), smem_desc(dsa + kk * 2048, L::ATOM, 1024, 2),
-                       smem_desc(ka + hh * L::ATOM + kk * 2048, L::ATOM, 1024, 2), IDESC_DQ, kk > 0);
-        tc_commit(&qd_empty[st]);
-        tc_commit(dq_full);
+            tc_mma_f16(tmem + g * 128 + 64, smem_desc(ka + kk * 2048, L::A128, 1024, 2),
+                       smem_desc(dsa + kk * 2048, L::A128, 1024, 2), IDESC_DQT, kk > 0);
+          tc_commit(&qd_empty[st]);
+          tc_commit(&dq_full[g]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (lane == 0 && any) {
       tc_commit(done);
@@ -1329,45 +1309,57 @@ __global__ void __launch_bounds__(512, 1)
     }
     __syncwarp();
   } else if (warp >= 4 && warp < 12) {
-    const int grp = (warp - 4) >> 2;          // query columns [64 grp, 64 grp + 64)
+    const int grp = (warp - 4) >> 2;          // buffer / alternate iterations
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;        // key row
     const int k = k0 + r;
     const bool kvalid = k < a.S;
-    const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* ds_row = smem + L::OFF_DS + (r >> 3) * 1024 + (r & 7) * 128;
+    const int tid = ((warp - 4) & 3) * 32 + lane;
+    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tb = tmem + lb + grp * 128;
+    uint8_t* ds_row = smem + L::OFF_DS + grp * L::DST + (r >> 3) * 1024 + (r & 7) * 128;
     bool ok = n_it > 0;
-    for (int i = 0; ok && i < n_it; ++i) {
+    for (int i = grp; i < n_it && ok; i += 2) {
+      const int u = i >> 1;
       const int g = i / n_q, qi = qt_lo + i % n_q;
-      (void)g;
-      const int q0 = qi * 128;
-      if (!warp_wait(ld_full, i & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE) ||
-          !warp_wait(sp_full, i & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      const int h = hk * G + g;
+      const int qb0 = qi * 64;
+      const int64_t bh = (int64_t)b * a.H + h;
+      const int li = grp * 2 + (u & 1);
+      float* s_lse2 = s_ld + li * 128;
+      float* s_D = s_lse2 + 64;
+      if (tid < 64) {
+        const int qq = qb0 + tid;
+        s_lse2[tid] = qq < a.S ? __ldg(a.lse + bh * a.S + qq) * LOG2E : INFINITY;
+      } else {
+        const int qq = qb0 + tid - 64;
+        s_D[tid - 64] = qq < a.S ? __ldg(a.D + bh * a.S + qq) : 0.f;
+      }
+      mbar_arrive(&ld_full[li]);
+      if (!warp_wait(&ld_full[li], (u >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE) ||
+          !warp_wait(&sp_full[grp], u & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool edge = (q0 < k0 + 128) || (q0 + 127 >= a.S) || a.seg_start != nullptr ||
-                        (a.window > 0 && q0 + 127 - k0 >= a.window);
-      // chunk c: query columns [16c, 16c + 16); packed outputs go to columns [8c, 8c + 8)
-      uint32_t held_p[2][8], held_d[2][8];
+      const bool edge = (qb0 < k0 + 128) || (qb0 + 63 >= a.S) || a.seg_start != nullptr ||
+                        (a.window > 0 && qb0 + 63 - k0 >= a.window);
+      uint32_t pw[4][8], dw[4][8];
 #pragma unroll
-      for (int step = 0; step < 4; ++step) {
-        const int c = grp == 0 ? ((step + 2) & 3) : 4 + step;   // group 0: chunks 2, 3, 0, 1
+      for (int ch = 0; ch < 4; ++ch) {
         uint32_t sr[16], dr[16];
-        tmem_ld_32x32b_x16(tb + c * 16, sr);
-        tmem_ld_32x32b_x16(tb + 128 + c * 16, dr);
+        tmem_ld_32x32b_x16(tb + ch * 16, sr);
+        tmem_ld_32x32b_x16(tb + 64 + ch * 16, dr);
         tc_wait_ld();
-        uint32_t pw[8], dw[8];
 #pragma unroll
         for (int x = 0; x < 8; ++x) {
           float pv[2], dv2[2];
 #pragma unroll
           for (int y = 0; y < 2; ++y) {
-            const int cl = 2 * x + y, qc = c * 16 + cl;
+            const int cl = 2 * x + y, c = ch * 16 + cl;
             bool vis = kvalid;
             if (edge) {
-              const int q = q0 + qc;
+              const int q = qb0 + c;
               vis = vis && q < a.S && q >= k;
               if (a.window > 0) vis = vis && (q - k < a.window);
               if (a.seg_start != nullptr) {
@@ -1375,53 +1367,33 @@ __global__ void __launch_bounds__(512, 1)
                 vis = vis && sg >= 0 && sg <= k;
               }
             }
-            const float p = vis ? fast_exp2(fmaf(__uint_as_float(sr[cl]), a.scale_log2, -s_lse2[qc])) : 0.f;
+            const float p = vis ? fast_exp2(fmaf(__uint_as_float(sr[cl]), a.scale_log2, -s_lse2[c])) : 0.f;
             pv[y] = p;
-            dv2[y] = p * (__uint_as_float(dr[cl]) - s_D[qc]);
+            dv2[y] = p * (__uint_as_float(dr[cl]) - s_D[c]);
           }
           __nv_bfloat162 p2 = __floats2bfloat162_rn(pv[0], pv[1]);
           __nv_bfloat162 d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
-          pw[x] = *reinterpret_cast<uint32_t*>(&p2);
-          dw[x] = *reinterpret_cast<uint32_t*>(&d2);
+          pw[ch][x] = *reinterpret_cast<uint32_t*>(&p2);
+          dw[ch][x] = *reinterpret_cast<uint32_t*>(&d2);
         }
-        // dS (bf16) for the dQ product: 16 queries = two 16-byte chunks of this key's row
-        // in atom c / 4, 128-byte swizzle (chunk index XOR row within the 8-row group)
-        {
-          uint8_t* base = ds_row + (c >> 2) * L::ATOM;
-          const int j0 = (c & 3) * 2;
-          *reinterpret_cast<uint4*>(base + ((j0 ^ (r & 7)) << 4)) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
-          *reinterpret_cast<uint4*>(base + (((j0 + 1) ^ (r & 7)) << 4)) = make_uint4(dw[4], dw[5], dw[6], dw[7]);
-        }
-        if (grp == 0 && step < 2) {
-#pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            held_p[step][x] = pw[x];
-            held_d[step][x] = dw[x];
-          }
-          if (step == 1) mbar_arrive(&half_read[quarter]);   // columns [32, 64), [160, 192) read
-          continue;
-        }
-        if (grp == 1 && step == 0 &&
-            !warp_wait(&half_read[quarter], i & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-          ok = false;
-          break;
-        }
-        tmem_st_32x32b_x8(tb + c * 8, pw);
-        tmem_st_32x32b_x8(tb + 128 + c * 8, dw);
+        // dS row of this key into shared buffer grp: queries [16ch, 16ch + 16) are 16-byte
+        // chunks 2ch and 2ch + 1 of the 128-byte row, XOR-swizzled with the row in its 8-row group
+        *reinterpret_cast<uint4*>(ds_row + (((2 * ch) ^ (r & 7)) << 4)) =
+            make_uint4(dw[ch][0], dw[ch][1], dw[ch][2], dw[ch][3]);
+        *reinterpret_cast<uint4*>(ds_row + (((2 * ch + 1) ^ (r & 7)) << 4)) =
+            make_uint4(dw[ch][4], dw[ch][5], dw[ch][6], dw[ch][7]);
       }
-      if (!ok) break;
-      if (grp == 0) {
-        tmem_st_32x32b_x8(tb + 16, held_p[0]);
-        tmem_st_32x32b_x8(tb + 128 + 16, held_d[0]);
-        tmem_st_32x32b_x8(tb + 24, held_p[1]);
-        tmem_st_32x32b_x8(tb + 128 + 24, held_d[1]);
+      // every S^T / dP^T column of this iteration has been read: P^T -> [0, 32), dS^T -> [32, 64)
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        tmem_st_32x32b_x8(tb + ch * 8, pw[ch]);
+        tmem_st_32x32b_x8(tb + 32 + ch * 8, dw[ch]);
       }
       tc_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[grp]);
     }
-    // after the last products: group 0 writes dV, group 1 dK (scaled)
     if (ok && n_it > 0 && warp_wait(done, 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
       const float mul = grp == 0 ? 1.0f : a.scale;
@@ -1429,7 +1401,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tb + 256 + grp * HD + c * 32, v);
+        tmem_ld_32x32b_x32(tmem + lb + 256 + grp * HD + c * 32, v);
         tc_wait_ld();
         if (kvalid) {
           uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
@@ -1448,35 +1420,36 @@ __global__ void __launch_bounds__(512, 1)
       }
     }
   } else if (warp >= 12) {
-    // dQ readout: query row r of the iteration's tile, head columns in two halves
+    // dQ^T readout: lane row = head column c, the 64 columns = the iteration's queries
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int c = quarter * 32 + lane;
+    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
     bool ok = n_it > 0;
     for (int i = 0; ok && i < n_it; ++i) {
+      const int gbuf = i & 1;
       const int g = i / n_q, qi = qt_lo + i % n_q;
       const int h = hk * G + g;
-      const int q = qi * 128 + r;
-      if (!warp_wait(dq_full, i & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
+      const int qb0 = qi * 64;
+      if (!warp_wait(&dq_full[gbuf], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float* dst = dq_acc + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+      float* dst = dq_acc + (row0 + qb0) * (int64_t)(a.H * a.hd) + (int64_t)h * HD + c;
+      const int nq = min(64, a.S - qb0);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int half = 0; half < 2; ++half) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tb + (c < 2 ? 64 : 192) + (c & 1) * 32, v);
+        tmem_ld_32x32b_x32(tmem + lb + gbuf * 128 + 64 + half * 32, v);
         tc_wait_ld();
-        if (q < a.S) {
 #pragma unroll
-          for (int x = 0; x < 8; ++x)
-            red_add_v4(dst + c * 32 + x * 4, __uint_as_float(v[4 * x]), __uint_as_float(v[4 * x + 1]),
-                       __uint_as_float(v[4 * x + 2]), __uint_as_float(v[4 * x + 3]));
+        for (int j = 0; j < 32; ++j) {
+          const int qq = half * 32 + j;
+          if (qq < nq) red_add_f32(dst + (int64_t)qq * (a.H * a.hd), __uint_as_float(v[j]));
         }
       }
       tc_fence_before();
-      mbar_arrive(dq_empty);
+      mbar_arrive(&dq_empty[gbuf]);
     }
   }
   tc_fence_before();
@@ -1586,10 +1559,10 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
                ZS_ERR_WORKSPACE);
     float* dq_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
     ZS_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)B * S * H * hd * sizeof(float), stream));
-    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn::FusedBwdSmem::ALLOC));
-    attn::attn_bwd_fused_kernel<<<gkv, 512, attn::FusedBwdSmem::ALLOC, stream>>>(tk128, tv128, tq128, tdo128, a,
-                                                                                 dq_acc);
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_pingpong_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::PingPongBwdSmem::ALLOC));
+    attn::attn_bwd_pingpong_kernel<<<gkv, 512, attn::PingPongBwdSmem::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a,
+                                                                                       dq_acc);
     ZS_CUDA_TRY(cudaGetLastError());
     attn::attn_bwd_dq_finish_kernel<<<(unsigned)blocks, 256, 0, stream>>>(dq_acc, a, ds_sink);
     ZS_CUDA_TRY(cudaGetLastError());
