@@ -1126,390 +1126,13 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-// ------------------------------------------- fused backward, 64-query ping-pong (hd 128)
-//
-// dK, dV and dQ in one kernel: one CTA per (128-key tile, kv head, batch row),
-// looping over the GQA group's query heads and 64-row query tiles, the
-// iterations alternating between two TMEM buffers so the softmax of one overlaps
-// the products of the other.  Buffer g (128 columns at g*128), per iteration:
-//   S^T = K Q^T -> [0, 64), dP^T = V dO^T -> [64, 128)           (MMA warp)
-//   softmax group g: P^T (bf16 pairs) -> [0, 32), dS^T -> [32, 64), and dS to
-//       shared buffer g (the B operand of dQ^T)
-//   dV += P^T dO, dK += dS^T Q                   -> [256, 384), [384, 512)
-//   dQ^T = K^T dS                                -> [64, 128): head dim on the lanes,
-//       the 64 queries on the columns
-//   4 dQ warps read dQ^T and add it into the f32 accumulator: each warp
-//       instruction adds 32 consecutive head columns of one query row (128 bytes).
-// The next products into buffer g wait until its dQ^T has been read out.
-struct PingPongBwdSmem {
-  static constexpr int KT = 128 * 128 * 2;          // K, V tiles (128 keys, two 64-column atoms)
-  static constexpr int A128 = 128 * 128;            // one atom of a 128-row tile
-  static constexpr int QT = 64 * 128 * 2;           // Q, dO tiles of 64 rows
-  static constexpr int A64 = 64 * 128;              // one atom of a 64-row tile
-  static constexpr int NQS = 3;                     // Q/dO ring stages
-  static constexpr int DST = 128 * 128;             // dS buffer: 128 keys x 64 queries bf16 (one atom)
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = KT;
-  static constexpr int OFF_QD = 2 * KT;
-  static constexpr int OFF_DS = OFF_QD + NQS * 2 * QT;
-  static constexpr int OFF_LD = OFF_DS + 2 * DST;   // [2 groups][2] x (lse2[64], D[64])
-  static constexpr int OFF_BAR = OFF_LD + 4 * 128 * 4;
-  // kv_full, qd_full[NQS], qd_empty[NQS], sp_full[2], ds_full[2], dq_full[2], dq_empty[2], done, ld_full[4]
-  static constexpr int NBAR = 1 + 2 * NQS + 8 + 1 + 4;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
-};
-
-__device__ __forceinline__ void red_add_f32(float* addr, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
-}
-
-__global__ void __launch_bounds__(512, 1)
-    attn_bwd_pingpong_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                             const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmDO64,
-                             const BwdArgs a, float* __restrict__ dq_acc) {
-  using L = PingPongBwdSmem;
-  constexpr int HD = 128;
-  constexpr int NQS = L::NQS;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = qd_full + NQS;
-  uint64_t* sp_full = qd_empty + NQS;   // [2]
-  uint64_t* ds_full = sp_full + 2;      // [2]
-  uint64_t* dq_full = ds_full + 2;      // [2]
-  uint64_t* dq_empty = dq_full + 2;     // [2]
-  uint64_t* done = dq_empty + 2;
-  uint64_t* ld_full = done + 1;         // [4]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  float* s_ld = reinterpret_cast<float*>(smem + L::OFF_LD);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-  const int G = a.H / a.Hkv;
-  const int k0 = kt * 128;
-  const int64_t row0 = (int64_t)b * a.S;
-  const int qt_lo = k0 / 64;
-  int q_last = a.S - 1;
-  if (a.window > 0) q_last = min(q_last, k0 + 127 + a.window - 1);
-  const int qt_hi = q_last / 64;
-  const int n_q = qt_hi - qt_lo + 1;
-  const int n_it = k0 < a.S ? G * n_q : 0;
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < NQS; ++s) {
-      mbar_init(&qd_full[s], 1);
-      mbar_init(&qd_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sp_full[s], 1);
-      mbar_init(&ds_full[s], 128);
-      mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_empty[s], 128);
-    }
-    mbar_init(done, 1);
-    for (int s = 0; s < 4; ++s) mbar_init(&ld_full[s], 128);
-    *s_abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(s_tmem, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *s_tmem;
-  constexpr uint32_t IDESC_SP = idesc_f16(128, 64, 1, 0, 0);
-  constexpr uint32_t IDESC_ACC = idesc_f16(128, HD, 1, 0, 1);
-  constexpr uint32_t IDESC_DQT = idesc_f16(128, 64, 1, 1, 1);
-  if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
-      uint32_t issued = 0, par = 0;
-      mbar_arrive_expect_tx(kv_full, 2 * L::KT);
-      for (int at = 0; at < 2; ++at) {
-        tma_load_2d(smem + L::OFF_K + at * L::A128, &tmK, kv_full, hk * HD + at * 64, (int)(row0 + k0));
-        tma_load_2d(smem + L::OFF_V + at * L::A128, &tmV, kv_full, hk * HD + at * 64, (int)(row0 + k0));
-      }
-      for (int i = 0; i < n_it; ++i) {
-        const int st = i % NQS;
-        const int g = i / n_q, qi = qt_lo + i % n_q;
-        const int h = hk * G + g;
-        if (!mbar_wait(&qd_empty[st], ((i / NQS) & 1) ^ 1, s_abort, ZS_DEVERR_TIMEOUT_PRODUCER)) break;
-        uint8_t* qb = smem + L::OFF_QD + st * 2 * L::QT;
-        mbar_arrive_expect_tx(&qd_full[st], 2 * L::QT);
-        for (int at = 0; at < 2; ++at) {
-          tma_load_2d(qb + at * L::A64, &tmQ64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
-          tma_load_2d(qb + L::QT + at * L::A64, &tmDO64, &qd_full[st], h * HD + at * 64, (int)(row0 + qi * 64));
-        }
-        issued |= 1u << st;
-        par = (par & ~(1u << st)) | ((uint32_t)((i / NQS) & 1) << st);
-      }
-      mbar_wait(kv_full, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < NQS; ++s)
-        if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-    }
-  } else if (warp == 1) {
-    bool ok = n_it > 0 && warp_wait(kv_full, 0, s_abort, ZS_DEVERR_TIMEOUT_MMA);
-    bool any = false;
-    const uint32_t ka = smem_u32(smem + L::OFF_K), va = smem_u32(smem + L::OFF_V);
-    for (int i = 0; ok && i <= n_it; ++i) {
-      if (i < n_it) {
-        const int st = i % NQS, g = i & 1;
-        if (!warp_wait(&qd_full[st], (i / NQS) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        // buffer g's dQ^T of iteration i - 2 has been read out
-        if (i >= 2 && !warp_wait(&dq_empty[g], ((i - 2) >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t offa = (kk / 4) * L::A128 + (kk % 4) * 32, offb = (kk / 4) * L::A64 + (kk % 4) * 32;
-            tc_mma_f16(tmem + g * 128, smem_desc(ka + offa, 16, 1024, 2), smem_desc(qa + offb, 16, 1024, 2),
-                       IDESC_SP, kk > 0);
-            tc_mma_f16(tmem + g * 128 + 64, smem_desc(va + offa, 16, 1024, 2), smem_desc(da + offb, 16, 1024, 2),
-                       IDESC_SP, kk > 0);
-          }
-          tc_commit(&sp_full[g]);
-          any = true;
-        }
-        __syncwarp();
-      }
-      if (i >= 1) {
-        const int ii = i - 1, st = ii % NQS, g = ii & 1;
-        if (!warp_wait(&ds_full[g], (ii >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t qa = smem_u32(smem + L::OFF_QD + st * 2 * L::QT), da = qa + L::QT;
-          const uint32_t dsa = smem_u32(smem + L::OFF_DS + g * L::DST);
-#pragma unroll
-          for (int kk = 0; kk < 64 / 16; ++kk) {
-            tc_mma_f16_ts(tmem + 256, tmem + g * 128 + kk * 8, smem_desc(da + kk * 2048, L::A64, 1024, 2),
-                          IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_f16_ts(tmem + 384, tmem + g * 128 + 32 + kk * 8, smem_desc(qa + kk * 2048, L::A64, 1024, 2),
-                          IDESC_ACC, (ii > 0 || kk > 0) ? 1u : 0u);
-          }
-          // dQ^T [hd x 64 queries] = K^T dS^T-as-B: A = K (MN-major, head dim on M),
-          // B = dS (MN-major, queries on N), contraction over the 128 keys
-#pragma unroll
-          for (int kk = 0; kk < 128 / 16; ++kk)
-            tc_mma_f16(tmem + g * 128 + 64, smem_desc(ka + kk * 2048, L::A128, 1024, 2),
-                       smem_desc(dsa + kk * 2048, L::A128, 1024, 2), IDESC_DQT, kk > 0);
-          tc_commit(&qd_empty[st]);
-          tc_commit(&dq_full[g]);
-        }
-        __syncwarp();
-      }
-    }
-    if (lane == 0 && any) {
-      tc_commit(done);
-      mbar_wait(done, 0, nullptr, ZS_DEVERR_TIMEOUT_DRAIN);
-    }
-    __syncwarp();
-  } else if (warp >= 4 && warp < 12) {
-    const int grp = (warp - 4) >> 2;          // buffer / alternate iterations
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;        // key row
-    const int k = k0 + r;
-    const bool kvalid = k < a.S;
-    const int tid = ((warp - 4) & 3) * 32 + lane;
-    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tb = tmem + lb + grp * 128;
-    uint8_t* ds_row = smem + L::OFF_DS + grp * L::DST + (r >> 3) * 1024 + (r & 7) * 128;
-    bool ok = n_it > 0;
-    for (int i = grp; i < n_it && ok; i += 2) {
-      const int u = i >> 1;
-      const int g = i / n_q, qi = qt_lo + i % n_q;
-      const int h = hk * G + g;
-      const int qb0 = qi * 64;
-      const int64_t bh = (int64_t)b * a.H + h;
-      const int li = grp * 2 + (u & 1);
-      float* s_lse2 = s_ld + li * 128;
-      float* s_D = s_lse2 + 64;
-      if (tid < 64) {
-        const int qq = qb0 + tid;
-        s_lse2[tid] = qq < a.S ? __ldg(a.lse + bh * a.S + qq) * LOG2E : INFINITY;
-      } else {
-        const int qq = qb0 + tid - 64;
-        s_D[tid - 64] = qq < a.S ? __ldg(a.D + bh * a.S + qq) : 0.f;
-      }
-      mbar_arrive(&ld_full[li]);
-      if (!warp_wait(&ld_full[li], (u >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE) ||
-          !warp_wait(&sp_full[grp], u & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool edge = (qb0 < k0 + 128) || (qb0 + 63 >= a.S) || a.seg_start != nullptr ||
-                        (a.window > 0 && qb0 + 63 - k0 >= a.window);
-      uint32_t pw[4][8], dw[4][8];
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sr[16], dr[16];
-        tmem_ld_32x32b_x16(tb + ch * 16, sr);
-        tmem_ld_32x32b_x16(tb + 64 + ch * 16, dr);
-        tc_wait_ld();
-#pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          float pv[2], dv2[2];
-#pragma unroll
-          for (int y = 0; y < 2; ++y) {
-            const int cl = 2 * x + y, c = ch * 16 + cl;
-            bool vis = kvalid;
-            if (edge) {
-              const int q = qb0 + c;
-              vis = vis && q < a.S && q >= k;
-              if (a.window > 0) vis = vis && (q - k < a.window);
-              if (a.seg_start != nullptr) {
-                const int sg = q < a.S ? __ldg(a.seg_start + row0 + q) : -1;
-                vis = vis && sg >= 0 && sg <= k;
-              }
-            }
-            const float p = vis ? fast_exp2(fmaf(__uint_as_float(sr[cl]), a.scale_log2, -s_lse2[c])) : 0.f;
-            pv[y] = p;
-            dv2[y] = p * (__uint_as_float(dr[cl]) - s_D[c]);
-          }
-          __nv_bfloat162 p2 = __floats2bfloat162_rn(pv[0], pv[1]);
-          __nv_bfloat162 d2 = __floats2bfloat162_rn(dv2[0], dv2[1]);
-          pw[ch][x] = *reinterpret_cast<uint32_t*>(&p2);
-          dw[ch][x] = *reinterpret_cast<uint32_t*>(&d2);
-        }
-        // dS row of this key into shared buffer grp: queries [16ch, 16ch + 16) are 16-byte
-        // chunks 2ch and 2ch + 1 of the 128-byte row, XOR-swizzled with the row in its 8-row group
-        *reinterpret_cast<uint4*>(ds_row + (((2 * ch) ^ (r & 7)) << 4)) =
-            make_uint4(dw[ch][0], dw[ch][1], dw[ch][2], dw[ch][3]);
-        *reinterpret_cast<uint4*>(ds_row + (((2 * ch + 1) ^ (r & 7)) << 4)) =
-            make_uint4(dw[ch][4], dw[ch][5], dw[ch][6], dw[ch][7]);
-      }
-      // every S^T / dP^T column of this iteration has been read: P^T -> [0, 32), dS^T -> [32, 64)
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        tmem_st_32x32b_x8(tb + ch * 8, pw[ch]);
-        tmem_st_32x32b_x8(tb + 32 + ch * 8, dw[ch]);
-      }
-      tc_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&ds_full[grp]);
-    }
-    if (ok && n_it > 0 && warp_wait(done, 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-      tc_fence_after();
-      const float mul = grp == 0 ? 1.0f : a.scale;
-      __nv_bfloat16* dst_row = (grp == 0 ? a.dv : a.dk) + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lb + 256 + grp * HD + c * 32, v);
-        tc_wait_ld();
-        if (kvalid) {
-          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            uint32_t w[4];
-#pragma unroll
-            for (int y = 0; y < 4; ++y) {
-              __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(v[x * 8 + 2 * y]) * mul,
-                                                        __uint_as_float(v[x * 8 + 2 * y + 1]) * mul);
-              w[y] = *reinterpret_cast<uint32_t*>(&pp);
-            }
-            dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-      }
-    }
-  } else if (warp >= 12) {
-    // dQ^T readout: lane row = head column c, the 64 columns = the iteration's queries
-    const int quarter = warp & 3;
-    const int c = quarter * 32 + lane;
-    const uint32_t lb = (uint32_t)(quarter * 32) << 16;
-    bool ok = n_it > 0;
-    for (int i = 0; ok && i < n_it; ++i) {
-      const int gbuf = i & 1;
-      const int g = i / n_q, qi = qt_lo + i % n_q;
-      const int h = hk * G + g;
-      const int qb0 = qi * 64;
-      if (!warp_wait(&dq_full[gbuf], (i >> 1) & 1, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float* dst = dq_acc + (row0 + qb0) * (int64_t)(a.H * a.hd) + (int64_t)h * HD + c;
-      const int nq = min(64, a.S - qb0);
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lb + gbuf * 128 + 64 + half * 32, v);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int qq = half * 32 + j;
-          if (qq < nq) red_add_f32(dst + (int64_t)qq * (a.H * a.hd), __uint_as_float(v[j]));
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&dq_empty[gbuf]);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// dQ = bf16(scale * (dq_acc + dS_sink k_sink)), dS_sink = -P_sink D (sink value 0),
-// one warp per (token, head); ds_sink (when the sink exists) receives dS_sink.
-__global__ void attn_bwd_dq_finish_kernel(const float* __restrict__ dq_acc, const BwdArgs a,
-                                          float* __restrict__ ds_sink) {
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)a.B * a.S * a.H;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows; w += warps) {
-    const int64_t tok = w / a.H;
-    const int h = (int)(w - tok * a.H);
-    const int64_t b = tok / a.S, qpos = tok - b * a.S;
-    const int64_t off = tok * (int64_t)(a.H * a.hd) + (int64_t)h * a.hd;
-    const float4 acc = *reinterpret_cast<const float4*>(dq_acc + off + lane * 4);
-    float v[4] = {acc.x, acc.y, acc.z, acc.w};
-    if (a.k_sink != nullptr) {
-      const int64_t bh = b * a.H + h;
-      float dot = 0.f;
-#pragma unroll
-      for (int x = 0; x < 4; ++x) dot = fmaf(__bfloat162float(a.q[off + lane * 4 + x]), sink_at(a, h * a.hd + lane * 4 + x), dot);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      const float lse2 = __ldg(a.lse + bh * a.S + qpos) * LOG2E;
-      const float dss = -fast_exp2(dot * a.scale_log2 - lse2) * __ldg(a.D + bh * a.S + qpos);
-      if (lane == 0) ds_sink[bh * a.S + qpos] = dss;
-#pragma unroll
-      for (int x = 0; x < 4; ++x) v[x] = fmaf(dss, sink_at(a, h * a.hd + lane * 4 + x), v[x]);
-    }
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0] * a.scale, v[1] * a.scale);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2] * a.scale, v[3] * a.scale);
-    uint2 o2;
-    o2.x = *reinterpret_cast<uint32_t*>(&p0);
-    o2.y = *reinterpret_cast<uint32_t*>(&p1);
-    *reinterpret_cast<uint2*>(a.dq + off + lane * 4) = o2;
-  }
-}
-
 }  // namespace attn
 }  // namespace zs
-
-extern "C" size_t zs_attention_backward_workspace(int B, int S, int H, int hd) {
-  // head dim 128: the f32 dQ accumulator of the fused kernel
-  return hd == 128 ? (size_t)B * S * H * hd * sizeof(float) + 256 : 0;
-}
 
 extern "C" int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
                                      const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H,
                                      int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
-                                     int sink_dtype, float* ds_sink, float softmax_scale, void* workspace,
-                                     size_t workspace_bytes, void* stream_) {
+                                     int sink_dtype, float* ds_sink, float softmax_scale, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv && D, ZS_ERR_ARG);
   ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, ZS_ERR_SHAPE);
@@ -1555,28 +1178,24 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   dim3 gq((S + 127) / 128, H, B), gkv((S + 127) / 128, Hkv, B);
   if (hd == 128) {
-    ZS_REQUIRE(workspace != nullptr && workspace_bytes >= zs_attention_backward_workspace(B, S, H, hd),
-               ZS_ERR_WORKSPACE);
-    float* dq_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
-    ZS_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)B * S * H * hd * sizeof(float), stream));
-    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_pingpong_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     attn::PingPongBwdSmem::ALLOC));
-    attn::attn_bwd_pingpong_kernel<<<gkv, 512, attn::PingPongBwdSmem::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a,
-                                                                                       dq_acc);
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DqSmem<128>::ALLOC));
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DkvSmem<128>::ALLOC));
+    attn::attn_bwd_dq_kernel<128><<<gq, 320, attn::DqSmem<128>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+                                                                                 ds_sink);
     ZS_CUDA_TRY(cudaGetLastError());
-    attn::attn_bwd_dq_finish_kernel<<<(unsigned)blocks, 256, 0, stream>>>(dq_acc, a, ds_sink);
+    attn::attn_bwd_dkv_kernel<128><<<gkv, 320, attn::DkvSmem<128>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
+  } else {
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DqSmem<64>::ALLOC));
+    ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn::DkvSmem<64>::ALLOC));
+    attn::attn_bwd_dq_kernel<64><<<gq, 320, attn::DqSmem<64>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
+                                                                               ds_sink);
     ZS_CUDA_TRY(cudaGetLastError());
-    return ZS_OK;
+    attn::attn_bwd_dkv_kernel<64><<<gkv, 320, attn::DkvSmem<64>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
   }
-  // head dim 64: the dQ kernel per query tile and the dK/dV kernel per key tile
-  ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   attn::DqSmem<64>::ALLOC));
-  ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   attn::DkvSmem<64>::ALLOC));
-  attn::attn_bwd_dq_kernel<64><<<gq, 320, attn::DqSmem<64>::ALLOC, stream>>>(tq128, tdo128, tk64, tv64, a,
-                                                                             ds_sink);
-  ZS_CUDA_TRY(cudaGetLastError());
-  attn::attn_bwd_dkv_kernel<64><<<gkv, 320, attn::DkvSmem<64>::ALLOC, stream>>>(tk128, tv128, tq64, tdo64, a);
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
 }

@@ -62,9 +62,8 @@ _SIGNATURES = {
                        _i32, _vp]),
     "zs_attention_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i32,
                                     _f32, _vp]),
-    "zs_attention_backward_workspace": (_sz, [_i32, _i32, _i32, _i32]),
     "zs_attention_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
-                                     _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _sz, _vp]),
+                                     _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp]),
     "zs_muonmd_pre_workspace": (_sz, [_i64, _i64, _i64]),
     "zs_ipc_handle_size": (_i32, []),
     "zs_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),

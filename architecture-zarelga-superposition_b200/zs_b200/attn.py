@@ -75,15 +75,12 @@ class _Attention(torch.autograd.Function):
         D = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
         ds_sink = torch.empty(B, H, S, dtype=torch.float32, device=q.device) if k_sink is not None else None
         L = Z.lib()
-        ws_bytes = int(L.zs_attention_backward_workspace(B, S, H, hd))
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         with Z.timed("attention_bwd", 2.5 * attention_flops(B, S, H, hd, ctx.window)):
             Z.check(L.zs_attention_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
                                             lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                             D.data_ptr(), B, S, H, Hkv, hd, ctx.window, Z.ptr(seg_start),
                                             Z.ptr(k_sink), Z.dtype_code(k_sink.dtype) if k_sink is not None else 0,
-                                            Z.ptr(ds_sink), ctx.scale, Z.ptr(ws), ws_bytes, Z.stream_of(q)),
-                    "zs_attention_backward")
+                                            Z.ptr(ds_sink), ctx.scale, Z.stream_of(q)), "zs_attention_backward")
         Z.count(3)
         dk_sink = None
         if k_sink is not None and ctx.needs_input_grad[3]:

@@ -372,17 +372,12 @@ int zs_attention_forward(const void* q, const void* k, const void* v, void* o, f
  * scratch: rowsum(dout * o)), and with k_sink: ds_sink (f32 [B, H, S]) =
  * d loss / d (sink logit) per query row; the sink's own gradient is
  * scale * sum_{b,q} ds_sink[b, h, q] * q[b, q, h, :].  dq already holds the
- * sink key's share.  hd 128 runs one fused kernel per 128-key tile that adds its
- * dQ share into an f32 accumulator in the workspace
- * (zs_attention_backward_workspace bytes; 0 for hd 64, where workspace may be
- * NULL); the reduction order of that sum varies between runs.
+ * sink key's share.
  */
-size_t zs_attention_backward_workspace(int B, int S, int H, int hd);
 int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
                           const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H, int Hkv,
                           int hd, int window, const int* seg_start, const void* k_sink, int sink_dtype,
-                          float* ds_sink, float softmax_scale, void* workspace, size_t workspace_bytes,
-                          void* stream);
+                          float* ds_sink, float softmax_scale, void* stream);
 
 /* ------------------------------------------------ cross entropy (a16-a18) */
 
