@@ -38,8 +38,11 @@ struct FwdArgs {
   const int* seg_start;       // nullable [B*S]: first position of the token's packed sequence (-1: padding)
   const void* k_sink;         // nullable [H, hd] (dtype of sink_dtype)
   int sink_dtype;
-  __nv_bfloat16* o;           // [B*S, H*hd]
+  __nv_bfloat16* o;           // [B*S, H*hd] rows of ldo elements
+  int64_t ldo;
   float* lse;                 // [B, H, S] natural-log log-sum-exp
+  const __nv_bfloat16* gate;  // nullable [B*S, H] rows of ldg: O is multiplied by sigmoid(gate)
+  int64_t ldg;
 };
 
 template <int HD>
@@ -441,8 +444,12 @@ __global__ void __launch_bounds__(320, 1)
     }
     if (ok && warp_wait(&o_done[t], 0, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      __nv_bfloat16* orow_g = a.o + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+      float inv = l > 0.f ? 1.0f / l : 0.f;
+      if (a.gate != nullptr && qvalid) {   // the head's output gate, sigmoid in f32
+        const float gl = __bfloat162float(a.gate[(row0 + q) * a.ldg + h]);
+        inv *= 1.0f / (1.0f + expf(-gl));
+      }
+      __nv_bfloat16* orow_g = a.o + (row0 + q) * a.ldo + (int64_t)h * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t orow[32];
@@ -480,22 +487,32 @@ __global__ void __launch_bounds__(320, 1)
 
 using namespace zs;
 
-extern "C" int zs_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int S,
-                                    int H, int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
-                                    int sink_dtype, float softmax_scale, void* stream_) {
+static bool attn_ld_ok(const void* p, int64_t ld, int64_t width) {
+  return p == nullptr || (ld >= width && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0);
+}
+
+extern "C" int zs_gated_attention_forward(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                          int64_t ldv, void* o, int64_t ldo, float* lse, const void* gate_logits,
+                                          int64_t ldg, int B, int S, int H, int Hkv, int hd, int window,
+                                          const int* seg_start, const void* k_sink, int sink_dtype,
+                                          float softmax_scale, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(q && k && v && o && lse, ZS_ERR_ARG);
   ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, ZS_ERR_SHAPE);
   ZS_REQUIRE(hd == 64 || hd == 128, ZS_ERR_SHAPE);
   ZS_REQUIRE((int64_t)B * S < ((int64_t)1 << 31), ZS_ERR_SHAPE);
   ZS_REQUIRE(k_sink == nullptr || sink_dtype == ZS_F32 || sink_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(attn_ld_ok(q, ldq, (int64_t)H * hd) && attn_ld_ok(k, ldk, (int64_t)Hkv * hd) &&
+                 attn_ld_ok(v, ldv, (int64_t)Hkv * hd) && attn_ld_ok(o, ldo, (int64_t)H * hd),
+             ZS_ERR_ALIGN);
+  ZS_REQUIRE(gate_logits == nullptr || ldg >= H, ZS_ERR_SHAPE);
   ZS_BIND(q);
   CUtensorMap tq, tk, tv;
   int rc;
   const uint64_t rows = (uint64_t)B * S;
-  if ((rc = make_tmap(&tq, q, ZS_BF16, (uint64_t)H * hd, rows, (uint64_t)H * hd * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tk, k, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)Hkv * hd * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tv, v, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)Hkv * hd * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tq, q, ZS_BF16, (uint64_t)H * hd, rows, (uint64_t)ldq * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk, k, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)ldk * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv, v, ZS_BF16, (uint64_t)Hkv * hd, rows, (uint64_t)ldv * 2, 64, 128)) != ZS_OK) return rc;
   attn::FwdArgs a{};
   a.B = B;
   a.S = S;
@@ -508,7 +525,10 @@ extern "C" int zs_attention_forward(const void* q, const void* k, const void* v,
   a.k_sink = k_sink;
   a.sink_dtype = sink_dtype;
   a.o = reinterpret_cast<__nv_bfloat16*>(o);
+  a.ldo = ldo;
   a.lse = lse;
+  a.gate = reinterpret_cast<const __nv_bfloat16*>(gate_logits);
+  a.ldg = ldg;
   dim3 grid((S + 2 * attn::BQ - 1) / (2 * attn::BQ), H, B);
   if (hd == 128) {
     using L = attn::FwdSmem<128>;
@@ -521,6 +541,14 @@ extern "C" int zs_attention_forward(const void* q, const void* k, const void* v,
   }
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
+}
+
+extern "C" int zs_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int S,
+                                    int H, int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
+                                    int sink_dtype, float softmax_scale, void* stream) {
+  const int64_t qw = (int64_t)H * hd, kw = (int64_t)Hkv * hd;
+  return zs_gated_attention_forward(q, qw, k, kw, v, kw, o, qw, lse, nullptr, 0, B, S, H, Hkv, hd, window, seg_start,
+                                    k_sink, sink_dtype, softmax_scale, stream);
 }
 
 // ------------------------------------------------------------------ backward
@@ -551,9 +579,11 @@ struct BwdArgs {
   const void* k_sink;   // nullable [H, hd]
   int sink_dtype;
   const __nv_bfloat16* q;
+  int64_t ldq;          // row strides (elements) of q and of the three gradients
   __nv_bfloat16* dq;    // [B*S, H*hd]
   __nv_bfloat16* dk;    // [B*S, Hkv*hd]
   __nv_bfloat16* dv;
+  int64_t lddq, lddk, lddv;
 };
 
 __device__ __forceinline__ float sink_at(const BwdArgs& a, int i) {
@@ -561,17 +591,25 @@ __device__ __forceinline__ float sink_at(const BwdArgs& a, int i) {
                                 : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.k_sink)[i]);
 }
 
-// D[b, h, q] = sum_d dO * O over the head's row
-__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                                     float* __restrict__ D, int B, int S, int H, int hd) {
+// D[b, h, q] = sum_d dO * O over the head's row.  With an output gate (the forward
+// stored O_g = sigmoid(z) * O): dout is the gradient of O_g, and per (token, head)
+//   D      = sum_d dout * O_g   (= sum_d dO * O for dO = sigmoid(z) * dout)
+//   do_raw = bf16(sigmoid(z) * dout)               (the attention core's dO)
+//   dz     = D * (1 - sigmoid(z))                  (d loss / d gate logit)
+// and the gate_pad columns after the H gate-gradient columns are zeroed.
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
+                                     const __nv_bfloat16* __restrict__ dout, int64_t lddo,
+                                     const __nv_bfloat16* __restrict__ gate, int64_t ldg,
+                                     __nv_bfloat16* __restrict__ do_raw, __nv_bfloat16* __restrict__ dgate,
+                                     int64_t lddg, int gate_pad, float* __restrict__ D, int B, int S, int H, int hd) {
   const int lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)B * S * H;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows; w += warps) {
     const int64_t tok = w / H;
     const int h = (int)(w - tok * H);
-    const __nv_bfloat16* po = o + tok * (int64_t)H * hd + (int64_t)h * hd;
-    const __nv_bfloat16* pd = dout + tok * (int64_t)H * hd + (int64_t)h * hd;
+    const __nv_bfloat16* po = o + tok * ldo + (int64_t)h * hd;
+    const __nv_bfloat16* pd = dout + tok * lddo + (int64_t)h * hd;
     float acc = 0.f;
     for (int c = lane * 2; c < hd; c += 64) {
       const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + c));
@@ -582,6 +620,16 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const 
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     const int64_t b = tok / S, q = tok - b * S;
     if (lane == 0) D[(b * H + h) * S + q] = acc;
+    if (gate != nullptr) {
+      const float g = 1.0f / (1.0f + expf(-__bfloat162float(gate[tok * ldg + h])));
+      __nv_bfloat16* pr = do_raw + tok * (int64_t)H * hd + (int64_t)h * hd;
+      for (int c = lane * 2; c < hd; c += 64) {
+        const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + c));
+        *reinterpret_cast<__nv_bfloat162*>(pr + c) = __floats2bfloat162_rn(g * d.x, g * d.y);
+      }
+      if (lane == 0) dgate[tok * lddg + h] = __float2bfloat16_rn(acc * (1.0f - g));
+      if (h == 0 && lane < gate_pad) dgate[tok * lddg + H + lane] = __float2bfloat16_rn(0.f);
+    }
   }
 }
 
@@ -805,13 +853,13 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       float dss = 0.f;
       if (a.k_sink != nullptr && qvalid) {
-        const __nv_bfloat16* qr = a.q + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+        const __nv_bfloat16* qr = a.q + (row0 + q) * a.ldq + (int64_t)h * HD;
         float dot = 0.f;
         for (int c = 0; c < HD; ++c) dot = fmaf(__bfloat162float(qr[c]), sink_at(a, h * HD + c), dot);
         dss = -fast_exp2(dot * a.scale_log2 - lse2) * Dq;
         if (grp == 0) ds_sink[bh * a.S + q] = dss;
       }
-      __nv_bfloat16* out = a.dq + (row0 + q) * (int64_t)(a.H * a.hd) + (int64_t)h * HD;
+      __nv_bfloat16* out = a.dq + (row0 + q) * a.lddq + (int64_t)h * HD;
 #pragma unroll 1
       for (int c = grp * (HD / 64); c < (grp + 1) * (HD / 64); ++c) {
         uint32_t v[32];
@@ -1094,7 +1142,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const int part = grp;
       const float mul = part == 0 ? 1.0f : a.scale;
-      __nv_bfloat16* dst_row = (part == 0 ? a.dv : a.dk) + (row0 + k) * (int64_t)(a.Hkv * a.hd) + (int64_t)hk * HD;
+      __nv_bfloat16* dst_row = (part == 0 ? a.dv + (row0 + k) * a.lddv : a.dk + (row0 + k) * a.lddk) + (int64_t)hk * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
@@ -1129,10 +1177,16 @@ __global__ void __launch_bounds__(320, 1)
 }  // namespace attn
 }  // namespace zs
 
-extern "C" int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
-                                     const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H,
-                                     int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
-                                     int sink_dtype, float* ds_sink, float softmax_scale, void* stream_) {
+extern "C" size_t zs_gated_attention_backward_workspace(int B, int S, int H, int hd, int gated) {
+  return gated ? (size_t)B * S * H * hd * 2 + 256 : 0;
+}
+
+extern "C" int zs_gated_attention_backward(
+    const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, const void* o, int64_t ldo,
+    const void* dout, int64_t lddo, const float* lse, const void* gate_logits, int64_t ldg, void* dq, int64_t lddq,
+    void* dk, int64_t lddk, void* dv, int64_t lddv, void* dgate_logits, int64_t lddg, int gate_pad, float* D, int B,
+    int S, int H, int Hkv, int hd, int window, const int* seg_start, const void* k_sink, int sink_dtype,
+    float* ds_sink, float softmax_scale, void* workspace, size_t workspace_bytes, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv && D, ZS_ERR_ARG);
   ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, ZS_ERR_SHAPE);
@@ -1140,24 +1194,43 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
   ZS_REQUIRE((k_sink == nullptr) == (ds_sink == nullptr), ZS_ERR_ARG);
   ZS_REQUIRE(k_sink == nullptr || sink_dtype == ZS_F32 || sink_dtype == ZS_BF16, ZS_ERR_DTYPE);
   ZS_REQUIRE((int64_t)B * S < ((int64_t)1 << 31), ZS_ERR_SHAPE);
+  const int64_t qw = (int64_t)H * hd, kw = (int64_t)Hkv * hd;
+  ZS_REQUIRE(attn_ld_ok(q, ldq, qw) && attn_ld_ok(k, ldk, kw) && attn_ld_ok(v, ldv, kw) && attn_ld_ok(o, ldo, qw) &&
+                 attn_ld_ok(dout, lddo, qw) && attn_ld_ok(dq, lddq, qw) && attn_ld_ok(dk, lddk, kw) &&
+                 attn_ld_ok(dv, lddv, kw),
+             ZS_ERR_ALIGN);
+  const bool gated = gate_logits != nullptr;
+  ZS_REQUIRE(!gated || (dgate_logits != nullptr && ldg >= H && lddg >= H + gate_pad && gate_pad >= 0 &&
+                        gate_pad < 32),
+             ZS_ERR_ARG);
+  ZS_REQUIRE(!gated || (workspace != nullptr &&
+                        workspace_bytes >= zs_gated_attention_backward_workspace(B, S, H, hd, 1)),
+             ZS_ERR_WORKSPACE);
   ZS_BIND(q);
+  // the attention core's dO: dout itself, or sigmoid(gate) * dout in the workspace
+  __nv_bfloat16* do_raw =
+      gated ? reinterpret_cast<__nv_bfloat16*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255))
+            : nullptr;
+  const void* dO = gated ? static_cast<const void*>(do_raw) : dout;
+  const int64_t lddO = gated ? qw : lddo;
   int64_t blocks = ((int64_t)B * S * H + 7) / 8;
   if (blocks > 148 * 32) blocks = 148 * 32;
   attn::attn_bwd_prep_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(dout), D, B, S, H, hd);
+      reinterpret_cast<const __nv_bfloat16*>(o), ldo, reinterpret_cast<const __nv_bfloat16*>(dout), lddo,
+      reinterpret_cast<const __nv_bfloat16*>(gate_logits), ldg, do_raw,
+      reinterpret_cast<__nv_bfloat16*>(dgate_logits), lddg, gate_pad, D, B, S, H, hd);
   ZS_CUDA_TRY(cudaGetLastError());
   const uint64_t rows = (uint64_t)B * S;
   CUtensorMap tq128, tdo128, tk64, tv64, tk128, tv128, tq64, tdo64;
   int rc;
-  const uint64_t qw = (uint64_t)H * hd, kw = (uint64_t)Hkv * hd;
-  if ((rc = make_tmap(&tq128, q, ZS_BF16, qw, rows, qw * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tdo128, dout, ZS_BF16, qw, rows, qw * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tq64, q, ZS_BF16, qw, rows, qw * 2, 64, 64)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tdo64, dout, ZS_BF16, qw, rows, qw * 2, 64, 64)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tk128, k, ZS_BF16, kw, rows, kw * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tv128, v, ZS_BF16, kw, rows, kw * 2, 64, 128)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tk64, k, ZS_BF16, kw, rows, kw * 2, 64, 64)) != ZS_OK) return rc;
-  if ((rc = make_tmap(&tv64, v, ZS_BF16, kw, rows, kw * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tq128, q, ZS_BF16, qw, rows, ldq * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tdo128, dO, ZS_BF16, qw, rows, lddO * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tq64, q, ZS_BF16, qw, rows, ldq * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tdo64, dO, ZS_BF16, qw, rows, lddO * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk128, k, ZS_BF16, kw, rows, ldk * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv128, v, ZS_BF16, kw, rows, ldv * 2, 64, 128)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tk64, k, ZS_BF16, kw, rows, ldk * 2, 64, 64)) != ZS_OK) return rc;
+  if ((rc = make_tmap(&tv64, v, ZS_BF16, kw, rows, ldv * 2, 64, 64)) != ZS_OK) return rc;
   attn::BwdArgs a{};
   a.B = B;
   a.S = S;
@@ -1173,9 +1246,13 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
   a.k_sink = k_sink;
   a.sink_dtype = sink_dtype;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.ldq = ldq;
   a.dq = reinterpret_cast<__nv_bfloat16*>(dq);
   a.dk = reinterpret_cast<__nv_bfloat16*>(dk);
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  a.lddq = lddq;
+  a.lddk = lddk;
+  a.lddv = lddv;
   dim3 gq((S + 127) / 128, H, B), gkv((S + 127) / 128, Hkv, B);
   if (hd == 128) {
     ZS_CUDA_TRY(cudaFuncSetAttribute(attn::attn_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1198,4 +1275,14 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
   }
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
+}
+
+extern "C" int zs_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                     const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H,
+                                     int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
+                                     int sink_dtype, float* ds_sink, float softmax_scale, void* stream) {
+  const int64_t qw = (int64_t)H * hd, kw = (int64_t)Hkv * hd;
+  return zs_gated_attention_backward(q, qw, k, kw, v, kw, o, qw, dout, qw, lse, nullptr, 0, dq, qw, dk, kw, dv, kw,
+                                     nullptr, 0, 0, D, B, S, H, Hkv, hd, window, seg_start, k_sink, sink_dtype,
+                                     ds_sink, softmax_scale, nullptr, 0, stream);
 }

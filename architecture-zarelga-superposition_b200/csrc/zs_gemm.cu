@@ -1870,14 +1870,15 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
   char* Bbuf = Abuf + ((batch * m * m * es + 255) / 256) * 256;
   char* Xtmp = Bbuf + ((batch * m * m * es + 255) / 256) * 256;
   float* ss = reinterpret_cast<float*>(Xtmp + ((batch * m * n * es + 255) / 256) * 256);  // [batch, 32] partials
-  // X0 = G / (||G|| + 1e-7) -> X_out; iterate X_out -> Xtmp -> X_out ...
+  // X0 = G / (||G|| + 1e-7); the iterates alternate between two buffers, X0 placed so
+  // that the last one lands in X_out (no final copy)
+  char* X = (steps & 1) ? Xtmp : reinterpret_cast<char*>(X_out);
+  char* Xn = (steps & 1) ? reinterpret_cast<char*>(X_out) : Xtmp;
   {
-    const int rc = dtype == ZS_BF16 ? ns_normalize<__nv_bfloat16>(G, X_out, ss, batch, m * n, stream)
-                                    : ns_normalize<__half>(G, X_out, ss, batch, m * n, stream);
+    const int rc = dtype == ZS_BF16 ? ns_normalize<__nv_bfloat16>(G, X, ss, batch, m * n, stream)
+                                    : ns_normalize<__half>(G, X, ss, batch, m * n, stream);
     if (rc != ZS_OK) return rc;
   }
-  char* X = reinterpret_cast<char*>(X_out);
-  char* Xn = Xtmp;
   for (int it = 0; it < steps; ++it) {
     CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128;
     int rc;
@@ -1937,7 +1938,5 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     X = Xn;
     Xn = t;
   }
-  if (X != reinterpret_cast<char*>(X_out))
-    ZS_CUDA_TRY(cudaMemcpyAsync(X_out, X, (size_t)batch * m * n * es, cudaMemcpyDeviceToDevice, stream));
   return ZS_OK;
 }

@@ -7,6 +7,7 @@
 #include "zs_norm.cu"
 #include "zs_attn.cu"
 #include "zs_muon.cu"
+#include "zs_adam.cu"
 #include "zs_comm.cu"
 #include "zs_sparse.cu"
 #include "zs_api.cu"

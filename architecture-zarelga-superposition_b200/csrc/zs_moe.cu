@@ -314,6 +314,80 @@ extern "C" int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int6
   return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
 }
 
+namespace zs {
+// The MoE layer's output added into the f32 residual stream in one pass:
+//   out[t] = residual[t] + (f32(shared[t]) + f32(bf16(sum_j w[t, j] * rows[t*k + j])))
+// -- the values of the block's `h + (shared.float() + routed)` with the routed
+// combine rounded to the storage dtype first, as the unfused path computes them.
+// rows / shared in dtype (bf16 or f16), residual / out f32; C % 8 == 0.
+__global__ void moe_combine_kernel(float* __restrict__ out, int64_t o_sm, const char* __restrict__ in, int64_t i_sm,
+                                   const void* w, int w_dtype, int64_t T, int k, int64_t C, int dtype,
+                                   const char* __restrict__ shared, int64_t s_sm, const float* __restrict__ residual,
+                                   int64_t r_sm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+    float wt[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wt[j] = (j < k && w != nullptr) ? load_as_f32(w, t * k + j, w_dtype) : 1.0f;
+    for (int64_t v = lane; v < C / 8; v += 32) {
+      uint4 raw[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(in + ((t * k + j) * i_sm) * 2) + v);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= k) break;
+        float f[8];
+        unpack8(raw[j], dtype, f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt[j], f[q], acc[q]);
+      }
+      float r8[8];
+      unpack8(pack8(acc, dtype), dtype, r8);   // the routed sum in the storage dtype
+      if (shared != nullptr) {
+        float s8[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(shared + (t * s_sm) * 2) + v), dtype, s8);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) r8[q] = s8[q] + r8[q];
+      }
+      float4* o4 = reinterpret_cast<float4*>(out + t * o_sm) + 2 * v;
+      if (residual != nullptr) {
+        const float4* x4 = reinterpret_cast<const float4*>(residual + t * r_sm) + 2 * v;
+        const float4 a = __ldg(x4), b = __ldg(x4 + 1);
+        o4[0] = make_float4(a.x + r8[0], a.y + r8[1], a.z + r8[2], a.w + r8[3]);
+        o4[1] = make_float4(b.x + r8[4], b.y + r8[5], b.z + r8[6], b.w + r8[7]);
+      } else {
+        o4[0] = make_float4(r8[0], r8[1], r8[2], r8[3]);
+        o4[1] = make_float4(r8[4], r8[5], r8[6], r8[7]);
+      }
+    }
+  }
+}
+}  // namespace zs
+
+extern "C" int zs_moe_combine(float* out, int64_t o_sm, const void* rows, int64_t i_sm, const void* weights,
+                              int w_dtype, int64_t T, int k, int64_t C, int dtype, const void* shared, int64_t s_sm,
+                              const float* residual, int64_t r_sm, void* stream) {
+  ZS_REQUIRE(out && rows, ZS_ERR_ARG);
+  ZS_REQUIRE(dtype == ZS_BF16 || dtype == ZS_F16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(T >= 0 && k >= 1 && k <= 8 && C >= 0, ZS_ERR_SHAPE);
+  ZS_REQUIRE(C % 8 == 0 && o_sm % 4 == 0 && i_sm % 8 == 0 && (shared == nullptr || s_sm % 8 == 0) &&
+                 (residual == nullptr || r_sm % 4 == 0) &&
+                 ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(rows) |
+                   reinterpret_cast<uintptr_t>(shared) | reinterpret_cast<uintptr_t>(residual)) % 16 == 0),
+             ZS_ERR_ALIGN);
+  ZS_BIND(rows);
+  if (T == 0 || C == 0) return ZS_OK;
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  zs::moe_combine_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      out, o_sm, reinterpret_cast<const char*>(rows), i_sm, weights, w_dtype, T, k, C, dtype,
+      reinterpret_cast<const char*>(shared), s_sm, residual, r_sm);
+  return cudaGetLastError() == cudaSuccess ? ZS_OK : ZS_ERR_CUDA;
+}
+
 extern "C" int zs_gathered_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, int64_t n_rows,
                                    const int64_t* row_of_slot, int64_t T, int k, int64_t C, int dtype,
                                    void* stream) {

@@ -95,6 +95,32 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, int64_t c, in
   }
 }
 
+// 8 consecutive bf16 of a row as four packed pairs (zeros past n); unpacked by unpack8_bf16
+template <bool VEC>
+__device__ __forceinline__ void load8_bf16_raw(const __nv_bfloat16* p, int64_t c, int64_t n, uint32_t (&r)[4]) {
+  if (VEC) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + c));
+    r[0] = u.x; r[1] = u.y; r[2] = u.z; r[3] = u.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h;
+      h.x = c + 2 * e < n ? p[c + 2 * e] : __float2bfloat16_rn(0.f);
+      h.y = c + 2 * e + 1 < n ? p[c + 2 * e + 1] : __float2bfloat16_rn(0.f);
+      r[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack8_bf16(const uint32_t (&r)[4], float (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[e]));
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+
 template <bool VEC>
 __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, int64_t c, int64_t n, const float (&v)[8]) {
   if (VEC) {
@@ -124,13 +150,130 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 }
 
 // softplus'd gains of the tile into shared memory (1 where a gain is absent)
+// Also the reciprocals s_ri[i] = 1 / (scalar * row gain) and s_ci[j] = 1 / column gain: the
+// passes divide W by the gain product as W * (s_ri * s_ci) (a few ulps from the quotient,
+// and a multiply instead of an IEEE division per element).
 __device__ __forceinline__ float tile_gains(const Gains& g, int64_t l, int64_t m, int64_t n, int64_t r0, int64_t c0,
-                                            float* s_r, float* s_c) {
-  for (int i = threadIdx.x; i < TR; i += THREADS)
-    s_r[i] = (g.row != nullptr && r0 + i < m) ? softplus_f(g.row[l * m + r0 + i]) : 1.f;
-  for (int i = threadIdx.x; i < TC; i += THREADS)
-    s_c[i] = (g.col != nullptr && c0 + i < n) ? softplus_f(g.col[l * n + c0 + i]) : 1.f;
-  return g.sc != nullptr ? softplus_f(g.sc[l]) : 1.f;
+                                            float* s_r, float* s_c, float* s_ri, float* s_ci) {
+  const float sc = g.sc != nullptr ? softplus_f(g.sc[l]) : 1.f;
+  for (int i = threadIdx.x; i < TR; i += THREADS) {
+    const float r = (g.row != nullptr && r0 + i < m) ? softplus_f(g.row[l * m + r0 + i]) : 1.f;
+    s_r[i] = r;
+    s_ri[i] = 1.0f / (sc * r);
+  }
+  for (int i = threadIdx.x; i < TC; i += THREADS) {
+    const float c = (g.col != nullptr && c0 + i < n) ? softplus_f(g.col[l * n + c0 + i]) : 1.f;
+    s_c[i] = c;
+    s_ci[i] = 1.0f / c;
+  }
+  return sc;
+}
+
+// The vectorised post passes stage each thread's eight rows of W (two 16-byte chunks
+// a row) and, in the plain layout, of U (one chunk) into shared memory with
+// cp.async before any arithmetic: all of a block's loads are in flight at once
+// without holding registers (96 KB a block, two blocks an SM).  Chunk j of row k of
+// thread t sits at [(k * NCH + j) * THREADS + t], so a warp's 16-byte reads are
+// contiguous.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+template <bool TRANS>
+struct Stage {
+  static constexpr int NCH = TRANS ? 2 : 3;
+  static constexpr int BYTES = 8 * NCH * THREADS * 16;
+};
+
+template <bool TRANS>
+__device__ __forceinline__ void stage_rows(uint4* st, const float* W, const __nv_bfloat16* U, int64_t l, int64_t m,
+                                           int64_t n, int64_t r0, int64_t c) {
+  constexpr int NCH = Stage<TRANS>::NCH;
+  const int warp = threadIdx.x >> 5, tid = threadIdx.x;
+  if (c >= n) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int64_t row = r0 + warp * 8 + k;
+    if (row >= m) break;
+    const int64_t off = (l * m + row) * n + c;
+    cp_async16(&st[(k * NCH + 0) * THREADS + tid], W + off);
+    cp_async16(&st[(k * NCH + 1) * THREADS + tid], W + off + 4);
+    if constexpr (!TRANS) cp_async16(&st[(k * NCH + 2) * THREADS + tid], U + off);
+  }
+}
+
+__device__ __forceinline__ void staged_w(const uint4* st, int k, int nch, float (&w)[8]) {
+  const int tid = threadIdx.x;
+  const uint4 a = st[(k * nch + 0) * THREADS + tid], b = st[(k * nch + 1) * THREADS + tid];
+  w[0] = __uint_as_float(a.x); w[1] = __uint_as_float(a.y); w[2] = __uint_as_float(a.z); w[3] = __uint_as_float(a.w);
+  w[4] = __uint_as_float(b.x); w[5] = __uint_as_float(b.y); w[6] = __uint_as_float(b.z); w[7] = __uint_as_float(b.w);
+}
+
+// Transposed bf16 layout [L, n, m] of the Newton-Schulz operand of a tall stack (m > n
+// runs as its transpose): a block's 64 x 256 tile is staged in shared memory as 256
+// columns of 32 words (row pairs), the word of row pair q of tile column j stored at
+// q ^ (j / 8 mod 32) -- a thread's eight columns j = lane*8 + e then fall in 32
+// different banks, and a warp moving one column to or from global memory touches each
+// bank once with 128 contiguous bytes.
+constexpr int TW = TR / 2;   // words per staged column
+
+__device__ __forceinline__ int tswz(int j, int q) { return q ^ ((j >> 3) & 31); }
+
+// global [L, n, m] -> staged tile (zeros outside the matrix); whole row pairs are copied
+// with cp.async (the caller waits for them with cp_async_wait_all before its barrier)
+__device__ __forceinline__ void stage_t_load(uint32_t (*s_t)[TW], const __nv_bfloat16* __restrict__ T, int64_t l,
+                                             int64_t m, int64_t n, int64_t r0, int64_t c0, bool words) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = r0 + 2 * lane;
+  for (int j = warp; j < TC; j += THREADS / 32) {
+    const int64_t col = c0 + j;
+    uint32_t* dst = &s_t[j][tswz(j, lane)];
+    const __nv_bfloat16* src = T + (l * n + col) * m + i;
+    if (col < n && words && i + 1 < m) {
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    } else {
+      __nv_bfloat162 h;
+      h.x = (col < n && i < m) ? src[0] : __float2bfloat16_rn(0.f);
+      h.y = (col < n && i + 1 < m) ? src[1] : __float2bfloat16_rn(0.f);
+      *dst = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+}
+
+// staged tile -> global [L, n, m] (only elements inside the matrix)
+__device__ __forceinline__ void stage_t_store(const uint32_t (*s_t)[TW], __nv_bfloat16* __restrict__ T, int64_t l,
+                                              int64_t m, int64_t n, int64_t r0, int64_t c0, bool words) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 4
+  for (int j = warp; j < TC; j += THREADS / 32) {
+    const int64_t col = c0 + j;
+    if (col >= n) continue;
+    const int q = tswz(j, lane);          // this lane's physical word holds logical row pair q
+    const uint32_t v = s_t[j][lane];
+    const int64_t i = r0 + 2 * q;
+    __nv_bfloat16* dst = T + (l * n + col) * m + i;
+    if (words && i + 1 < m) {
+      *reinterpret_cast<uint32_t*>(dst) = v;
+    } else {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&v);
+      if (i < m) dst[0] = h.x;
+      if (i + 1 < m) dst[1] = h.y;
+    }
+  }
+}
+
+// the eight staged values of tile row rr at columns lane*8 .. lane*8+7, as four bf16 pairs
+__device__ __forceinline__ void stage_t_row(const uint32_t (*s_t)[TW], int rr, int lane, uint32_t (&r)[4]) {
+  const int sh = (rr & 1) * 16;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t lo = (s_t[lane * 8 + 2 * e][(rr >> 1) ^ lane] >> sh) & 0xffffu;
+    const uint32_t hi = (s_t[lane * 8 + 2 * e + 1][(rr >> 1) ^ lane] >> sh) & 0xffffu;
+    r[e] = lo | (hi << 16);
+  }
 }
 
 // Pre-Newton-Schulz: buf.lerp_(g*G, 1-mom); X = lerp(g*G, buf, mom) (bf16);
@@ -146,55 +289,87 @@ struct Partials {
   float* s;
 };
 
-template <bool VEC>
-__global__ void __launch_bounds__(THREADS) md_pre_kernel(const float* __restrict__ W, const float* __restrict__ G,
+// TRANS: X is written in the transposed layout [L, n, m] (words: m even and X 4-byte aligned).
+template <bool VEC, bool TRANS>
+__global__ void __launch_bounds__(THREADS, 2) md_pre_kernel(const float* __restrict__ W, const float* __restrict__ G,
                                                          float* __restrict__ buf, Gains gains,
                                                          __nv_bfloat16* __restrict__ X, Partials part, bool want_s,
-                                                         bool want_r, bool want_c, int64_t m, int64_t n, float mom) {
-  __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
+                                                         bool want_r, bool want_c, int64_t m, int64_t n, float mom,
+                                                         bool words) {
+  __shared__ float s_r[TR], s_c[TC], s_ri[TR], s_ci[TC], s_col[THREADS / 32][TC], sh[32];
+  __shared__ uint32_t s_t[TRANS ? TC : 1][TW];
   const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
-  const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c);
+  const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c, s_ri, s_ci);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool have_g = gains.sc != nullptr || gains.row != nullptr || gains.col != nullptr;
   const int64_t c = c0 + lane * 8;
   float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float sacc = 0.f;
-#pragma unroll 2
-  for (int k = 0; k < 8; ++k) {
-    const int rr = warp * 8 + k;
-    const int64_t row = r0 + rr;
-    if (row >= m) continue;
-    float racc = 0.f;
-    if (c < n) {
-      const int64_t off = (l * m + row) * n;
-      float w[8], gr[8], b[8], x[8];
-      load8<VEC>(W + off, c, n, w);
-      load8<VEC>(G + off, c, n, gr);
-      load8_mut<VEC>(buf + off, c, n, b);
+  // four batches of two rows: each batch's six 32-byte loads are issued before its
+  // arithmetic and stores (buf is read and written in place, so the compiler keeps the
+  // loads of a later row behind an earlier row's stores)
+#pragma unroll 1
+  for (int kb = 0; kb < 8; kb += 2) {
+    float w[2][8], gr[2][8], b[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int64_t row = r0 + warp * 8 + kb + k;
+      if (row < m && c < n) {
+        const int64_t off = (l * m + row) * n;
+        load8<VEC>(W + off, c, n, w[k]);
+        load8<VEC>(G + off, c, n, gr[k]);
+        load8_mut<VEC>(buf + off, c, n, b[k]);
+      }
+    }
+    float x[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int rr = warp * 8 + kb + k;
+      const int64_t row = r0 + rr;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[k][e] = 0.f;
+      if (row >= m) continue;
+      float racc = 0.f;
+      if (c < n) {
+        const int64_t off = (l * m + row) * n;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float cg = s_c[lane * 8 + e];
+          float gh = gr[k][e];
+          if (have_g) {
+            const float gv = (sc * s_r[rr]) * cg;
+            const float wg = (w[k][e] * (s_ri[rr] * s_ci[lane * 8 + e])) * gr[k][e];
+            gh = gv * gr[k][e];
+            racc += wg * (cg * sc);
+            colacc[e] += wg * (s_r[rr] * sc);
+            sacc += wg * (s_r[rr] * cg);
+          }
+          b[k][e] = lerp_f(b[k][e], gh, 1.f - mom);
+          x[k][e] = lerp_f(gh, b[k][e], mom);
+        }
+        store8<VEC>(buf + off, c, n, b[k]);
+        if constexpr (!TRANS) store8_bf16<VEC>(X + off, c, n, x[k]);
+      }
+      if (want_r) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+        if (lane == 0) part.r[(l * m + row) * gridDim.x + blockIdx.x] = racc;
+      }
+    }
+    if constexpr (TRANS) {
+      // rows kb, kb+1 of this warp form row pair (warp*8 + kb) / 2 of every column
+      const int q = (warp * 8 + kb) >> 1;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float cg = s_c[lane * 8 + e];
-        float gh = gr[e];
-        if (have_g) {
-          const float gv = (sc * s_r[rr]) * cg;
-          const float wg = (w[e] / gv) * gr[e];
-          gh = gv * gr[e];
-          racc += wg * (cg * sc);
-          colacc[e] += wg * (s_r[rr] * sc);
-          sacc += wg * (s_r[rr] * cg);
-        }
-        b[e] = lerp_f(b[e], gh, 1.f - mom);
-        x[e] = lerp_f(gh, b[e], mom);
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[0][e], x[1][e]);
+        s_t[lane * 8 + e][q ^ lane] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      store8<VEC>(buf + off, c, n, b);
-      store8_bf16<VEC>(X + off, c, n, x);
     }
-    if (want_r) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-      if (lane == 0) part.r[(l * m + row) * gridDim.x + blockIdx.x] = racc;
-    }
+  }
+  if constexpr (TRANS) {
+    __syncthreads();
+    stage_t_store(s_t, X, l, m, n, r0, c0, words);
   }
   if (want_c) {
 #pragma unroll
@@ -231,46 +406,65 @@ struct PostArgs {
   float lr_host;
   float rescale;
   int norm_axis;          // 0 frobenius, 1 row, 2 column
+  bool u_words;           // transposed U: m even and U 4-byte aligned (32-bit row-pair accesses)
 };
 
 __device__ __forceinline__ float lr_of(const PostArgs& a) { return a.lr_dev != nullptr ? __ldg(a.lr_dev) : a.lr_host; }
 
 // sum of squares of W_hat' = W/g - lr * (rescale * U) per matrix / row / column
-template <bool VEC>
-__global__ void __launch_bounds__(THREADS) md_reduce_kernel(PostArgs a, Gains gains, Partials part) {
-  __shared__ float s_r[TR], s_c[TC], s_col[THREADS / 32][TC], sh[32];
+// (TRANS: U in the transposed layout [L, n, m])
+template <bool VEC, bool TRANS>
+__global__ void __launch_bounds__(THREADS, 2) md_reduce_kernel(PostArgs a, Gains gains, Partials part) {
+  __shared__ float s_r[TR], s_c[TC], s_ri[TR], s_ci[TC], s_col[THREADS / 32][TC], sh[32];
+  __shared__ uint32_t s_t[TRANS ? TC : 1][TW];
+  extern __shared__ __align__(16) uint8_t md_dyn[];
+  uint4* st = reinterpret_cast<uint4*>(md_dyn);
   const int64_t m = a.m, n = a.n;
   const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
-  const float sc = tile_gains(gains, l, m, n, r0, c0, s_r, s_c);
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float lr = lr_of(a);
   const int64_t c = c0 + lane * 8;
+  if constexpr (VEC) stage_rows<TRANS>(st, a.W, a.U, l, m, n, r0, c);
+  tile_gains(gains, l, m, n, r0, c0, s_r, s_c, s_ri, s_ci);
+  if constexpr (TRANS) stage_t_load(s_t, a.U, l, m, n, r0, c0, a.u_words);
+  if constexpr (VEC || TRANS) cp_async_wait_all();
+  __syncthreads();
+  const float lrr = lr_of(a) * a.rescale;
   float colacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float facc = 0.f;
-#pragma unroll
+#pragma unroll 2
   for (int k = 0; k < 8; ++k) {
     const int rr = warp * 8 + k;
     const int64_t row = r0 + rr;
-    if (row >= m) continue;   // warp-uniform; unrolled so the rows' loads overlap
-    float racc = 0.f;
-    if (c < n) {
-      const int64_t off = (l * m + row) * n;
-      float w[8], u[8];
-      load8<VEC>(a.W + off, c, n, w);
-      load8_bf16<VEC>(a.U + off, c, n, u);
+    // rows past m and columns past n read as zeros and add nothing
+    float w[8], u[8];
+    uint32_t ur[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (c + e >= n) continue;
-        const float gv = (sc * s_r[rr]) * s_c[lane * 8 + e];
-        const float wh = w[e] / gv - lr * (u[e] * a.rescale);
-        const float q = wh * wh;
-        racc += q;
-        colacc[e] += q;
-        facc += q;
+    for (int e = 0; e < 8; ++e) w[e] = 0.f;
+    if (row < m && c < n) {
+      if constexpr (VEC) {
+        staged_w(st, k, Stage<TRANS>::NCH, w);
+        if constexpr (!TRANS) {
+          const uint4 q4 = st[(k * 3 + 2) * THREADS + threadIdx.x];
+          ur[0] = q4.x; ur[1] = q4.y; ur[2] = q4.z; ur[3] = q4.w;
+        }
+      } else {
+        load8<VEC>(a.W + (l * m + row) * n, c, n, w);
+        if constexpr (!TRANS) load8_bf16_raw<VEC>(a.U + (l * m + row) * n, c, n, ur);
       }
+      if constexpr (TRANS) stage_t_row(s_t, rr, lane, ur);
     }
-    if (a.norm_axis == 1) {
+    unpack8_bf16(ur, u);
+    float racc = 0.f;
+    const float ri = s_ri[rr];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float wh = w[e] * (ri * s_ci[lane * 8 + e]) - lrr * u[e];
+      const float q = wh * wh;
+      racc += q;
+      colacc[e] += q;
+      facc += q;
+    }
+    if (a.norm_axis == 1 && row < m) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
       if (lane == 0) part.r[(l * m + row) * gridDim.x + blockIdx.x] = racc;
@@ -339,48 +533,87 @@ struct WriteArgs {
   const float* proj;
 };
 
-template <bool VEC, typename TP>
-__global__ void __launch_bounds__(THREADS) md_write_kernel(PostArgs a, WriteArgs wa, TP* __restrict__ p) {
-  __shared__ float s_ro[TR], s_rn[TR], s_co[TC], s_cn[TC];
+template <bool VEC, bool TRANS, typename TP>
+__global__ void __launch_bounds__(THREADS, 2) md_write_kernel(PostArgs a, WriteArgs wa, TP* __restrict__ p) {
+  // s_roi / s_coi: reciprocal old gains (row factor with the scalar folded in);
+  // s_rf / s_cf: new gains times the projection factor of the tile's rows / columns
+  __shared__ float s_roi[TR], s_rf[TR], s_coi[TC], s_cf[TC];
+  __shared__ uint32_t s_t[TRANS ? TC : 1][TW];
+  extern __shared__ __align__(16) uint8_t md_dyn[];
+  uint4* st = reinterpret_cast<uint4*>(md_dyn);
   const int64_t m = a.m, n = a.n;
   const int64_t l = blockIdx.z, r0 = (int64_t)blockIdx.y * TR, c0 = (int64_t)blockIdx.x * TC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = c0 + lane * 8;
+  // p may be W itself (the f32 parameter updated in place): every read of W is staged
+  // (or, unvectorised, loaded into registers) before the thread's first store
+  if constexpr (VEC) stage_rows<TRANS>(st, a.W, a.U, l, m, n, r0, c);
+  const float so = wa.sp_old[0] != nullptr ? wa.sp_old[0][l] : 1.f;
+  const float sn = wa.sp_new[0] != nullptr ? wa.sp_new[0][l] : 1.f;
+  const float pf = a.norm_axis == 0 ? wa.proj[l] : 1.f;
   for (int i = threadIdx.x; i < TR; i += THREADS) {
     const bool ok = wa.sp_old[1] != nullptr && r0 + i < m;
-    s_ro[i] = ok ? wa.sp_old[1][l * m + r0 + i] : 1.f;
-    s_rn[i] = ok ? wa.sp_new[1][l * m + r0 + i] : 1.f;
+    const float ro = ok ? wa.sp_old[1][l * m + r0 + i] : 1.f;
+    const float rn = ok ? wa.sp_new[1][l * m + r0 + i] : 1.f;
+    const float pr = a.norm_axis == 1 ? (r0 + i < m ? wa.proj[l * m + r0 + i] : 1.f) : pf;
+    s_roi[i] = 1.0f / (so * ro);
+    s_rf[i] = (sn * rn) * pr;
   }
   for (int i = threadIdx.x; i < TC; i += THREADS) {
     const bool ok = wa.sp_old[2] != nullptr && c0 + i < n;
-    s_co[i] = ok ? wa.sp_old[2][l * n + c0 + i] : 1.f;
-    s_cn[i] = ok ? wa.sp_new[2][l * n + c0 + i] : 1.f;
+    const float co = ok ? wa.sp_old[2][l * n + c0 + i] : 1.f;
+    const float cn = ok ? wa.sp_new[2][l * n + c0 + i] : 1.f;
+    const float pc = a.norm_axis == 2 && c0 + i < n ? wa.proj[l * n + c0 + i] : 1.f;
+    s_coi[i] = 1.0f / co;
+    s_cf[i] = cn * pc;
   }
-  const float so = wa.sp_old[0] != nullptr ? wa.sp_old[0][l] : 1.f;
-  const float sn = wa.sp_new[0] != nullptr ? wa.sp_new[0][l] : 1.f;
+  if constexpr (TRANS) stage_t_load(s_t, a.U, l, m, n, r0, c0, a.u_words);
+  if constexpr (VEC || TRANS) cp_async_wait_all();
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float lr = lr_of(a);
-  const int64_t c = c0 + lane * 8;
+  const float lrr = lr_of(a) * a.rescale;
   if (c >= n) return;
-  const float pf = a.norm_axis == 0 ? wa.proj[l] : 1.f;
-  float pc[8];
+  float wr[VEC ? 1 : 8][8];
+  uint32_t urr[VEC ? 1 : 8][4];
+  if constexpr (!VEC) {
 #pragma unroll
-  for (int e = 0; e < 8; ++e) pc[e] = (a.norm_axis == 2 && c + e < n) ? wa.proj[l * n + c + e] : 1.f;
-#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t row = r0 + warp * 8 + k;
+      if (row < m) {
+        load8<VEC>(a.W + (l * m + row) * n, c, n, wr[k]);
+        if constexpr (!TRANS) load8_bf16_raw<VEC>(a.U + (l * m + row) * n, c, n, urr[k]);
+      }
+    }
+  }
+#pragma unroll 2
   for (int k = 0; k < 8; ++k) {
     const int rr = warp * 8 + k;
     const int64_t row = r0 + rr;
-    if (row >= m) continue;
-    const float pr = a.norm_axis == 1 ? wa.proj[l * m + row] : pf;
+    if (row >= m) break;
     const int64_t off = (l * m + row) * n;
     float w[8], u[8], o[8];
-    load8<VEC>(a.W + off, c, n, w);
-    load8_bf16<VEC>(a.U + off, c, n, u);
+    uint32_t ur[4];
+    if constexpr (VEC) {
+      staged_w(st, k, Stage<TRANS>::NCH, w);
+      if constexpr (!TRANS) {
+        const uint4 q4 = st[(k * 3 + 2) * THREADS + threadIdx.x];
+        ur[0] = q4.x; ur[1] = q4.y; ur[2] = q4.z; ur[3] = q4.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = wr[k][e];
+      if constexpr (!TRANS) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ur[e] = urr[k][e];
+      }
+    }
+    if constexpr (TRANS) stage_t_row(s_t, rr, lane, ur);
+    unpack8_bf16(ur, u);
+    const float roi = s_roi[rr], rf = s_rf[rr];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float go = (so * s_ro[rr]) * s_co[lane * 8 + e];
-      const float gn = (sn * s_rn[rr]) * s_cn[lane * 8 + e];
-      const float wh = (w[e] / go - lr * (u[e] * a.rescale)) * (a.norm_axis == 2 ? pc[e] : pr);
-      o[e] = gn * wh;
+      // new gain * projected (W / old gain - lr * rescale * U)
+      const float wh = w[e] * (roi * s_coi[lane * 8 + e]) - lrr * u[e];
+      o[e] = wh * (rf * s_cf[lane * 8 + e]);
     }
     if constexpr (std::is_same<TP, float>::value) {
       store8<VEC>(p + off, c, n, o);
@@ -437,7 +670,8 @@ extern "C" size_t zs_muonmd_pre_workspace(int64_t L, int64_t m, int64_t n) {
 }
 
 extern "C" int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
-                             const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col,
+                             const float* g_col, void* x_out, int x_transposed, float* red_scalar, float* red_row,
+                             float* red_col,
                              int64_t L, int64_t m, int64_t n, float momentum, void* workspace,
                              size_t workspace_bytes, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -456,10 +690,16 @@ extern "C" int zs_muonmd_pre(const float* W, const float* G, float* buf, const f
                       : nullptr;
   const md::Partials part = any_red ? md_partials(ws, L, m, n) : md::Partials{nullptr, nullptr, nullptr};
   const bool ws_ = red_scalar != nullptr, wr = red_row != nullptr, wc = red_col != nullptr;
-  if (md_vec_ok(n, {W, G, buf, x_out}))
-    md::md_pre_kernel<true><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, part, ws_, wr, wc, m, n, momentum);
-  else
-    md::md_pre_kernel<false><<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, part, ws_, wr, wc, m, n, momentum);
+  const bool words = m % 2 == 0 && (reinterpret_cast<uintptr_t>(x_out) & 3) == 0;
+  const bool vec = x_transposed ? md_vec_ok(n, {W, G, buf}) : md_vec_ok(n, {W, G, buf, x_out});
+  auto launch = [&](auto kern) {
+    kern<<<grid, md::THREADS, 0, stream>>>(W, G, buf, g, X, part, ws_, wr, wc, m, n, momentum, words);
+  };
+  if (x_transposed) {
+    if (vec) launch(md::md_pre_kernel<true, true>); else launch(md::md_pre_kernel<false, true>);
+  } else {
+    if (vec) launch(md::md_pre_kernel<true, false>); else launch(md::md_pre_kernel<false, false>);
+  }
   ZS_CUDA_TRY(cudaGetLastError());
   int rc;
   if (ws_ && (rc = md_finish(part, 0, red_scalar, L, m, n, stream)) != ZS_OK) return rc;
@@ -475,7 +715,7 @@ extern "C" size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n) {
   return (size_t)(2 * L * mx + 2 * (L + L * m + L * n) + md_partial_floats(L, m, n)) * sizeof(float) + 8 * 256;
 }
 
-extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
+extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype, float* g_scalar, float* g_row,
                               float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
                               float* m1_col, float* m2_col, const float* red_scalar, const float* red_row,
                               const float* red_col, const float* step_dev, float step_host, float b1, float b2,
@@ -502,14 +742,25 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_
   float* sp_old[3] = {sp, sp + L, sp + L + L * m};
   float* sp_new[3] = {sp_old[2] + L * n, sp_old[2] + L * n + L, sp_old[2] + L * n + L + L * m};
   const md::Partials part = md_partials(sp_new[2] + L * n, L, m, n);
-  md::PostArgs a{W, reinterpret_cast<const __nv_bfloat16*>(U), m, n, lr_dev, lr_host, rescale, norm_axis};
+  md::PostArgs a{W, reinterpret_cast<const __nv_bfloat16*>(U), m, n, lr_dev, lr_host, rescale, norm_axis,
+                 m % 2 == 0 && (reinterpret_cast<uintptr_t>(U) & 3) == 0};
   md::Gains g{g_scalar, g_row, g_col};
   const dim3 grid = md_grid(L, m, n);
-  const bool vec = md_vec_ok(n, {W, U, p_out});
-  if (vec)
-    md::md_reduce_kernel<true><<<grid, md::THREADS, 0, stream>>>(a, g, part);
+  const bool vec = u_transposed ? md_vec_ok(n, {W, p_out}) : md_vec_ok(n, {W, U, p_out});
+  // the vectorised passes stage their rows in dynamic shared memory (md::Stage)
+  auto reduce = [&](auto kern, int dyn) -> int {
+    if (dyn > 0) ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    kern<<<grid, md::THREADS, dyn, stream>>>(a, g, part);
+    return ZS_OK;
+  };
+  int rc0;
+  if (u_transposed)
+    rc0 = vec ? reduce(md::md_reduce_kernel<true, true>, md::Stage<true>::BYTES)
+              : reduce(md::md_reduce_kernel<false, true>, 0);
   else
-    md::md_reduce_kernel<false><<<grid, md::THREADS, 0, stream>>>(a, g, part);
+    rc0 = vec ? reduce(md::md_reduce_kernel<true, false>, md::Stage<false>::BYTES)
+              : reduce(md::md_reduce_kernel<false, false>, 0);
+  if (rc0 != ZS_OK) return rc0;
   ZS_CUDA_TRY(cudaGetLastError());
   {
     const int rc = md_finish(part, norm_axis, ss, L, m, n, stream);
@@ -549,19 +800,22 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_
   if (blocks > 148 * 4) blocks = 148 * 4;
   md::md_gain_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ga);
   ZS_CUDA_TRY(cudaGetLastError());
-  if (p_dtype == ZS_F32) {
-    if (vec)
-      md::md_write_kernel<true, float><<<grid, md::THREADS, 0, stream>>>(a, wa, reinterpret_cast<float*>(p_out));
-    else
-      md::md_write_kernel<false, float><<<grid, md::THREADS, 0, stream>>>(a, wa, reinterpret_cast<float*>(p_out));
-  } else {
-    if (vec)
-      md::md_write_kernel<true, __nv_bfloat16><<<grid, md::THREADS, 0, stream>>>(
-          a, wa, reinterpret_cast<__nv_bfloat16*>(p_out));
-    else
-      md::md_write_kernel<false, __nv_bfloat16><<<grid, md::THREADS, 0, stream>>>(
-          a, wa, reinterpret_cast<__nv_bfloat16*>(p_out));
-  }
+  auto launch_write = [&](auto kern, int dyn, auto* out_typed) -> int {
+    if (dyn > 0) ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    kern<<<grid, md::THREADS, dyn, stream>>>(a, wa, out_typed);
+    return ZS_OK;
+  };
+  auto write = [&](auto* out_typed) -> int {
+    using TP = std::remove_pointer_t<decltype(out_typed)>;
+    if (u_transposed)
+      return vec ? launch_write(md::md_write_kernel<true, true, TP>, md::Stage<true>::BYTES, out_typed)
+                 : launch_write(md::md_write_kernel<false, true, TP>, 0, out_typed);
+    return vec ? launch_write(md::md_write_kernel<true, false, TP>, md::Stage<false>::BYTES, out_typed)
+               : launch_write(md::md_write_kernel<false, false, TP>, 0, out_typed);
+  };
+  const int rc1 = p_dtype == ZS_F32 ? write(reinterpret_cast<float*>(p_out))
+                                    : write(reinterpret_cast<__nv_bfloat16*>(p_out));
+  if (rc1 != ZS_OK) return rc1;
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
 }

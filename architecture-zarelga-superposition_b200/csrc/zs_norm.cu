@@ -594,3 +594,255 @@ extern "C" int zs_rope(void* q, int64_t q_row_stride, void* k, int64_t k_row_str
                          seq_len, cos_batch, n_q_heads, n_kv_heads, head_dim, head_dim / 2, dtype, table_dtype,
                          backward, stream);
 }
+
+// ------------------------------------------------------------- q/k norm + RoPE
+//
+// GatedAttention's per-head QK normalisation followed by its partial position
+// RoPE (modeling/attention.py:140-150 with modeling/zRMSNorm.py:4-20 and the
+// rotate-half RoPE of modeling/liger_rope.py), fused: one warp per (token,
+// head) row of hd values, lane l holding the E = hd/32 consecutive values
+// [l*E, l*E + E).  The pair partner of value c (c + hd/2, or c - hd/2) sits in
+// lane l ^ 16, one shuffle away.  Rows are the q heads then the k heads of a
+// token, read from the leading (Hq + Hk) * hd columns of x (the fused q/k/v/gate
+// projection, row stride ldx) and written in the same order to y.  The
+// normalised value is rotated in f32 and rounded to bf16 once.
+namespace zs {
+namespace qkn {
+
+struct Args {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const float* wq;
+  const float* wk;
+  const void* cos;
+  const void* sin;
+  int table_f32;
+  int64_t cos_row_stride;
+  int cos_bs;
+  int rot;
+  int64_t tokens;
+  int seq_len, Hq, Hk;
+  float eps;
+};
+
+template <int E>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[E]) {
+  if constexpr (E == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  } else {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    v[0] = a.x; v[1] = a.y;
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[E]) {
+  if constexpr (E == 4) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  } else {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+  }
+}
+
+__device__ __forceinline__ float table_at(const Args& a, const void* t, int64_t i) {
+  return a.table_f32 ? __ldg(reinterpret_cast<const float*>(t) + i)
+                     : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(t)[i]);
+}
+
+// rotate the row's values in place: forward (sign +1) x1' = x1 c - x2 s, x2' = x2 c + x1 s;
+// backward (sign -1) the transpose.  Lanes below 16 hold the first half of the row.
+template <int E>
+__device__ __forceinline__ void rotate(const Args& a, int64_t tok, float (&v)[E], float sign) {
+  const int lane = threadIdx.x & 31;
+  float pv[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, v[e], 16);
+  const int p0 = (lane & 15) * E;   // pair index of this lane's first value
+  if (p0 >= a.rot) return;
+  const int64_t b = tok / a.seq_len, s = tok - b * a.seq_len;
+  const int64_t crow = (a.cos_bs == 1 ? s : b * a.seq_len + s) * a.cos_row_stride;
+  const bool low = lane < 16;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int p = p0 + e;
+    if (p >= a.rot) break;
+    const float c = table_at(a, a.cos, crow + p), sn = sign * table_at(a, a.sin, crow + p);
+    v[e] = low ? v[e] * c - pv[e] * sn : v[e] * c + pv[e] * sn;
+  }
+}
+
+template <int E>
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(Args a, __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                               float* __restrict__ rstd) {
+  constexpr int HD = 32 * E;
+  const int lane = threadIdx.x & 31;
+  const int heads = a.Hq + a.Hk;
+  const int64_t rows = a.tokens * heads;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const int64_t tok = r / heads;
+    const int hh = (int)(r - tok * heads);
+    const float* w = hh < a.Hq ? a.wq : a.wk;
+    float v[E];
+    load_row<E>(a.x + tok * a.ldx + (int64_t)hh * HD + lane * E, v);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float rs = rsqrtf(ss / (float)HD + a.eps);
+    if (lane == 0) rstd[r] = rs;
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = (v[e] * rs) * (1.0f + __ldg(w + lane * E + e));
+    rotate<E>(a, tok, v, 1.f);
+    store_row<E>(y + tok * ldy + (int64_t)hh * HD + lane * E, v);
+  }
+}
+
+// g = the RoPE transpose of dy; dx = rs * (g (1 + w) - n * mean(g (1 + w) n)), n = x rs;
+// dw partial sums (q rows and k rows apart) per block, reduced in a fixed order afterwards.
+template <int E>
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(Args a, const __nv_bfloat16* __restrict__ dy,
+                                                               int64_t lddy, const float* __restrict__ rstd,
+                                                               __nv_bfloat16* __restrict__ dx, int64_t lddx,
+                                                               float* __restrict__ part) {
+  constexpr int HD = 32 * E;
+  __shared__ float s_acc[8][2][HD];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int heads = a.Hq + a.Hk;
+  const int64_t rows = a.tokens * heads;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  float accq[E], acck[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) accq[e] = acck[e] = 0.f;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; r < rows; r += warps) {
+    const int64_t tok = r / heads;
+    const int hh = (int)(r - tok * heads);
+    const bool isq = hh < a.Hq;
+    const float* w = isq ? a.wq : a.wk;
+    float g[E], xv[E];
+    load_row<E>(dy + tok * lddy + (int64_t)hh * HD + lane * E, g);
+    load_row<E>(a.x + tok * a.ldx + (int64_t)hh * HD + lane * E, xv);
+    rotate<E>(a, tok, g, -1.f);
+    const float rs = __ldg(rstd + r);
+    float dot = 0.f, dn[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float n = xv[e] * rs;
+      dn[e] = g[e] * (1.0f + __ldg(w + lane * E + e));
+      dot = fmaf(dn[e], n, dot);
+      if (isq) accq[e] = fmaf(g[e], n, accq[e]); else acck[e] = fmaf(g[e], n, acck[e]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / (float)HD;
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = rs * (dn[e] - xv[e] * rs * mean);
+    store_row<E>(dx + tok * lddx + (int64_t)hh * HD + lane * E, o);
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    s_acc[warp][0][lane * E + e] = accq[e];
+    s_acc[warp][1][lane * E + e] = acck[e];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t += s_acc[q][i / HD][i % HD];
+    part[(int64_t)blockIdx.x * 2 * HD + i] = t;
+  }
+}
+
+__global__ void qk_norm_dw_finish_kernel(const float* __restrict__ part, int blocks, int hd, float* __restrict__ dwq,
+                                         float* __restrict__ dwk) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 2 * hd) return;
+  float t = 0.f;
+  for (int b = 0; b < blocks; ++b) t += part[(int64_t)b * 2 * hd + i];
+  if (i < hd) dwq[i] = t; else dwk[i - hd] = t;
+}
+
+constexpr int BWD_BLOCKS = 148 * 4;
+
+}  // namespace qkn
+}  // namespace zs
+
+static int qkn_args(zs::qkn::Args& a, const void* x, int64_t ldx, const float* wq, const float* wk, const void* cos,
+                    const void* sin, int table_dtype, int64_t cos_row_stride, int cos_bs, int rot, int64_t tokens,
+                    int seq_len, int Hq, int Hk, int hd, float eps) {
+  ZS_REQUIRE(x && wq && wk, ZS_ERR_ARG);
+  ZS_REQUIRE(hd == 64 || hd == 128, ZS_ERR_SHAPE);
+  ZS_REQUIRE(tokens >= 1 && seq_len >= 1 && tokens % seq_len == 0 && Hq >= 1 && Hk >= 1, ZS_ERR_SHAPE);
+  ZS_REQUIRE(rot >= 0 && rot <= hd / 2 && (rot == 0 || (cos && sin && cos_bs >= 1)), ZS_ERR_ARG);
+  ZS_REQUIRE(table_dtype == ZS_F32 || table_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(ldx >= (int64_t)(Hq + Hk) * hd && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0,
+             ZS_ERR_ALIGN);
+  a = zs::qkn::Args{reinterpret_cast<const __nv_bfloat16*>(x), ldx, wq, wk, cos, sin, table_dtype == ZS_F32,
+                    cos_row_stride, cos_bs, rot, tokens, seq_len, Hq, Hk, eps};
+  return ZS_OK;
+}
+
+extern "C" int zs_qk_norm_rope_forward(const void* x, int64_t ldx, const float* wq, const float* wk, const void* cos,
+                                       const void* sin, int table_dtype, int64_t cos_row_stride, int cos_bs, int rot,
+                                       void* y, int64_t ldy, float* rstd, int64_t tokens, int seq_len, int Hq, int Hk,
+                                       int hd, float eps, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  zs::qkn::Args a;
+  int rc = qkn_args(a, x, ldx, wq, wk, cos, sin, table_dtype, cos_row_stride, cos_bs, rot, tokens, seq_len, Hq, Hk,
+                    hd, eps);
+  if (rc != ZS_OK) return rc;
+  ZS_REQUIRE(y && rstd, ZS_ERR_ARG);
+  ZS_REQUIRE(ldy >= (int64_t)(Hq + Hk) * hd && ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0,
+             ZS_ERR_ALIGN);
+  ZS_BIND(x);
+  const int64_t rows = tokens * (Hq + Hk);
+  int64_t blocks = (rows + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  auto* yo = reinterpret_cast<__nv_bfloat16*>(y);
+  if (hd == 128)
+    zs::qkn::qk_norm_rope_fwd_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(a, yo, ldy, rstd);
+  else
+    zs::qkn::qk_norm_rope_fwd_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(a, yo, ldy, rstd);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}
+
+extern "C" size_t zs_qk_norm_rope_backward_workspace(int hd) {
+  return (size_t)zs::qkn::BWD_BLOCKS * 2 * hd * sizeof(float) + 256;
+}
+
+extern "C" int zs_qk_norm_rope_backward(const void* dy, int64_t lddy, const void* x, int64_t ldx, const float* wq,
+                                        const float* wk, const void* cos, const void* sin, int table_dtype,
+                                        int64_t cos_row_stride, int cos_bs, int rot, const float* rstd, void* dx,
+                                        int64_t lddx, float* dwq, float* dwk, int64_t tokens, int seq_len, int Hq,
+                                        int Hk, int hd, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  zs::qkn::Args a;
+  int rc = qkn_args(a, x, ldx, wq, wk, cos, sin, table_dtype, cos_row_stride, cos_bs, rot, tokens, seq_len, Hq, Hk,
+                    hd, 0.f);
+  if (rc != ZS_OK) return rc;
+  ZS_REQUIRE(dy && rstd && dx && dwq && dwk, ZS_ERR_ARG);
+  ZS_REQUIRE(lddy >= (int64_t)(Hq + Hk) * hd && lddy % 4 == 0 && (reinterpret_cast<uintptr_t>(dy) & 7) == 0 &&
+                 lddx >= (int64_t)(Hq + Hk) * hd && lddx % 4 == 0 && (reinterpret_cast<uintptr_t>(dx) & 7) == 0,
+             ZS_ERR_ALIGN);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_qk_norm_rope_backward_workspace(hd), ZS_ERR_WORKSPACE);
+  ZS_BIND(x);
+  float* part = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  const int blocks = zs::qkn::BWD_BLOCKS;
+  const auto* dyi = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto* dxo = reinterpret_cast<__nv_bfloat16*>(dx);
+  if (hd == 128)
+    zs::qkn::qk_norm_rope_bwd_kernel<4><<<blocks, 256, 0, stream>>>(a, dyi, lddy, rstd, dxo, lddx, part);
+  else
+    zs::qkn::qk_norm_rope_bwd_kernel<2><<<blocks, 256, 0, stream>>>(a, dyi, lddy, rstd, dxo, lddx, part);
+  ZS_CUDA_TRY(cudaGetLastError());
+  zs::qkn::qk_norm_dw_finish_kernel<<<(2 * hd + 127) / 128, 128, 0, stream>>>(part, blocks, hd, dwq, dwk);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}

@@ -7,8 +7,11 @@ per head (the key-sink of modeling/hca.py:138-144, value 0) is off by default
 so the state dict matches the reference's.
 
 Everything runs in libzs.so: the q/k/v/head-gate projections as one grouped-GEMM
-product over the concatenated weights, QK-norm, RoPE, the attention core
-(tcgen05 flash attention, forward and backward) and the output projection.
+product over the concatenated weights; then, on the fused path, one kernel for the
+QK-norm + RoPE of q and k and the tcgen05 flash attention reading v and the gate
+logits in place from the projection output, with the sigmoid gate applied in its
+epilogue (backward: the attention kernels and the norm/RoPE transpose write the
+projection output's gradient directly); and the output projection.
 """
 from __future__ import annotations
 
@@ -19,6 +22,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from zs_b200.attn import attention as attention_core
+from zs_b200.attn import gated_attention_core
 from zs_b200.dense import dense_linear
 
 from .liger_rope import LigerRopeFunction, PartialRopeFunction  # noqa: F401
@@ -98,10 +102,19 @@ class GatedAttention(nn.Module):
         sin_table[:, : self.pos_rope_pairs] = freqs.sin().to(dtype)
         return cos_table, sin_table
 
+    # q/k norm + RoPE + attention + output gate as one autograd function over the fused
+    # projection output (zs_b200.attn.gated_attention_core); off: the step-by-step path
+    fused_core = True
+
+    def _fused_core_ok(self, qkvg):
+        return (self.fused_core and qkvg.dtype == torch.bfloat16 and qkvg.is_contiguous() and self.use_qk_norm
+                and isinstance(self.q_norm, ZeroCenteredRMSNorm) and isinstance(self.k_norm, ZeroCenteredRMSNorm)
+                and self.q_norm.weight.dtype == torch.float32 and self.k_norm.weight.dtype == torch.float32
+                and self.q_norm.eps == self.k_norm.eps and self.head_dim in (64, 128)
+                and qkvg.shape[-1] % 8 == 0)
+
     def forward(self, hidden_states, position_ids=None, cu_seqlens=None, max_seqlen=None, unpad_indices=None):
         bsz, seq_len, _ = hidden_states.shape
-        if self.do_rope and position_ids is None:
-            position_ids = torch.arange(seq_len, device=hidden_states.device).expand(bsz, seq_len)
         # q, k, v and the head gate read the same input: one GEMM over the
         # concatenated weights (the input is cast once, and its gradient is one
         # f32-accumulated product instead of a sum of four).  Zero rows pad the
@@ -112,6 +125,27 @@ class GatedAttention(nn.Module):
         pad = -n_out % 16
         ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.head_gate_proj.weight]
         qkvg = dense_linear(hidden_states, ws, tag="proj_qkvg", pad=pad)
+        seq_ids = None
+        if cu_seqlens is not None:
+            seq_ids = _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len)
+        if self._fused_core_ok(qkvg):
+            # q/k norm + RoPE, attention and the output gate straight from the projection output
+            rp = self.pos_rope_pairs if self.do_rope else 0
+            cos = sin = None
+            if rp:
+                if position_ids is None:
+                    cos = self.pos_cos_cache[:seq_len, :rp].unsqueeze(0)
+                    sin = self.pos_sin_cache[:seq_len, :rp].unsqueeze(0)
+                else:
+                    cos = self.pos_cos_cache[:, :rp][position_ids]
+                    sin = self.pos_sin_cache[:, :rp][position_ids]
+            attn = gated_attention_core(qkvg, self.q_norm.weight, self.k_norm.weight, n_heads=self.num_heads,
+                                        n_kv_heads=self.num_key_value_heads, head_dim=self.head_dim, cos=cos, sin=sin,
+                                        rot_pairs=rp, eps=self.q_norm.eps, window=self.window_size, seq_ids=seq_ids,
+                                        k_sink=self.k_sink, pad=pad)
+            return dense_linear(attn, [self.o_proj.weight], tag="proj_o")
+        if self.do_rope and position_ids is None:
+            position_ids = torch.arange(seq_len, device=hidden_states.device).expand(bsz, seq_len)
         q, k, v, gate_logits = torch.split(qkvg, [qd, kd, kd, self.num_heads + pad], dim=-1)
         gate_logits = gate_logits[..., : self.num_heads]
         q = q.reshape(bsz, seq_len, self.num_heads, self.head_dim)
@@ -126,9 +160,6 @@ class GatedAttention(nn.Module):
             cos = self.pos_cos_cache[:, :rp][position_ids]
             sin = self.pos_sin_cache[:, :rp][position_ids]
             q, k = PartialRopeFunction.apply(q, k, cos, sin, rp)
-        seq_ids = None
-        if cu_seqlens is not None:
-            seq_ids = _seq_ids_from_cu_seqlens(cu_seqlens, unpad_indices, bsz, seq_len)
         attn = attention_core(q, k, v, window=self.window_size, seq_ids=seq_ids, k_sink=self.k_sink)
         gate = torch.sigmoid(gate_logits)
         attn = attn * gate.unsqueeze(-1)

@@ -33,9 +33,14 @@ class MoELayer(nn.Module):
         nn.init.normal_(self.routed_experts.experts.weight, mean=0.0, std=std)
         nn.init.normal_(self.routed_experts.output_experts.weight, mean=0.0, std=std)
 
-    def forward(self, hidden_states, unpad_indices=None, out_dtype=None):
+    # the block's residual add, the shared expert's output and the routed combine as one
+    # kernel (scattermoe.mlp.GLUExpertsFunction with shared / residual); off: torch adds
+    fused_close = True
+
+    def forward(self, hidden_states, unpad_indices=None, out_dtype=None, residual=None):
         """(out, topk_idx); out in the input's dtype, or out_dtype when given (a block whose
-        norm already produced the bf16 input passes its f32 residual dtype)."""
+        norm already produced the bf16 input passes its f32 residual dtype).  With residual
+        (f32, the stream the block adds the layer's output to) out = residual + layer output."""
         if unpad_indices is not None:
             bsz, seq_len, d = hidden_states.shape
             x = hidden_states.reshape(bsz * seq_len, d).index_select(0, unpad_indices).unsqueeze(0)
@@ -50,10 +55,18 @@ class MoELayer(nn.Module):
         logits = F.linear(x.reshape(-1, d), self.gate.weight)   # the router: T x E, tiny
         topk_idx, topk_weight = self.gate.route(logits)
         shared = se(x)
+        if (residual is not None and unpad_indices is None and self.fused_close and residual.dtype == torch.float32
+                and x.dtype in (torch.bfloat16, torch.float16) and type(self.routed_experts) is GLUMLP
+                and self.routed_experts._fused_ok()
+                and self.routed_experts.top_k <= 8 and x.size(-1) % 8 == 0):
+            out = self.routed_experts(x, topk_weight, topk_idx, shared=shared, residual=residual)
+            return out.view(residual.shape), topk_idx.view(*x.shape[:-1], k)
         routed = self.routed_experts(x, topk_weight, topk_idx)
         # the reference adds a bf16 shared output to f32 routed rows: the sum in f32
         out = shared.to(in_dtype) + routed
         topk_idx = topk_idx.view(*x.shape[:-1], k)
+        if residual is not None and unpad_indices is None:
+            out = residual + out
         if unpad_indices is not None:
             full = out.new_zeros(bsz * seq_len, out.size(-1))
             full.index_copy_(0, unpad_indices, out.squeeze(0))
@@ -61,4 +74,6 @@ class MoELayer(nn.Module):
             idx_full = topk_idx.new_zeros(bsz * seq_len, k)
             idx_full.index_copy_(0, unpad_indices, topk_idx.reshape(-1, k))
             topk_idx = idx_full.view(bsz, seq_len, k)
+            if residual is not None:
+                out = residual + out
         return out, topk_idx

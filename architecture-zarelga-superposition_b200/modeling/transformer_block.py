@@ -47,5 +47,4 @@ class TransformerBlock(nn.Module):
         if attn.dtype != torch.bfloat16:
             attn = attn.to(torch.bfloat16)
         h, y2 = AddZRMSNormFunction.apply(x, attn, n2.weight, n2.eps)
-        moe_out, topk_idx = self.mlp(y2, unpad_indices=unpad_indices, out_dtype=torch.float32)
-        return h + moe_out, topk_idx
+        return self.mlp(y2, unpad_indices=unpad_indices, out_dtype=torch.float32, residual=h)

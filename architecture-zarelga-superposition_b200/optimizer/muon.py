@@ -14,6 +14,7 @@ has host syncs, so a whole step can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
@@ -160,11 +161,13 @@ def _flat3(t, m, n):
     return t.reshape(-1, m, n)
 
 
-def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
+def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable, x_out=None, x_trans=False):
     """Fused first half of the MD step: returns (W f32, gain reductions, X bf16 [..., m, n]).
 
     W = p (f32 view or copy); buf.lerp_(g*G, 1-momentum); X = lerp(g*G, buf, momentum) in
-    bf16 (the Newton-Schulz input); the gain gradients' reductions of (W/g)*G from the old gains."""
+    bf16 (the Newton-Schulz input); the gain gradients' reductions of (W/g)*G from the old gains.
+    x_out: a contiguous bf16 [L, m, n] destination for X (a slice of a Newton-Schulz stack),
+    or [L, n, m] with x_trans (X written transposed, the layout a tall stack runs in)."""
     W = p if p.dtype == torch.float32 else p.float()
     G = grad if grad.dtype == torch.float32 else grad.float()
     W, G = W.contiguous(), G.contiguous()
@@ -172,7 +175,16 @@ def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
     if len(state) == 0:
         _init_md_state(state, W, gain_mode, norm_axis, capturable)
     L = W.numel() // (m * n)
-    X = torch.empty(W.shape, dtype=torch.bfloat16, device=W.device)
+    if x_out is None:
+        if x_trans:
+            raise ValueError("x_trans needs x_out")
+        X = torch.empty(W.shape, dtype=torch.bfloat16, device=W.device)
+    else:
+        want = (L, n, m) if x_trans else (L, m, n)
+        if (tuple(x_out.shape) != want or x_out.dtype != torch.bfloat16 or not x_out.is_contiguous()
+                or x_out.device != W.device):
+            raise Z.ZsError(f"x_out must be a contiguous bf16 {want} tensor on {W.device}")
+        X = x_out
     red = {k: torch.empty_like(state[k]) for k in ("g_scalar", "g_row", "g_col") if k in state}
     buf = state["momentum_buffer"]
     ws = torch.empty(int(Z.lib().zs_muonmd_pre_workspace(L, m, n)) if red else 0, dtype=torch.uint8,
@@ -180,7 +192,7 @@ def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
     Z.count(1 + len(red))
     Z.check(Z.lib().zs_muonmd_pre(W.data_ptr(), G.data_ptr(), buf.data_ptr(),
                                   Z.ptr(state.get("g_scalar")), Z.ptr(state.get("g_row")), Z.ptr(state.get("g_col")),
-                                  X.data_ptr(), Z.ptr(red.get("g_scalar")), Z.ptr(red.get("g_row")),
+                                  X.data_ptr(), int(bool(x_trans)), Z.ptr(red.get("g_scalar")), Z.ptr(red.get("g_row")),
                                   Z.ptr(red.get("g_col")), L, m, n, float(momentum), ws.data_ptr() if red else None,
                                   ws.numel(), Z.stream_of(W)), "zs_muonmd_pre")
     return W, red, X
@@ -189,9 +201,10 @@ def _md_pre(p, grad, state, *, momentum, gain_mode, norm_axis, capturable):
 _AXIS = {"frobenius": 0, "row": 1, "col": 2}
 
 
-def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axis, rescale_mode):
+def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axis, rescale_mode, u_trans=False):
     """Fused second half: W_hat' = W/g - lr*rescale*U projected onto the sphere, gain Adam
-    steps from the old gains, p = g_new * W_hat' in p's dtype."""
+    steps from the old gains, p = g_new * W_hat' in p's dtype.  U is [..., m, n], or the
+    transposed [L, n, m] with u_trans."""
     if norm_axis not in _AXIS:
         raise ValueError(f"unknown norm_axis {norm_axis!r}")
     m, n = W.shape[-2], W.shape[-1]
@@ -206,7 +219,11 @@ def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axi
     lr_dev = lr if torch.is_tensor(lr) else None
     if lr_dev is not None:
         lr_dev = lr_dev.to(device=W.device, dtype=torch.float32)
-    U = U.contiguous()
+    if u_trans:
+        if tuple(U.shape) != (L, n, m) or not U.is_contiguous() or U.dtype != torch.bfloat16:
+            raise Z.ZsError(f"a transposed update must be a contiguous bf16 {(L, n, m)} tensor")
+    else:
+        U = U.contiguous()
     target = state["target_norm"].contiguous()
     direct = p.is_contiguous() and p.dtype in (torch.float32, torch.bfloat16)
     out = p if direct else W
@@ -214,7 +231,7 @@ def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axi
     g = lambda k: state.get(k)  # noqa: E731
     Z.count(4)
     Z.check(Z.lib().zs_muonmd_post(
-        W.data_ptr(), U.data_ptr(), out.data_ptr(), Z.dtype_code(out.dtype),
+        W.data_ptr(), U.data_ptr(), int(bool(u_trans)), out.data_ptr(), Z.dtype_code(out.dtype),
         Z.ptr(g("g_scalar")), Z.ptr(g("g_row")), Z.ptr(g("g_col")),
         Z.ptr(g("g_scalar_m1")), Z.ptr(g("g_scalar_m2")), Z.ptr(g("g_row_m1")), Z.ptr(g("g_row_m2")),
         Z.ptr(g("g_col_m1")), Z.ptr(g("g_col_m2")),
@@ -253,55 +270,60 @@ def _ns_sharded(stack, steps, process_group, ns):
     return full[:b]
 
 
+def _ns_plan(shapes, steps, world):
+    """The batched Newton-Schulz launches for matrices stacks of the given (L, m, n) shapes
+    and step counts: [(mm, nn, steps, indices)], mm <= nn the oriented shape.  Stacks of one
+    oriented shape and step count share a launch; a stack of 32+ matrices per rank fills
+    the GPU on its own; smaller ones are merged up to 64 matrices per rank and about 1 GiB
+    of Newton-Schulz workspace per rank."""
+    groups = {}
+    for i, ((L, m, n), st) in enumerate(zip(shapes, steps)):
+        groups.setdefault((min(m, n), max(m, n), int(st)), []).append(i)
+    plan = []
+    for (mm, nn, st), idx in groups.items():
+        chunk, batch = [], 0
+        for i in idx:
+            b = shapes[i][0]
+            if b >= 32 * world:
+                plan.append((mm, nn, st, [i]))
+                continue
+            if chunk and (batch + b > 64 * world or (batch + b) * mm * (2 * mm + nn) * 2 > (1 << 30) * world):
+                plan.append((mm, nn, st, chunk))
+                chunk, batch = [], 0
+            chunk.append(i)
+            batch += b
+        if chunk:
+            plan.append((mm, nn, st, chunk))
+    return plan
+
+
 def _zeropower_many(Xs, steps, process_group=None, ns=None):
     """zeropower_via_newtonschulz5 of every tensor in Xs; matrices of one oriented shape
-    (and step count) from different tensors share batched launches.  With a
-    process group of more than one rank, each batch is split over the ranks and
-    the orthogonalised matrices are all-gathered (_ns_sharded).  `ns` replaces the
+    (and step count) from different tensors share batched launches (_ns_plan).  With a
+    process group of more than one rank, each batch is split over the ranks and the
+    orthogonalised matrices are all-gathered (_ns_sharded).  `ns` replaces the
     Newton-Schulz function (default: the libzs kernels)."""
     ns = zeropower_via_newtonschulz5 if ns is None else ns
     world, _ = _world(process_group)
     out = [None] * len(Xs)
-    groups = {}
-    for i, (X, st) in enumerate(zip(Xs, steps)):
-        m, n = X.shape[-2], X.shape[-1]
-        groups.setdefault((min(m, n), max(m, n), int(st)), []).append(i)
-    for (mm, nn, st), idx in groups.items():
-        chunk, batch = [], 0
-
-        def flush(chunk):
-            if not chunk:
-                return
-            parts = []
-            for i in chunk:
-                X = Xs[i]
-                Xo = X.mT if X.shape[-2] > X.shape[-1] else X
-                parts.append(Xo.reshape(-1, mm, nn))
-            stack = parts[0] if len(parts) == 1 else torch.cat(parts, 0)
-            Y = _ns_sharded(stack, st, process_group, ns)
-            off = 0
-            for i, part in zip(chunk, parts):
-                X = Xs[i]
-                b = part.shape[0]
-                tall = X.shape[-2] > X.shape[-1]
-                y = Y[off:off + b]
-                off += b
-                y = y.reshape(X.mT.shape if tall else X.shape)
-                out[i] = y.mT if tall else y
-
-        for i in idx:
-            b = Xs[i].numel() // (mm * nn)
-            # a stack of 32+ matrices per rank fills the GPU on its own; small ones are merged
-            # up to 64 matrices per rank (and about 1 GiB of Newton-Schulz workspace) per launch
-            if b >= 32 * world:
-                flush([i])
-                continue
-            if chunk and (batch + b > 64 * world or (batch + b) * mm * (2 * mm + nn) * 2 > (1 << 30) * world):
-                flush(chunk)
-                chunk, batch = [], 0
-            chunk.append(i)
-            batch += b
-        flush(chunk)
+    shapes = [(X.numel() // (X.shape[-2] * X.shape[-1]), X.shape[-2], X.shape[-1]) for X in Xs]
+    for mm, nn, st, chunk in _ns_plan(shapes, steps, world):
+        parts = []
+        for i in chunk:
+            X = Xs[i]
+            Xo = X.mT if X.shape[-2] > X.shape[-1] else X
+            parts.append(Xo.reshape(-1, mm, nn))
+        stack = parts[0] if len(parts) == 1 else torch.cat(parts, 0)
+        Y = _ns_sharded(stack, st, process_group, ns)
+        off = 0
+        for i, part in zip(chunk, parts):
+            X = Xs[i]
+            b = part.shape[0]
+            tall = X.shape[-2] > X.shape[-1]
+            y = Y[off:off + b]
+            off += b
+            y = y.reshape(X.mT.shape if tall else X.shape)
+            out[i] = y.mT if tall else y
     return out
 
 
@@ -322,18 +344,45 @@ def md_decoupled_step(p, grad, state, *, lr, momentum, gain_lr, gain_betas, gain
 def md_decoupled_steps(jobs, states, process_group=None):
     """md_decoupled_step for many parameters at once: jobs = [(p, hyper-parameter dict)].
     Same result per parameter; the Newton-Schulz launches are shared across parameters
-    whose matrices have the same shape.  With a process group, every rank runs the
-    element-wise passes on all parameters (their state stays replicated) and the
-    Newton-Schulz batches are split over the ranks and all-gathered."""
-    pre = []
+    whose matrices have the same shape (_ns_plan).  zs_muonmd_pre writes each parameter's
+    Newton-Schulz input straight into its slice of the batch's stack -- transposed for a
+    tall stack -- and zs_muonmd_post reads the orthogonalised update from the same place,
+    so no stack is assembled, transposed or split by copies.  With a process group, every
+    rank runs the element-wise passes on all parameters (their state stays replicated)
+    and the Newton-Schulz batches are split over the ranks and all-gathered."""
+    world, _ = _world(process_group)
+    shapes = []
     for p, hp in jobs:
         Z.require_cuda(p, p.grad)
-        pre.append(_md_pre(p, p.grad, states[p], momentum=hp["momentum"], gain_mode=hp["gain_mode"],
-                           norm_axis=hp["norm_axis"], capturable=hp["capturable"]))
-    Us = _zeropower_many([x for _, _, x in pre], [hp["ns_steps"] for _, hp in jobs], process_group)
-    for (p, hp), (W, red, _), U in zip(jobs, pre, Us):
-        _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
-                 gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"])
+        m, n = p.shape[-2], p.shape[-1]
+        shapes.append((p.numel() // (m * n), m, n))
+    for mm, nn, st, chunk in _ns_plan(shapes, [hp["ns_steps"] for _, hp in jobs], world):
+        total = sum(shapes[i][0] for i in chunk)
+        # the kernels' 8-element granularity: other shapes are padded by the copying path
+        direct = mm % 8 == 0 and nn % 8 == 0
+        stack = torch.empty(total, mm, nn, dtype=torch.bfloat16, device=jobs[chunk[0]][0].device) if direct else None
+        pre, off = [], 0
+        for i in chunk:
+            p, hp = jobs[i]
+            L, m, n = shapes[i]
+            x_out = stack[off:off + L] if direct else None
+            off += L
+            pre.append(_md_pre(p, p.grad, states[p], momentum=hp["momentum"], gain_mode=hp["gain_mode"],
+                               norm_axis=hp["norm_axis"], capturable=hp["capturable"], x_out=x_out,
+                               x_trans=direct and m > n))
+        if direct:
+            Y = _ns_sharded(stack, st, process_group, zeropower_via_newtonschulz5)
+            Us, off = [], 0
+            for i in chunk:
+                Us.append(Y[off:off + shapes[i][0]])
+                off += shapes[i][0]
+        else:
+            Us = _zeropower_many([x for _, _, x in pre], [st] * len(chunk), process_group)
+        for i, (W, red, _), U in zip(chunk, pre, Us):
+            p, hp = jobs[i]
+            _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
+                     gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"],
+                     u_trans=direct and shapes[i][1] > shapes[i][2])
 
 
 def _muon_steps(jobs, states, process_group=None):
@@ -359,16 +408,67 @@ def _muon_steps(jobs, states, process_group=None):
         _scaled_add_(p, U.reshape(p.shape), group["lr"])
 
 
-def _adam_steps(group, states):
-    """AdamW with decoupled weight decay for an aux-Adam group (optimizer/muon.py:226-240)."""
-    for p in group["params"]:
+def _adam_fused_ok(params):
+    return all(p.is_cuda and p.dtype == torch.float32 and p.is_contiguous() and p.grad is not None
+               and not p.grad.is_sparse and p.grad.dtype == torch.float32 and p.grad.is_contiguous()
+               for p in params)
+
+
+def _adamw_fused(group, params, states):
+    """One zs_adamw_step launch for every parameter of an aux-Adam group (CUDA f32): the
+    state and its layout are the reference's (exp_avg, exp_avg_sq, step), the step
+    counters advance first as `state["step"] += 1` does."""
+    b1, b2 = group["betas"]
+    lr = group["lr"]
+    dev_steps, descs = [], []
+    for p in params:
+        st = states[p]
+        if torch.is_tensor(st["step"]):
+            dev_steps.append(st["step"])
+        else:
+            st["step"] += 1
+    if dev_steps:
+        torch._foreach_add_(dev_steps, 1.0)
+    for p in params:
+        st = states[p]
+        d = Z.AdamWTensor()
+        d.p, d.g, d.m1, d.m2 = p.data_ptr(), p.grad.data_ptr(), st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr()
+        if torch.is_tensor(st["step"]):
+            d.step_dev = st["step"].data_ptr()
+        else:
+            # torch divides by a Python scalar as a product with its f32 reciprocal
+            d.inv_bc1_host = float(np.float32(1.0) / np.float32(1 - b1 ** st["step"]))
+            d.inv_bc2_host = float(np.float32(1.0) / np.float32(1 - b2 ** st["step"]))
+        d.shadow_bf16 = None
+        d.n = p.numel()
+        descs.append(d)
+    arr = (Z.AdamWTensor * len(descs))(*descs)
+    lr_dev = lr.to(device=params[0].device, dtype=torch.float32) if torch.is_tensor(lr) else None
+    Z.count(-(-len(descs) // 96))
+    Z.check(Z.lib().zs_adamw_step(arr, len(descs), Z.ptr(lr_dev), 0.0 if lr_dev is not None else float(lr),
+                                  1.0 if lr_dev is not None else float(1 - lr * group["weight_decay"]), float(b1),
+                                  float(b2), 1 - b1, 1 - b2, float(group["eps"]), float(group["weight_decay"]),
+                                  Z.stream_of(params[0])), "zs_adamw_step")
+
+
+def _adam_steps(group, states, capturable=False):
+    """AdamW with decoupled weight decay for an aux-Adam group (optimizer/muon.py:226-240,
+    :616-650).  CUDA f32 parameters run as one fused launch (zs_adamw_step); anything else
+    (CPU tensors, other dtypes) runs the reference's tensor formulation."""
+    params = group["params"]
+    for p in params:
         if p.grad is None:
             p.grad = torch.zeros_like(p)
-        state = states[p]
+        state = states.setdefault(p, {})
         if len(state) == 0:
             state["exp_avg"] = torch.zeros_like(p)
             state["exp_avg_sq"] = torch.zeros_like(p)
-            state["step"] = 0
+            state["step"] = torch.zeros((), dtype=torch.float32, device=p.device) if capturable else 0
+    if params and _adam_fused_ok(params):
+        _adamw_fused(group, params, states)
+        return
+    for p in params:
+        state = states[p]
         state["step"] += 1
         update = adam_update(p.grad, state["exp_avg"], state["exp_avg_sq"], state["step"], group["betas"],
                              group["eps"])
@@ -518,20 +618,11 @@ class SingleDeviceMuonMDWithAuxAdam(torch.optim.Optimizer):
                             for p in group["params"] if p.grad is not None], self.state,
                            getattr(self, "process_group", None))
         for group in self.param_groups:
-            for p in group["params"]:
-                if p.grad is None or group["use_muon"]:
-                    continue
-                state = self.state[p]
-                if len(state) == 0:
-                    state["exp_avg"] = torch.zeros_like(p)
-                    state["exp_avg_sq"] = torch.zeros_like(p)
-                    state["step"] = (torch.zeros((), dtype=torch.float32, device=p.device) if group["capturable"]
-                                     else 0)
-                state["step"] += 1
-                update = adam_update(p.grad, state["exp_avg"], state["exp_avg_sq"], state["step"], group["betas"],
-                                     group["eps"])
-                p.mul_(1 - group["lr"] * group["weight_decay"])
-                _scaled_add_(p, update, group["lr"])
+            if group["use_muon"]:
+                continue
+            # parameters without a gradient are skipped (their state does not advance)
+            _adam_steps(dict(group, params=[p for p in group["params"] if p.grad is not None]), self.state,
+                        capturable=group["capturable"])
         return loss
 
 

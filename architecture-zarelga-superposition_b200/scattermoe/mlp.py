@@ -119,8 +119,8 @@ class GLUExpertsFunction(torch.autograd.Function):
     and lets a data-parallel reducer start on each as soon as it is complete."""
 
     @staticmethod
-    def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k, fuse_wgrad=False):
-        Z.require_cuda(x, expert_p, expert_idxs, W1, W2)
+    def forward(ctx, x, expert_p, expert_idxs, W1, W2, num_experts, k, fuse_wgrad=False, shared=None, residual=None):
+        Z.require_cuda(x, expert_p, expert_idxs, W1, W2, shared, residual)
         cdt = _compute_dtype(x)
         xc = x.to(cdt).contiguous()
         W1c = W1.to(cdt).contiguous()
@@ -133,10 +133,27 @@ class GLUExpertsFunction(torch.autograd.Function):
         y_rows = torch.empty((T * k, W2c.size(1)), dtype=cdt, device=x.device)
         ops._launch_scatter2scatter(y_rows, W2c.permute(0, 2, 1), act, 1, sei, ssi, None, True, False,
                                     expert_offsets=offs, tag="down_fwd")
-        y = weighted_row_sum(y_rows, pc, T, k)
         ctx.save_for_backward(xg, act, hfull, y_rows, sei, ssi, offs, pc, W1c, W2c)
         ctx.meta = (x.dtype, expert_p.dtype, W1.dtype, W2.dtype, num_experts, k, T)
         ctx.fused_params = (W1, W2) if fuse_wgrad and W1.is_leaf and W2.is_leaf else None
+        ctx.closed = shared is not None or residual is not None
+        if ctx.closed:
+            # residual + (shared + routed) in f32, one pass (zs_moe_combine)
+            y = torch.empty((T, W2c.size(1)), dtype=torch.float32, device=x.device)
+            sh = shared.reshape(T, -1).to(cdt).contiguous() if shared is not None else None
+            rs = residual.reshape(T, -1).contiguous() if residual is not None else None
+            if rs is not None and rs.dtype != torch.float32:
+                raise Z.ZsError("the residual stream of the fused MoE close must be f32")
+            Z.count(1)
+            Z.check(Z.lib().zs_moe_combine(y.data_ptr(), y.stride(0), y_rows.data_ptr(), y_rows.stride(0),
+                                           pc.data_ptr(), Z.dtype_code(pc.dtype), T, k, y.size(1),
+                                           Z.dtype_code(cdt), Z.ptr(sh), sh.stride(0) if sh is not None else 0,
+                                           Z.ptr(rs), rs.stride(0) if rs is not None else 0, Z.stream_of(y)),
+                    "zs_moe_combine")
+            ctx.shared_meta = (shared.shape, shared.dtype) if shared is not None else None
+            ctx.residual_meta = (residual.shape, residual.dtype) if residual is not None else None
+            return y
+        y = weighted_row_sum(y_rows, pc, T, k)
         return y.to(x.dtype)
 
     @staticmethod
@@ -166,7 +183,15 @@ class GLUExpertsFunction(torch.autograd.Function):
         ops._launch_scatter2scatter(dx_rows, W1c, dhfull, 1, sei, ssi, None, True, False, expert_offsets=offs,
                                     tag="up_dx")
         dx = weighted_row_sum(dx_rows, None, T, k)
-        return dx.to(x_dt), d_p, None, gW1, gW2, None, None, None
+        d_shared = d_res = None
+        if ctx.closed:
+            # the f32 gradient of the closed sum goes to the residual as is and, in the
+            # compute dtype already cast once above, to the shared expert
+            if ctx.shared_meta is not None:
+                d_shared = dyc.view(ctx.shared_meta[0]).to(ctx.shared_meta[1])
+            if ctx.residual_meta is not None:
+                d_res = dy.view(ctx.residual_meta[0])
+        return dx.to(x_dt), d_p, None, gW1, gW2, None, None, None, d_shared, d_res
 
 
 class MLP(nn.Module):
@@ -213,10 +238,20 @@ class GLUMLP(nn.Module):
     def _fused_ok(self) -> bool:
         return self.experts.bias is None and isinstance(self.activation, nn.SiLU)
 
-    def forward(self, x: torch.Tensor, expert_p: torch.Tensor, expert_idxs: torch.Tensor):
+    def forward(self, x: torch.Tensor, expert_p: torch.Tensor, expert_idxs: torch.Tensor, shared=None,
+                residual=None):
+        """y = the routed experts' output; with shared and/or residual (this package's fused
+        path only: bias-free SiLU experts, k <= 8, 16-bit compute) y = residual + (shared + routed)
+        in f32, the transformer block's MoE close in one pass."""
         x_shape = x.size()
         x = x.view(-1, x_shape[-1])
-        if self._fused_ok():
+        if shared is not None or residual is not None:
+            if not (self._fused_ok() and self.top_k <= 8):
+                raise Z.ZsError("the fused MoE close needs bias-free SiLU experts with top_k <= 8")
+            y = GLUExpertsFunction.apply(x, expert_p.reshape(x.size(0), -1), expert_idxs.reshape(x.size(0), -1),
+                                         self.experts.weight, self.output_experts.weight, self.num_experts,
+                                         self.top_k, self.fuse_weight_grad, shared, residual)
+        elif self._fused_ok():
             y = GLUExpertsFunction.apply(x, expert_p.reshape(x.size(0), -1), expert_idxs.reshape(x.size(0), -1),
                                          self.experts.weight, self.output_experts.weight, self.num_experts,
                                          self.top_k, self.fuse_weight_grad)

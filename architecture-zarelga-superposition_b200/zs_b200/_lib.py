@@ -20,6 +20,12 @@ _DTYPE_CODE = {torch.float32: ZS_F32, torch.bfloat16: ZS_BF16, torch.float16: ZS
 
 _vp, _i64, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 
+class AdamWTensor(ctypes.Structure):
+    """zs_adamw_tensor (include/zs.h)."""
+    _fields_ = [("p", _vp), ("g", _vp), ("m1", _vp), ("m2", _vp), ("step_dev", _vp), ("inv_bc1_host", _f32),
+                ("inv_bc2_host", _f32), ("shadow_bf16", _vp), ("n", _i64)]
+
+
 # name -> (restype, argtypes); mirrors include/zs.h
 _SIGNATURES = {
     "zs_version": (_i32, []),
@@ -71,10 +77,24 @@ _SIGNATURES = {
     "zs_ipc_close": (_i32, [_vp]),
     "zs_ce_allreduce_chunk": (_i64, [_i64, _i32]),
     "zs_ce_allreduce": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp]),
-    "zs_muonmd_pre": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _sz,
-                             _vp]),
+    "zs_muonmd_pre": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp,
+                             _sz, _vp]),
     "zs_muonmd_post_workspace": (_sz, [_i64, _i64, _i64]),
-    "zs_muonmd_post": (_i32, [_vp, _vp, _vp, _i32] + [_vp] * 12 + [_vp, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
+    "zs_adamw_step": (_i32, [_vp, _i32, _vp, _f32, _f32, _f32, _f32, ctypes.c_double, ctypes.c_double, _f32, _f32,
+                             _vp]),
+    "zs_qk_norm_rope_forward": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _i64, _vp, _i64,
+                                       _i32, _i32, _i32, _i32, _f32, _vp]),
+    "zs_qk_norm_rope_backward_workspace": (_sz, [_i32]),
+    "zs_qk_norm_rope_backward": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp,
+                                        _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "zs_gated_attention_forward": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32,
+                                          _i32, _i32, _i32, _i32, _vp, _vp, _i32, _f32, _vp]),
+    "zs_gated_attention_backward_workspace": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "zs_gated_attention_backward": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64,
+                                           _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32,
+                                           _i32, _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _sz, _vp]),
+    "zs_moe_combine": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
+    "zs_muonmd_post": (_i32, [_vp, _vp, _i32, _vp, _i32] + [_vp] * 12 + [_vp, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
                                                                   _f32, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "zs_newton_schulz5_workspace": (_sz, [_i64, _i64, _i64, _i32]),
     "zs_newton_schulz5": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _f32, _f32, _f32, _vp, _sz, _i32, _vp]),

@@ -99,3 +99,119 @@ def attention(q, k, v, *, window=None, seq_ids=None, k_sink=None, scale=None):
     scale = 1.0 / math.sqrt(hd) if scale is None else float(scale)
     seg_start = seg_start_from_seq_ids(seq_ids) if seq_ids is not None else None
     return _Attention.apply(q, k, v, k_sink, int(window) if window else 0, seg_start, scale)
+
+
+class _GatedAttentionCore(torch.autograd.Function):
+    """GatedAttention between its two projections, on the fused q/k/v/gate projection
+    output qkvg [B, S, W] (bf16; columns: H query heads, Hkv key heads, Hkv value heads,
+    H gate logits, zero padding): the per-head q/k zero-centred RMSNorm + partial RoPE
+    (zs_qk_norm_rope_forward, one kernel writing the normalised q and k), attention with
+    the sigmoid output gate applied in its epilogue, reading v and the gate logits in
+    place (zs_gated_attention_forward).  The backward writes the whole gradient of qkvg
+    -- dq/dk through the norm/RoPE transpose, dv and the gate logits' gradient from the
+    attention kernels, zeros in the padding -- with no split, cat or copy."""
+
+    @staticmethod
+    def forward(ctx, qkvg, wq, wk, k_sink, cos, sin, H, Hkv, hd, rot, eps, window, seg_start, scale, pad):
+        B, S, W = qkvg.shape
+        dev = qkvg.device
+        qk = torch.empty(B, S, (H + Hkv) * hd, dtype=torch.bfloat16, device=dev)
+        rstd = torch.empty(B * S * (H + Hkv), dtype=torch.float32, device=dev)
+        L = Z.lib()
+        tab_dt = Z.dtype_code(cos.dtype) if cos is not None else Z.ZS_F32
+        cos_bs = cos.shape[0] if cos is not None else 1
+        cos_ld = cos.stride(-2) if cos is not None else 0
+        Z.count(1)
+        Z.check(L.zs_qk_norm_rope_forward(qkvg.data_ptr(), W, wq.data_ptr(), wk.data_ptr(), Z.ptr(cos), Z.ptr(sin),
+                                          tab_dt, cos_ld, cos_bs, rot, qk.data_ptr(), (H + Hkv) * hd,
+                                          rstd.data_ptr(), B * S, S, H, Hkv, hd, float(eps), Z.stream_of(qkvg)),
+                "zs_qk_norm_rope_forward")
+        o = torch.empty(B, S, H * hd, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+        ld_qk = (H + Hkv) * hd
+        v_ptr = qkvg.data_ptr() + 2 * (H + Hkv) * hd
+        g_ptr = qkvg.data_ptr() + 2 * (H + 2 * Hkv) * hd
+        with Z.timed("attention_fwd", attention_flops(B, S, H, hd, window)):
+            Z.check(L.zs_gated_attention_forward(qk.data_ptr(), ld_qk, qk.data_ptr() + 2 * H * hd, ld_qk, v_ptr, W,
+                                                 o.data_ptr(), H * hd, lse.data_ptr(), g_ptr, W, B, S, H, Hkv, hd,
+                                                 window, Z.ptr(seg_start), Z.ptr(k_sink),
+                                                 Z.dtype_code(k_sink.dtype) if k_sink is not None else 0, scale,
+                                                 Z.stream_of(qkvg)), "zs_gated_attention_forward")
+        Z.count(1)
+        ctx.save_for_backward(qkvg, qk, o, lse, rstd, wq, wk, k_sink, cos, sin, seg_start)
+        ctx.meta = (H, Hkv, hd, rot, window, scale, pad)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkvg, qk, o, lse, rstd, wq, wk, k_sink, cos, sin, seg_start = ctx.saved_tensors
+        H, Hkv, hd, rot, window, scale, pad = ctx.meta
+        B, S, W = qkvg.shape
+        dev = qkvg.device
+        do = do.contiguous()
+        if do.dtype != torch.bfloat16:
+            do = do.to(torch.bfloat16)
+        L = Z.lib()
+        dqkvg = torch.empty_like(qkvg)
+        dqk = torch.empty_like(qk)
+        D = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+        ds_sink = torch.empty(B, H, S, dtype=torch.float32, device=dev) if k_sink is not None else None
+        ws = torch.empty(int(L.zs_gated_attention_backward_workspace(B, S, H, hd, 1)), dtype=torch.uint8, device=dev)
+        ld_qk = (H + Hkv) * hd
+        base = qkvg.data_ptr()
+        dbase = dqkvg.data_ptr()
+        with Z.timed("attention_bwd", 2.5 * attention_flops(B, S, H, hd, window)):
+            Z.check(L.zs_gated_attention_backward(
+                qk.data_ptr(), ld_qk, qk.data_ptr() + 2 * H * hd, ld_qk, base + 2 * (H + Hkv) * hd, W,
+                o.data_ptr(), H * hd, do.data_ptr(), H * hd, lse.data_ptr(), base + 2 * (H + 2 * Hkv) * hd, W,
+                dqk.data_ptr(), ld_qk, dqk.data_ptr() + 2 * H * hd, ld_qk, dbase + 2 * (H + Hkv) * hd, W,
+                dbase + 2 * (H + 2 * Hkv) * hd, W, pad, D.data_ptr(), B, S, H, Hkv, hd, window, Z.ptr(seg_start),
+                Z.ptr(k_sink), Z.dtype_code(k_sink.dtype) if k_sink is not None else 0, Z.ptr(ds_sink), scale,
+                ws.data_ptr(), ws.numel(), Z.stream_of(qkvg)), "zs_gated_attention_backward")
+        Z.count(3)
+        dwq = torch.empty(hd, dtype=torch.float32, device=dev)
+        dwk = torch.empty(hd, dtype=torch.float32, device=dev)
+        ws2 = torch.empty(int(L.zs_qk_norm_rope_backward_workspace(hd)), dtype=torch.uint8, device=dev)
+        tab_dt = Z.dtype_code(cos.dtype) if cos is not None else Z.ZS_F32
+        cos_bs = cos.shape[0] if cos is not None else 1
+        cos_ld = cos.stride(-2) if cos is not None else 0
+        Z.count(2)
+        Z.check(L.zs_qk_norm_rope_backward(dqk.data_ptr(), ld_qk, base, W, wq.data_ptr(), wk.data_ptr(), Z.ptr(cos),
+                                           Z.ptr(sin), tab_dt, cos_ld, cos_bs, rot, rstd.data_ptr(), dbase, W,
+                                           dwq.data_ptr(), dwk.data_ptr(), B * S, S, H, Hkv, hd, ws2.data_ptr(),
+                                           ws2.numel(), Z.stream_of(qkvg)),
+                "zs_qk_norm_rope_backward")
+        dk_sink = None
+        if k_sink is not None and ctx.needs_input_grad[3]:
+            q = qk[..., : H * hd].reshape(B, S, H, hd)
+            dk_sink = (torch.einsum("bhs,bshd->hd", ds_sink, q.float()) * scale).to(k_sink.dtype)
+        return (dqkvg, dwq.to(wq.dtype), dwk.to(wk.dtype), dk_sink) + (None,) * 11
+
+
+def gated_attention_core(qkvg, wq, wk, *, n_heads, n_kv_heads, head_dim, cos=None, sin=None, rot_pairs=0,
+                         eps=1e-6, window=None, seq_ids=None, k_sink=None, scale=None, pad=0):
+    """o [B, S, H * hd] (bf16) = sigmoid(gate) * attention(rope(norm(q)), rope(norm(k)), v) from the
+    fused projection output qkvg [B, S, (H + 2 Hkv) * hd + H + pad] (bf16, contiguous); cos/sin
+    [1 or B, S, rot_pairs] RoPE tables (None when rot_pairs is 0)."""
+    Z.require_cuda(qkvg, wq, wk, k_sink, seq_ids, cos, sin)
+    H, Hkv, hd = int(n_heads), int(n_kv_heads), int(head_dim)
+    if qkvg.dtype != torch.bfloat16 or not qkvg.is_contiguous():
+        raise Z.ZsError("the fused projection output must be a contiguous bf16 tensor")
+    if hd not in (64, 128) or H % Hkv:
+        raise Z.ZsError(f"attention supports head_dim 64/128 and H % Hkv == 0 (got hd={hd}, H={H}, Hkv={Hkv})")
+    W = qkvg.shape[-1]
+    if W != (H + 2 * Hkv) * hd + H + pad or W % 8 or not 0 <= pad < 32:
+        raise Z.ZsError(f"qkvg width {W} does not match H={H}, Hkv={Hkv}, hd={hd}, pad={pad} (rows must be "
+                        "multiples of 8 elements)")
+    if wq.dtype != torch.float32 or wk.dtype != torch.float32:
+        raise Z.ZsError("the q/k norm weights must be f32")
+    scale = 1.0 / math.sqrt(hd) if scale is None else float(scale)
+    seg_start = seg_start_from_seq_ids(seq_ids) if seq_ids is not None else None
+    if rot_pairs:
+        cos, sin = cos.contiguous(), sin.contiguous()
+    else:
+        cos = sin = None
+    return _GatedAttentionCore.apply(qkvg, wq.contiguous(), wk.contiguous(), k_sink, cos, sin, H, Hkv, hd,
+                                     int(rot_pairs), float(eps), int(window) if window else 0, seg_start, scale,
+                                     int(pad))
+

@@ -955,22 +955,40 @@ def _kernel_xent(args, g):
 
 
 def _kernel_muonmd(args, g):
-    """One md_decoupled_step on config 4's W1 expert stack [64, 1536, 1536] f32 (gains "both")."""
+    """md_decoupled_step on config 4's expert stacks, f32, gains "both": W1 [64, 1536, 1536]
+    (square) and W2 [64, 1536, 768] (tall: Newton-Schulz runs on the transpose); for W1 also
+    its element-wise passes alone (md_pre: momentum + Newton-Schulz input + gain reductions;
+    md_post: the projection reduction, gain Adam and the weight write)."""
     import torch
 
-    from optimizer.muon import md_decoupled_step
+    from optimizer.muon import _md_post, _md_pre, md_decoupled_step, zeropower_via_newtonschulz5
 
-    p = torch.randn(64, 1536, 1536, device="cuda", generator=g) * 0.02
-    grad = torch.randn(64, 1536, 1536, device="cuda", generator=g) * 1e-3
-    state = {}
+    hp = dict(momentum=0.95, gain_mode="both", norm_axis="frobenius", capturable=True)
+    post = dict(gain_lr=1e-3, gain_betas=(0.9, 0.95), gain_eps=1e-10, rescale_mode="balanced")
     lr = torch.tensor(0.02, device="cuda")
+    parts = []
+    for name, shape in (("w1", (64, 1536, 1536)), ("w2", (64, 1536, 768))):
+        p = torch.randn(*shape, device="cuda", generator=g) * 0.02
+        grad = torch.randn(*shape, device="cuda", generator=g) * 1e-3
+        state = {}
 
-    def step():
-        md_decoupled_step(p, grad, state, lr=lr, momentum=0.95, gain_lr=1e-3, gain_betas=(0.9, 0.95),
-                          gain_eps=1e-10, gain_mode="both", norm_axis="frobenius", ns_steps=5, capturable=True,
-                          rescale_mode="balanced")
+        def step(p=p, grad=grad, state=state):
+            md_decoupled_step(p, grad, state, lr=lr, ns_steps=5, **hp, **post)
 
-    return {"shape": [64, 1536, 1536]}, [("step", step, 0.0)]
+        parts.append((f"{name}_step", step, 0.0))
+        if name == "w1":
+            step()
+            W, red, X = _md_pre(p, grad, state, **hp)
+            U = zeropower_via_newtonschulz5(X, steps=5)
+
+            def pre(p=p, grad=grad, state=state):
+                _md_pre(p, grad, state, **hp)
+
+            def post_(p=p, W=W, red=red, U=U, state=state):
+                _md_post(p, W, red, U, state, lr=lr, norm_axis="frobenius", **post)
+
+            parts += [("w1_md_pre", pre, 0.0), ("w1_md_post", post_, 0.0)]
+    return {"shapes": [[64, 1536, 1536], [64, 1536, 768]]}, parts
 
 
 def _kernel_norm_rope(args, g):

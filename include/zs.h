@@ -236,6 +236,19 @@ int zs_weighted_row_sum(void* out, int64_t o_sm, const void* in, int64_t i_sm, c
                         int64_t T, int k, int64_t C, int dtype, void* stream);
 
 /*
+ * The MoE layer's close added into the f32 residual stream (the transformer
+ * block's `h + (shared_experts(x) + routed_experts(x))`,
+ * modeling/transformer_block.py:39-45 with modeling/moe_layer.py:44-58):
+ *   out[t, c] = residual[t, c] + (shared[t, c] + round(sum_j w[t, j] * rows[t*k + j, c]))
+ * in f32, the routed sum rounded to the rows' dtype (bf16 / f16) first as the
+ * unfused path stores it.  shared (rows' dtype) and residual (f32) may be NULL.
+ * k <= 8; C % 8 == 0; 16-byte aligned rows.
+ */
+int zs_moe_combine(float* out, int64_t o_sm, const void* rows, int64_t i_sm, const void* weights, int w_dtype,
+                   int64_t T, int k, int64_t C, int dtype, const void* shared, int64_t s_sm, const float* residual,
+                   int64_t r_sm, void* stream);
+
+/*
  * The same k-way sum with the slot rows stored in another order (no
  * counterpart in the reference; the combine of the expert-parallel layer,
  * whose output rows return in expert order):
@@ -344,6 +357,35 @@ int zs_rope_partial(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride
                     int seq_len, int cos_batch, int n_q_heads, int n_kv_heads, int head_dim, int rot_pairs, int dtype,
                     int table_dtype, int backward, void* stream);
 
+/*
+ * GatedAttention's QK normalisation and partial position RoPE fused
+ * (modeling/attention.py:140-150: q_norm / k_norm = zero-centred RMSNorm per
+ * head, modeling/zRMSNorm.py:4-20, then the rotate-half RoPE of the first
+ * rot pairs, modeling/liger_rope.py).  x: bf16 rows of ldx elements (one row
+ * per token, tokens = batch * seq_len) whose leading (Hq + Hk) * hd columns
+ * are the Hq query heads then the Hk key heads (the fused q/k/v/gate
+ * projection's output); wq / wk: f32 [hd] norm weights (the gain is 1 + w).
+ * forward: y (bf16, rows of ldy, same column order) = rope(x * rsqrt(mean(x^2)
+ *   + eps) * (1 + w)) per head in f32, rounded once; rstd f32 [tokens *
+ *   (Hq + Hk)].  Tables as zs_rope_partial: [cos_bs (1 or batch), seq_len,
+ *   rot] with row stride cos_row_stride, f32 or bf16 (table_dtype).
+ * backward: dx (bf16, rows of lddx; may be the q/k columns of the projection's
+ *   gradient) from dy (rows of lddy); dwq / dwk (f32 [hd]) overwritten with the
+ *   weight gradients, reduced in a fixed order (workspace:
+ *   zs_qk_norm_rope_backward_workspace(hd) bytes).
+ * hd 64 or 128; row strides multiples of 4 elements, rows 8-byte aligned.
+ */
+int zs_qk_norm_rope_forward(const void* x, int64_t ldx, const float* wq, const float* wk, const void* cos,
+                            const void* sin, int table_dtype, int64_t cos_row_stride, int cos_bs, int rot, void* y,
+                            int64_t ldy, float* rstd, int64_t tokens, int seq_len, int Hq, int Hk, int hd, float eps,
+                            void* stream);
+size_t zs_qk_norm_rope_backward_workspace(int hd);
+int zs_qk_norm_rope_backward(const void* dy, int64_t lddy, const void* x, int64_t ldx, const float* wq,
+                             const float* wk, const void* cos, const void* sin, int table_dtype,
+                             int64_t cos_row_stride, int cos_bs, int rot, const float* rstd, void* dx, int64_t lddx,
+                             float* dwq, float* dwk, int64_t tokens, int seq_len, int Hq, int Hk, int hd,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ attention core (a13, a15) */
 
 /*
@@ -378,6 +420,33 @@ int zs_attention_backward(const void* q, const void* k, const void* v, const voi
                           const float* lse, void* dq, void* dk, void* dv, float* D, int B, int S, int H, int Hkv,
                           int hd, int window, const int* seg_start, const void* k_sink, int sink_dtype,
                           float* ds_sink, float softmax_scale, void* stream);
+
+/*
+ * zs_attention_forward / _backward with row strides and GatedAttention's
+ * per-head output gate fused (modeling/attention.py:151-154: o * sigmoid(
+ * head_gate_proj(x)) per head).  Every bf16 operand is rows of ld* elements
+ * (multiples of 8, 16-byte aligned), so q, k, v and the gate logits can be
+ * column ranges of one fused projection output.
+ * forward: with gate_logits (bf16 [B*S, H] rows of ldg, or NULL for no gate)
+ *   o = sigmoid(gate) * attention (sigmoid in f32, one rounding to bf16).
+ * backward: dout is the gradient of the (gated) o; with a gate the kernel
+ *   writes dgate_logits (bf16 [B*S, H] rows of lddg, followed by gate_pad < 32
+ *   zeroed columns) and needs zs_gated_attention_backward_workspace(B, S, H,
+ *   hd, 1) bytes of workspace (the ungated dO of the attention core).
+ *   D = rowsum(dout * o) as before.
+ */
+int zs_gated_attention_forward(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                               void* o, int64_t ldo, float* lse, const void* gate_logits, int64_t ldg, int B, int S,
+                               int H, int Hkv, int hd, int window, const int* seg_start, const void* k_sink,
+                               int sink_dtype, float softmax_scale, void* stream);
+size_t zs_gated_attention_backward_workspace(int B, int S, int H, int hd, int gated);
+int zs_gated_attention_backward(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse,
+                                const void* gate_logits, int64_t ldg, void* dq, int64_t lddq, void* dk, int64_t lddk,
+                                void* dv, int64_t lddv, void* dgate_logits, int64_t lddg, int gate_pad, float* D,
+                                int B, int S, int H, int Hkv, int hd, int window, const int* seg_start,
+                                const void* k_sink, int sink_dtype, float* ds_sink, float softmax_scale,
+                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------ cross entropy (a16-a18) */
 
@@ -439,7 +508,9 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  * effective gain is softplus(scalar) * softplus(row) * softplus(col)).
  *
  * zs_muonmd_pre:  buf = lerp(buf, g*G, 1 - momentum);
- *                 x_out (bf16 [L, m, n]) = lerp(g*G, buf, momentum);
+ *                 x_out (bf16 [L, m, n], or [L, n, m] when x_transposed: the
+ *                 layout Newton-Schulz runs a tall stack in) = lerp(g*G, buf,
+ *                 momentum);
  *                 red_* = the gain-gradient reductions of (W/g)*G times the
  *                 other gains over the axes each gain does not span (red_*
  *                 f32, same shapes as the gains, overwritten; NULL exactly
@@ -447,7 +518,8 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  *                 partial sums in a fixed order (no atomics): results are
  *                 bit-identical from run to run.  Workspace (only when a
  *                 gain is present): zs_muonmd_pre_workspace bytes.
- * zs_muonmd_post: with U the orthogonalised update (bf16 [L, m, n]):
+ * zs_muonmd_post: with U the orthogonalised update (bf16 [L, m, n], or
+ *                 [L, n, m] when u_transposed):
  *                 W' = W/g - lr * rescale * U, projected to target_norm
  *                 per matrix (norm_axis 0, target [L]), row (1, [L, m]) or
  *                 column (2, [L, n]); gain Adam (betas b1, b2, eps, step from
@@ -459,15 +531,48 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  */
 size_t zs_muonmd_pre_workspace(int64_t L, int64_t m, int64_t n);
 int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_scalar, const float* g_row,
-                  const float* g_col, void* x_out, float* red_scalar, float* red_row, float* red_col, int64_t L,
-                  int64_t m, int64_t n, float momentum, void* workspace, size_t workspace_bytes, void* stream);
+                  const float* g_col, void* x_out, int x_transposed, float* red_scalar, float* red_row,
+                  float* red_col, int64_t L, int64_t m, int64_t n, float momentum, void* workspace,
+                  size_t workspace_bytes, void* stream);
 size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n);
-int zs_muonmd_post(const float* W, const void* U, void* p_out, int p_dtype, float* g_scalar, float* g_row,
-                   float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row, float* m1_col,
-                   float* m2_col, const float* red_scalar, const float* red_row, const float* red_col,
+int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype, float* g_scalar,
+                   float* g_row, float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
+                   float* m1_col, float* m2_col, const float* red_scalar, const float* red_row, const float* red_col,
                    const float* step_dev, float step_host, float b1, float b2, float eps, float gain_lr,
                    const float* lr_dev, float lr_host, float rescale, int norm_axis, const float* target_norm,
                    int64_t L, int64_t m, int64_t n, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------ AdamW step (a23) */
+
+/*
+ * The aux-Adam groups of SingleDeviceMuonMDWithAuxAdam (optimizer/muon.py:
+ * 616-650, adam_update :131-136) over a list of f32 parameters in one launch:
+ *   m1 = lerp(m1, g, 1-b1); m2 = lerp(m2, g*g, 1-b2);
+ *   u  = (m1 / (1 - b1^t)) / (sqrt(m2 / (1 - b2^t)) + eps);
+ *   p  = p * (1 - lr*wd) - lr * u;   shadow_bf16 (optional) = bf16(p).
+ * Per tensor: step_dev (f32 device scalar, already incremented for this step)
+ * or, when NULL, the host step given as the f32 reciprocals of its bias
+ * corrections (inv_bc*_host = 1 / (1 - b^t) computed in double).  lr from
+ * lr_dev (f32 device scalar; decay = 1 - lr*wd in f32) or lr_host with
+ * decay_host.  one_minus_b* are the lerp weights as the host computes them.
+ * p, g, m1, m2 contiguous, n elements each; any number of tensors (launched
+ * 96 per kernel).
+ */
+typedef struct {
+  float* p;
+  const float* g;
+  float* m1;
+  float* m2;
+  const float* step_dev;
+  float inv_bc1_host;
+  float inv_bc2_host;
+  void* shadow_bf16;
+  int64_t n;
+} zs_adamw_tensor;
+
+int zs_adamw_step(const zs_adamw_tensor* tensors, int count, const float* lr_dev, float lr_host, float decay_host,
+                  float b1, float b2, double one_minus_b1, double one_minus_b2, float eps, float weight_decay,
+                  void* stream);
 
 /*
  * Data-parallel all-reduce over NVLink peer memory with the copy engines (no

@@ -131,3 +131,117 @@ def test_attention_rejects_unsupported():
         attention(q, q, q)
     with pytest.raises(Z.ZsError):
         attention(q.cpu(), q.cpu(), q.cpu())
+
+
+GATED_CASES = [
+    # hidden, H, Hkv, window, packed, sink, pos_rope_dims
+    (256, 4, 4, None, False, False, 32),
+    (1536, 12, 4, None, False, True, 16),
+    (512, 4, 2, 64, True, False, 16),
+    (768, 6, 2, None, True, True, 128),
+]
+
+
+@pytest.mark.parametrize("case", GATED_CASES, ids=lambda c: "-".join(str(x) for x in c))
+def test_fused_gated_attention_core_matches_stepwise_path(case):
+    """GatedAttention's fused core (q/k norm + RoPE kernel, attention reading v and the gate
+    logits in place with the sigmoid gate in its epilogue, the backward writing the
+    projection's gradient) against the same module's step-by-step path (split, norms, RoPE,
+    attention, torch gate): output, input gradient and every parameter gradient."""
+    from modeling.attention import GatedAttention
+    from modeling.model_config import ModelConfig
+    from zs_b200 import _lib as Z
+
+    hidden, H, Hkv, window, packed, sink, prd = case
+    B, S = 2, 384
+    cfg = ModelConfig(vocab_size=256, embed_size=hidden, hidden_size=hidden, transformer_depth=1,
+                      intermediate_size=64, n_experts=3, n_shared_experts=1, n_experts_per_token=1,
+                      n_attention_heads=H, n_key_value_heads=Hkv, attention_window_pattern=(window,),
+                      max_position_embeddings=S, sequence_length=S, pos_rope_dims=prd, attention_sink=sink)
+    torch.manual_seed(hidden + H)
+    m = GatedAttention(cfg, window_size=window).cuda()
+    with torch.no_grad():
+        m.q_norm.weight.normal_(0, 0.1)
+        m.k_norm.weight.normal_(0, 0.1)
+        m.head_gate_proj.weight.normal_(0, 0.2)
+    x = torch.randn(B, S, hidden, device="cuda")
+    cu, unpad = None, None
+    if packed:
+        lens = [100, 150, 84, 200, 40]   # two rows: 100+150+84 = 334 (+50 pad), 200+40 = 240 (+144 pad)
+        starts = [0, 100, 250, S, S + 200]
+        unpad = torch.cat([torch.arange(s, s + n) for s, n in zip(starts, lens)]).cuda()
+        cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32, device="cuda")
+    dy = torch.randn(B, S, hidden, device="cuda")
+    outs = []
+    for fused in (True, False):
+        m.fused_core = fused
+        m.zero_grad(set_to_none=True)
+        xi = x.clone().requires_grad_(True)
+        Z.clear_device_error()
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            y = m(xi, cu_seqlens=cu, unpad_indices=unpad, max_seqlen=None)
+        y.float().backward(dy)
+        torch.cuda.synchronize()
+        assert Z.device_error() == 0
+        outs.append((y.float(), xi.grad, {n: p.grad.float() for n, p in m.named_parameters() if p.grad is not None}))
+    (yf, gxf, gpf), (ys, gxs, gps) = outs
+    if packed:   # padding positions are not attended to by anything; compare real tokens
+        yf, ys = yf.reshape(-1, hidden)[unpad], ys.reshape(-1, hidden)[unpad]
+    assert rel_err(yf, ys) < 2e-2 and cosine(yf, ys) > 0.9995
+    assert rel_err(gxf, gxs) < 3e-2 and cosine(gxf, gxs) > 0.999
+    assert set(gpf) == set(gps)
+    for n in gps:
+        assert cosine(gpf[n], gps[n]) > 0.999 and rel_err(gpf[n], gps[n]) < 3e-2, n
+
+
+def test_fused_gated_attention_core_matches_f32_torch():
+    """The fused core against an f32 PyTorch restatement of GatedAttention between its
+    projections: per-head zero-centred RMSNorm of q and k, partial rotate-half RoPE, causal
+    GQA softmax attention, o * sigmoid(gate logits)."""
+    from zs_b200.attn import gated_attention_core
+
+    torch.manual_seed(3)
+    B, S, H, Hkv, hd, rp = 2, 512, 8, 2, 128, 8
+    pad = -((H + 2 * Hkv) * hd + H) % 16
+    qkvg = (torch.randn(B, S, (H + 2 * Hkv) * hd + H + pad, device="cuda")).bfloat16()
+    qkvg[..., (H + 2 * Hkv) * hd + H:] = 0
+    qkvg.requires_grad_(True)
+    wq = (torch.randn(hd, device="cuda") * 0.1).requires_grad_(True)
+    wk = (torch.randn(hd, device="cuda") * 0.1).requires_grad_(True)
+    inv = 1.0 / (10000 ** (torch.arange(0, 2 * rp, 2, device="cuda").float() / (2 * rp)))
+    ang = torch.outer(torch.arange(S, device="cuda").float(), inv)
+    cos, sin = ang.cos()[None], ang.sin()[None]
+    o = gated_attention_core(qkvg, wq, wk, n_heads=H, n_kv_heads=Hkv, head_dim=hd, cos=cos, sin=sin, rot_pairs=rp,
+                             eps=1e-6, pad=pad)
+    do = torch.randn_like(o)
+    o.backward(do)
+
+    xr = qkvg.detach().float().requires_grad_(True)
+    wqr, wkr = wq.detach().clone().requires_grad_(True), wk.detach().clone().requires_grad_(True)
+    q = xr[..., : H * hd].reshape(B, S, H, hd)
+    k = xr[..., H * hd:(H + Hkv) * hd].reshape(B, S, Hkv, hd)
+    v = xr[..., (H + Hkv) * hd:(H + 2 * Hkv) * hd].reshape(B, S, Hkv, hd)
+    gl = xr[..., (H + 2 * Hkv) * hd:(H + 2 * Hkv) * hd + H]
+
+    def norm(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * (1 + w)
+
+    def rope(t):
+        c, s_ = cos[:, :, None, :], sin[:, :, None, :]
+        x1, x2 = t[..., :rp], t[..., hd // 2: hd // 2 + rp]
+        out = t.clone()
+        out[..., :rp] = x1 * c - x2 * s_
+        out[..., hd // 2: hd // 2 + rp] = x2 * c + x1 * s_
+        return out
+
+    qn, kn = rope(norm(q, wqr)), rope(norm(k, wkr))
+    a = F.scaled_dot_product_attention(qn.transpose(1, 2), kn.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                       enable_gqa=True).transpose(1, 2)
+    ref = (a * torch.sigmoid(gl)[..., None]).reshape(B, S, H * hd)
+    ref.backward(do.float())
+    assert rel_err(o, ref) < 1e-2 and cosine(o, ref) > 0.9995
+    W = (H + 2 * Hkv) * hd + H
+    assert rel_err(qkvg.grad[..., :W], xr.grad[..., :W]) < 3e-2 and cosine(qkvg.grad[..., :W], xr.grad[..., :W]) > 0.999
+    assert torch.all(qkvg.grad[..., W:] == 0)
+    for a_, b_ in ((wq.grad, wqr.grad), (wk.grad, wkr.grad)):
+        assert cosine(a_, b_) > 0.999 and rel_err(a_, b_) < 3e-2

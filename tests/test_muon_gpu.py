@@ -207,18 +207,21 @@ def test_fused_md_step_bf16_param_and_float_lr():
 
 
 def test_batched_optimizer_matches_per_parameter_steps():
-    """SingleDeviceMuonMDWithAuxAdam batches Newton-Schulz across same-shape matrices;
-    the result equals stepping each parameter alone."""
+    """SingleDeviceMuonMDWithAuxAdam batches Newton-Schulz across same-shape matrices,
+    writing each parameter's input into its slice of the batch (transposed for a tall
+    stack, partial 64 x 256 tiles included) and reading the update back from there; the
+    result equals stepping each parameter alone."""
     from optimizer.muon import SingleDeviceMuonMDWithAuxAdam, md_decoupled_step
 
     gen = torch.Generator(device="cuda").manual_seed(3)
-    shapes = [(256, 512), (256, 512), (512, 256), (4, 256, 512), (64, 512), (12, 128), (12, 128), (40, 33)]
+    shapes = [(256, 512), (256, 512), (512, 256), (4, 256, 512), (64, 512), (12, 128), (200, 72), (3, 96, 40),
+              (2, 72, 200), (12, 128), (40, 33), (3, 200, 72)]
     ps = [torch.nn.Parameter(torch.randn(*s, device="cuda", generator=gen) * 0.05) for s in shapes]
     ref = [p.detach().clone() for p in ps]
     lr = torch.tensor(0.02, device="cuda")
     opt = SingleDeviceMuonMDWithAuxAdam([
-        dict(params=ps[:6], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, capturable=True),
-        dict(params=ps[6:], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, norm_axis="row", gain_mode="col",
+        dict(params=ps[:9], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, capturable=True),
+        dict(params=ps[9:], use_muon=True, lr=lr, momentum=0.95, gain_lr=1e-3, norm_axis="row", gain_mode="col",
              rescale_mode="muon", capturable=True)])
     states = [{} for _ in ps]
     for _ in range(2):
@@ -227,7 +230,7 @@ def test_batched_optimizer_matches_per_parameter_steps():
             p.grad = g
         opt.step()
         for i, (r, g) in enumerate(zip(ref, gs)):
-            group = opt.param_groups[0] if i < 6 else opt.param_groups[1]
+            group = opt.param_groups[0] if i < 9 else opt.param_groups[1]
             md_decoupled_step(r, g, states[i], lr=lr, momentum=0.95, gain_lr=1e-3, gain_betas=group["gain_betas"],
                               gain_eps=group["gain_eps"], gain_mode=group["gain_mode"], norm_axis=group["norm_axis"],
                               ns_steps=5, capturable=True, rescale_mode=group["rescale_mode"])
