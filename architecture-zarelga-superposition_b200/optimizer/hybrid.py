@@ -69,8 +69,37 @@ class HybridGraphOptimizer:
         self._drop_sparse_graphs()
 
     def zero_grad(self, set_to_none=False):
-        self.dense.zero_grad(set_to_none=set_to_none)
+        """Dense gradients keep their buffers (set_to_none=False) so the recorded step reads
+        the same memory every replay; they are zeroed in one multi-tensor launch, except the
+        gradients whose producer overwrites them (parameters flagged `_zs_grad_overwrite`:
+        the expert weight gradients written straight from the weight-gradient GEMMs, see
+        zs_b200.train.enable_fused_weight_grad), which are only marked stale.  A stale
+        gradient that no backward wrote is zeroed before the step.  The sparse COO gradient
+        is always dropped."""
+        if set_to_none:
+            self.dense.zero_grad(set_to_none=True)
+        else:
+            fills = []
+            for g in self.dense.param_groups:
+                for p in g["params"]:
+                    if p.grad is None:
+                        continue
+                    if getattr(p, "_zs_grad_overwrite", False) and not p.grad.is_sparse:
+                        p._zs_grad_stale = True
+                    else:
+                        if p.grad.grad_fn is not None:
+                            p.grad.detach_()
+                        fills.append(p.grad)
+            if fills:
+                torch._foreach_zero_(fills)
         self.sparse.zero_grad(set_to_none=True)
+
+    def _zero_stale(self):
+        for g in self.dense.param_groups:
+            for p in g["params"]:
+                if getattr(p, "_zs_grad_stale", False):
+                    p.grad.zero_()
+                    p._zs_grad_stale = False
 
     # ------------------------------------------------------------------------- step
     def _graphs_on(self):
@@ -97,6 +126,7 @@ class HybridGraphOptimizer:
 
     @torch.no_grad()
     def step(self, closure=None):
+        self._zero_stale()
         graphed = self._graphs_on() and self._dense_steps >= self.capture_warmup_steps
         if graphed:
             if self._dense_graph is None:

@@ -81,8 +81,10 @@ def swiglu_backward(dact, hfull):
 def accumulate_weight_grad(W, DY, X, offs, tag):
     """W.grad (W's [E, N, K] layout) += DY_e^T X_e per expert, straight from the GEMM epilogue:
     f32 weights accumulate in f32; 16-bit weights get their gradient written in their dtype
-    (added to an existing .grad).  W.grad is created when absent.  Data-parallel reducers
-    registered for W are told the gradient is complete (zs_b200.dp.notify_grad_ready)."""
+    (added to an existing .grad).  W.grad is created when absent, and overwritten instead of
+    accumulated when an optimizer's zero_grad marked it stale (W._zs_grad_stale, see
+    optimizer.hybrid.HybridGraphOptimizer.zero_grad).  Data-parallel reducers registered for
+    W are told the gradient is complete (zs_b200.dp.notify_grad_ready)."""
     from zs_b200.dp import notify_grad_ready
 
     E, N, K = W.shape
@@ -95,6 +97,9 @@ def accumulate_weight_grad(W, DY, X, offs, tag):
         if g is None:
             g = W.grad = torch.empty_like(W, memory_format=torch.contiguous_format)
             acc = 0
+        elif getattr(W, "_zs_grad_stale", False):
+            acc = 0   # zero_grad left this buffer stale: the GEMM overwrites it
+        W._zs_grad_stale = False
         with Z.timed(tag, 2.0 * X.size(0) * K * N):
             Z.check(Z.lib().zs_group_xty_f32(E, g.data_ptr(), N * K, 1, K, DY.data_ptr(), DY.stride(0),
                                              X.data_ptr(), X.stride(0), X.size(0), K, N, offs.data_ptr(),

@@ -67,17 +67,43 @@ def _product(x2, W3, tag):
     return y
 
 
+_SPLITS = {}
+
+
+def _split_offsets(T: int, S: int, device):
+    """Inclusive row boundaries of S near-equal chunks of T rows (64-row multiples), cached."""
+    key = (T, S, str(device))
+    r = _SPLITS.get(key)
+    if r is None:
+        step = -(-T // S)
+        step = -(-step // 64) * 64
+        r = torch.tensor([min(T, (i + 1) * step) for i in range(S)], dtype=torch.int64, device=device)
+        if len(_SPLITS) > 32:
+            _SPLITS.clear()
+        _SPLITS[key] = r
+    return r
+
+
 def _weight_grad(dy2, x2, N, K, tag):
-    """f32 [N, K] = dy2^T x2 in one launch."""
+    """f32 [N, K] = dy2^T x2.  The product's 128 x 256 output tiles are too few to fill the
+    GPU for the small projections (a 1536 x 768 weight is 36 tiles for 148 SMs), so the T
+    rows are split into S chunks computed as S groups of one grouped launch into f32
+    partials, which are then summed in a fixed order."""
     T = x2.size(0)
-    _, _, offs = one_group_routing(T, x2.device)
-    g = torch.empty((N, K), dtype=torch.float32, device=x2.device)
+    tiles = -(-N // 128) * -(-K // 256)
+    S = max(1, min(8, 148 // tiles, T // 1024))
     Z.count(1)
+    if S == 1:
+        _, _, offs = one_group_routing(T, x2.device)
+        g = torch.empty((N, K), dtype=torch.float32, device=x2.device)
+    else:
+        offs = _split_offsets(T, S, x2.device)
+        g = torch.empty((S, N, K), dtype=torch.float32, device=x2.device)
     with Z.timed(tag, 2.0 * T * N * K):
-        Z.check(Z.lib().zs_group_xty_f32(1, g.data_ptr(), N * K, 1, K, dy2.data_ptr(), dy2.stride(0), x2.data_ptr(),
+        Z.check(Z.lib().zs_group_xty_f32(S, g.data_ptr(), N * K, 1, K, dy2.data_ptr(), dy2.stride(0), x2.data_ptr(),
                                          x2.stride(0), T, K, N, offs.data_ptr(), Z.dtype_code(x2.dtype), 0,
                                          Z.stream_of(x2)), "zs_group_xty_f32")
-    return g
+    return g if S == 1 else g.sum(0)
 
 
 class DenseLinearFunction(torch.autograd.Function):

@@ -59,6 +59,10 @@ def enable_fused_weight_grad(model, enabled=True):
     for m in model.modules():
         if isinstance(m, GLUMLP):
             m.fuse_weight_grad = bool(enabled)
+            # the GEMMs can overwrite a stale gradient: HybridGraphOptimizer.zero_grad skips
+            # the fill of these buffers
+            for w in (m.experts.weight, m.output_experts.weight):
+                w._zs_grad_overwrite = bool(enabled)
             n += 1
     return n
 

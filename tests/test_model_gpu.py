@@ -87,3 +87,41 @@ def test_fused_add_norm_block_matches_reference_op_sequence():
     assert ga.keys() == gb.keys()
     for n in ga:
         assert cos(ga[n], gb[n]) > 0.999, n
+
+
+def test_lazy_zero_grad_of_fused_expert_gradients_matches_filled_buffers():
+    """HybridGraphOptimizer.zero_grad marks the expert weight gradients that the weight-
+    gradient GEMMs write directly as stale instead of filling them, and the GEMMs overwrite
+    them: three full training steps (eager, then graph-replayed optimizer) leave every
+    parameter bit-identical to the run whose buffers are zero-filled and accumulated into."""
+    from cut_cross_entropy import linear_cross_entropy
+    from zs_b200.train import build_muonmd_optimizer, build_next_token_loss_inputs, enable_fused_weight_grad
+
+    runs = []
+    for lazy in (True, False):
+        cfg, m = _tiny()
+        enable_fused_weight_grad(m)
+        if not lazy:
+            for mod in m.modules():
+                for w in (getattr(getattr(mod, "experts", None), "weight", None),
+                          getattr(getattr(mod, "output_experts", None), "weight", None)):
+                    if w is not None:
+                        w._zs_grad_overwrite = False
+        opt = build_muonmd_optimizer(m, torch.device("cuda"), capture_warmup_steps=1)
+        g = torch.Generator(device="cuda").manual_seed(9)
+        for _ in range(3):
+            ids = torch.randint(0, cfg.vocab_size, (2, 256), device="cuda", generator=g)
+            mask = torch.ones_like(ids)
+            opt.zero_grad(set_to_none=False)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                h, _ = m.headless_forward(ids)
+                e, t = build_next_token_loss_inputs(h, ids, mask)
+                loss = linear_cross_entropy(e, m.get_classifier_weights(), t, ignore_index=-100)
+            loss.backward()
+            opt.step()
+        torch.cuda.synchronize()
+        runs.append({n: p.detach().clone() for n, p in m.named_parameters()})
+        stale = [n for n, p in m.named_parameters() if getattr(p, "_zs_grad_stale", False)]
+        assert not stale, stale
+    for n in runs[0]:
+        assert torch.equal(runs[0][n], runs[1][n]), n
