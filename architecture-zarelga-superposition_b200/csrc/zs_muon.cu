@@ -531,6 +531,7 @@ struct WriteArgs {
   const float* sp_old[3];  // null when the gain is absent
   const float* sp_new[3];
   const float* proj;
+  __nv_bfloat16* shadow;   // nullable: a bf16 copy of the new weights in p's layout (f32 p only)
 };
 
 template <bool VEC, bool TRANS, typename TP>
@@ -617,6 +618,7 @@ __global__ void __launch_bounds__(THREADS, 2) md_write_kernel(PostArgs a, WriteA
     }
     if constexpr (std::is_same<TP, float>::value) {
       store8<VEC>(p + off, c, n, o);
+      if (wa.shadow != nullptr) store8_bf16<VEC>(wa.shadow + off, c, n, o);
     } else {
       store8_bf16<VEC>(p + off, c, n, o);
     }
@@ -715,7 +717,8 @@ extern "C" size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n) {
   return (size_t)(2 * L * mx + 2 * (L + L * m + L * n) + md_partial_floats(L, m, n)) * sizeof(float) + 8 * 256;
 }
 
-extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype, float* g_scalar, float* g_row,
+extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype,
+                              void* shadow_bf16, float* g_scalar, float* g_row,
                               float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
                               float* m1_col, float* m2_col, const float* red_scalar, const float* red_row,
                               const float* red_col, const float* step_dev, float step_host, float b1, float b2,
@@ -725,6 +728,7 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, v
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   ZS_REQUIRE(W && U && p_out && target_norm, ZS_ERR_ARG);
   ZS_REQUIRE(p_dtype == ZS_F32 || p_dtype == ZS_BF16, ZS_ERR_DTYPE);
+  ZS_REQUIRE(shadow_bf16 == nullptr || p_dtype == ZS_F32, ZS_ERR_ARG);
   ZS_REQUIRE(norm_axis >= 0 && norm_axis <= 2, ZS_ERR_ARG);
   ZS_REQUIRE(L >= 1 && m >= 1 && n >= 1 && L < 65536 && (m + md::TR - 1) / md::TR < 65536, ZS_ERR_SHAPE);
   ZS_REQUIRE((g_scalar == nullptr || (m1_scalar && m2_scalar && red_scalar)) &&
@@ -746,7 +750,7 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, v
                  m % 2 == 0 && (reinterpret_cast<uintptr_t>(U) & 3) == 0};
   md::Gains g{g_scalar, g_row, g_col};
   const dim3 grid = md_grid(L, m, n);
-  const bool vec = u_transposed ? md_vec_ok(n, {W, p_out}) : md_vec_ok(n, {W, U, p_out});
+  const bool vec = u_transposed ? md_vec_ok(n, {W, p_out, shadow_bf16}) : md_vec_ok(n, {W, U, p_out, shadow_bf16});
   // the vectorised passes stage their rows in dynamic shared memory (md::Stage)
   auto reduce = [&](auto kern, int dyn) -> int {
     if (dyn > 0) ZS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
@@ -795,6 +799,7 @@ extern "C" int zs_muonmd_post(const float* W, const void* U, int u_transposed, v
   ga.proj = proj;
   ga.n_proj = n_proj;
   wa.proj = proj;
+  wa.shadow = reinterpret_cast<__nv_bfloat16*>(shadow_bf16);
   const int64_t work = n_proj > L * (1 + m + n) ? n_proj : L * (1 + m + n);
   int64_t blocks = (work + 255) / 256;
   if (blocks > 148 * 4) blocks = 148 * 4;

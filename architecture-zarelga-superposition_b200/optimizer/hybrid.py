@@ -32,6 +32,8 @@ from collections import OrderedDict
 
 import torch
 
+from zs_b200 import shadow
+
 
 class HybridGraphOptimizer:
     max_sparse_graphs = 4
@@ -43,6 +45,7 @@ class HybridGraphOptimizer:
         self.enable_cuda_graph = bool(enable_cuda_graph)
         self._dense_steps = 0
         self._dense_graph = None
+        self._dense_gen = -1
         self._sparse_graphs = OrderedDict()
 
     # ---------------------------------------------------------- torch.optim surface
@@ -129,7 +132,11 @@ class HybridGraphOptimizer:
         self._zero_stale()
         graphed = self._graphs_on() and self._dense_steps >= self.capture_warmup_steps
         if graphed:
+            # a bf16 weight shadow allocated after the recording is not written by it
+            if self._dense_graph is not None and self._dense_gen != shadow.GEN:
+                self._dense_graph = None
             if self._dense_graph is None:
+                self._dense_gen = shadow.GEN
                 self._dense_graph = self._record(self.dense.step)
             self._dense_graph.replay()
         else:

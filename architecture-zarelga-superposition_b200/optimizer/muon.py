@@ -20,6 +20,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from zs_b200 import _lib as Z
+from zs_b200.shadow import shadow_ptr
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
 _RAW_GAIN_INIT = 0.5413248546129181  # softplus^-1(1): every gain starts at exactly 1
@@ -228,10 +229,12 @@ def _md_post(p, W, red, U, state, *, lr, gain_lr, gain_betas, gain_eps, norm_axi
     direct = p.is_contiguous() and p.dtype in (torch.float32, torch.bfloat16)
     out = p if direct else W
     ws = torch.empty(int(Z.lib().zs_muonmd_post_workspace(L, m, n)), dtype=torch.uint8, device=W.device)
+    # the bf16 copy the forward GEMMs read is written with the new weights (zs_b200.shadow)
+    sh_ptr = shadow_ptr(p) if (direct and out.dtype == torch.float32) else None
     g = lambda k: state.get(k)  # noqa: E731
     Z.count(4)
     Z.check(Z.lib().zs_muonmd_post(
-        W.data_ptr(), U.data_ptr(), int(bool(u_trans)), out.data_ptr(), Z.dtype_code(out.dtype),
+        W.data_ptr(), U.data_ptr(), int(bool(u_trans)), out.data_ptr(), Z.dtype_code(out.dtype), sh_ptr,
         Z.ptr(g("g_scalar")), Z.ptr(g("g_row")), Z.ptr(g("g_col")),
         Z.ptr(g("g_scalar_m1")), Z.ptr(g("g_scalar_m2")), Z.ptr(g("g_row_m1")), Z.ptr(g("g_row_m2")),
         Z.ptr(g("g_col_m1")), Z.ptr(g("g_col_m2")),
@@ -439,7 +442,7 @@ def _adamw_fused(group, params, states):
             # torch divides by a Python scalar as a product with its f32 reciprocal
             d.inv_bc1_host = float(np.float32(1.0) / np.float32(1 - b1 ** st["step"]))
             d.inv_bc2_host = float(np.float32(1.0) / np.float32(1 - b2 ** st["step"]))
-        d.shadow_bf16 = None
+        d.shadow_bf16 = shadow_ptr(p)
         d.n = p.numel()
         descs.append(d)
     arr = (Z.AdamWTensor * len(descs))(*descs)

@@ -18,6 +18,7 @@ import torch
 from torch import nn
 
 from zs_b200 import _lib as Z
+from zs_b200.shadow import bf16_shadow
 from .kernels import ops
 from .parallel_experts import ParallelExperts, flatten_sort_count
 
@@ -128,8 +129,10 @@ class GLUExpertsFunction(torch.autograd.Function):
         Z.require_cuda(x, expert_p, expert_idxs, W1, W2, shared, residual)
         cdt = _compute_dtype(x)
         xc = x.to(cdt).contiguous()
-        W1c = W1.to(cdt).contiguous()
-        W2c = W2.to(cdt).contiguous()
+        # f32 master weights are read through their bf16 shadows (zs_b200.shadow): cast once,
+        # then kept in step by the optimizer instead of re-cast every forward
+        W1c = bf16_shadow(W1) if cdt == torch.bfloat16 else W1.to(cdt).contiguous()
+        W2c = bf16_shadow(W2) if cdt == torch.bfloat16 else W2.to(cdt).contiguous()
         pc = expert_p.to(cdt).contiguous()
         T = xc.size(0)
         sei, ssi, offs = flatten_sort_count(expert_idxs, num_experts)

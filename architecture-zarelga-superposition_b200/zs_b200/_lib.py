@@ -94,7 +94,7 @@ _SIGNATURES = {
                                            _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32,
                                            _i32, _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp, _sz, _vp]),
     "zs_moe_combine": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
-    "zs_muonmd_post": (_i32, [_vp, _vp, _i32, _vp, _i32] + [_vp] * 12 + [_vp, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
+    "zs_muonmd_post": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp] + [_vp] * 12 + [_vp, _f32, _f32, _f32, _f32, _f32, _vp, _f32,
                                                                   _f32, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "zs_newton_schulz5_workspace": (_sz, [_i64, _i64, _i64, _i32]),
     "zs_newton_schulz5": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _f32, _f32, _f32, _vp, _sz, _i32, _vp]),

@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib as Z
+from .shadow import bf16_shadow, concat_shadow
 
 _ROUTES = {}
 
@@ -44,15 +45,19 @@ def _bf16(t):
     return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
 
 
+def _w16(w):
+    """A weight in bf16: its persistent shadow when it is an f32 parameter."""
+    return w if w.dtype == torch.bfloat16 else bf16_shadow(w).contiguous()
+
+
 def _rows(x):
     return _bf16(x).reshape(-1, x.size(-1)).contiguous()
 
 
 def _weight_cat(weights, pad):
-    ws = [_bf16(w) for w in weights]
-    if pad:
-        ws.append(ws[0].new_zeros(pad, ws[0].size(1)))
-    return ws[0].contiguous() if len(ws) == 1 else torch.cat(ws, 0)
+    """bf16 row-concatenation of the weights plus `pad` zero rows: the persistent shadow buffer
+    of f32 parameters (zs_b200.shadow, no per-step cast or cat), else a fresh cast/cat."""
+    return concat_shadow(weights, pad)
 
 
 def _product(x2, W3, tag):
@@ -170,8 +175,8 @@ class DenseSwiGLUFunction(torch.autograd.Function):
         T = x2.size(0)
         f = w_up.size(0)
         sei, ssi, offs = one_group_routing(T, x2.device)
-        W1 = torch.cat([_bf16(w_up), _bf16(w_gate)], 0).unsqueeze(0)      # [1, 2f, d]: up rows, then gate rows
-        W2 = _bf16(w_down).contiguous().unsqueeze(0)                      # [1, d, f]
+        W1 = concat_shadow([w_up, w_gate]).unsqueeze(0)                  # [1, 2f, d]: up rows, then gate rows
+        W2 = _w16(w_down).unsqueeze(0)                                    # [1, d, f]
         act, hfull = up_swiglu(x2, W1, sei, offs)
         y = torch.empty((T, W2.size(1)), dtype=torch.bfloat16, device=x2.device)
         ops._launch_scatter2scatter(y, W2.permute(0, 2, 1), act, 1, sei, ssi, None, True, True,

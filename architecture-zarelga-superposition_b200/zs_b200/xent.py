@@ -5,6 +5,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib as Z
+from .shadow import bf16_shadow
 
 DEFAULT_V_CHUNK = 16384
 
@@ -18,7 +19,7 @@ class FusedLinearCrossEntropy(torch.autograd.Function):
         Z.require_cuda(hidden, classifier, labels, s_count)
         cdt = hidden.dtype if hidden.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
         h = hidden.to(cdt).contiguous()
-        c = classifier.to(cdt).contiguous()
+        c = bf16_shadow(classifier) if cdt == torch.bfloat16 else classifier.to(cdt).contiguous()
         lab = labels.to(torch.int64).contiguous()
         sc = s_count.to(torch.int32).contiguous()
         T, D = h.shape

@@ -526,7 +526,10 @@ int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int64_t m, int6
  *                 step_dev (f32 device scalar, already incremented) or
  *                 step_host) on dL/draw = red * sigmoid(raw), raw -= gain_lr
  *                 * update; p_out (f32 or bf16 by p_dtype, may alias W) =
- *                 g_new * W'.  lr from lr_dev (f32 device scalar) or lr_host.
+ *                 g_new * W', and with shadow_bf16 (f32 p_out only) the same
+ *                 values in bf16 in p_out's layout (the weight copy the next
+ *                 forward's GEMMs read).  lr from lr_dev (f32 device scalar)
+ *                 or lr_host.
  *                 Workspace: zs_muonmd_post_workspace bytes.
  */
 size_t zs_muonmd_pre_workspace(int64_t L, int64_t m, int64_t n);
@@ -535,8 +538,8 @@ int zs_muonmd_pre(const float* W, const float* G, float* buf, const float* g_sca
                   float* red_col, int64_t L, int64_t m, int64_t n, float momentum, void* workspace,
                   size_t workspace_bytes, void* stream);
 size_t zs_muonmd_post_workspace(int64_t L, int64_t m, int64_t n);
-int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype, float* g_scalar,
-                   float* g_row, float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
+int zs_muonmd_post(const float* W, const void* U, int u_transposed, void* p_out, int p_dtype, void* shadow_bf16,
+                   float* g_scalar, float* g_row, float* g_col, float* m1_scalar, float* m2_scalar, float* m1_row, float* m2_row,
                    float* m1_col, float* m2_col, const float* red_scalar, const float* red_row, const float* red_col,
                    const float* step_dev, float step_host, float b1, float b2, float eps, float gain_lr,
                    const float* lr_dev, float lr_host, float rescale, int norm_axis, const float* target_norm,
