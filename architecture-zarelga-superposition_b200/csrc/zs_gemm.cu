@@ -86,6 +86,8 @@ struct GemmArgs {
   int sym_upper;                       // uniform square groups (pair tiles): the product is symmetric,
                                        // only tiles (i, j >= i) are computed, strictly-upper ones also
                                        // write their transpose (EPI_STORE / EPI_AXPBY)
+  int tma_store;                       // EPI_STORE / EPI_AXPBY without row_map or bias: full 32 x 32
+                                       // chunks go out through the third tensor map (TMA stores)
 };
 
 template <int BN, int STAGES, bool PAIR = false>
@@ -101,7 +103,8 @@ struct Smem {
   static constexpr int OFF_TPREFIX = OFF_MISC + 16;
   static constexpr int OFF_RSTART = OFF_TPREFIX + (MAX_EXPERTS_GEMM + 1) * 4;
   static constexpr int OFF_ORDER = OFF_RSTART + (MAX_EXPERTS_GEMM + 1) * 4;
-  static constexpr int OFF_STG = ((OFF_ORDER + (MAX_EXPERTS_GEMM + 1) * 4 + 15) / 16) * 16;
+  // per-warp staging buffers start on 512-byte boundaries (the TMA-store box's swizzle atom)
+  static constexpr int OFF_STG = ((OFF_ORDER + (MAX_EXPERTS_GEMM + 1) * 4 + 1023) / 1024) * 1024;
   static constexpr int TOTAL = OFF_STG + 8 * 32 * 80;
   static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
 };
@@ -280,6 +283,41 @@ __device__ __forceinline__ void emit_packed_mirror(char* out, int64_t ldo, int64
   for (int q = 0; q < 4; ++q) dst[q] = make_uint4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
 }
 
+// One warp's 32 x 32 chunk of 16-bit outputs (lane = row, 16 packed pairs)
+// through its staging buffer to global memory by a TMA store at column c0,
+// row r0 of tmO (box 32 x 32, 64-byte swizzle: 16-byte unit u of buffer row j
+// sits at unit u ^ ((j >> 1) & 3)).  transposed: the chunk's column j becomes
+// buffer row j (the mirror of a symmetric tile).  The buffer is reused only
+// after the previous store from it has been read.
+__device__ __forceinline__ void tma_emit_chunk(const CUtensorMap* tmO, uint8_t* stg, const uint32_t (&p)[16], int c0,
+                                               int r0, bool transposed) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  if (!transposed) {
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ sw) << 4)) =
+          make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+  } else {
+    // value 2i of this lane -> (row 2i, column lane), value 2i+1 -> (row 2i+1, column lane)
+    const int u = lane >> 3, b = (lane & 7) * 2;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int off = ((u ^ (i & 3)) << 4) + b;
+      *reinterpret_cast<uint16_t*>(stg + (2 * i) * 64 + off) = (uint16_t)(p[i] & 0xffffu);
+      *reinterpret_cast<uint16_t*>(stg + (2 * i + 1) * 64 + off) = (uint16_t)(p[i] >> 16);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmO, stg, c0, r0);
+    bulk_commit();
+  }
+}
+
 // Read 32 consecutive 16-bit columns of this lane's row as f32.
 __device__ __forceinline__ void load_chunk(const char* src, int64_t row_off, int col0, int ncols, bool valid,
                                            float (&v)[32], int dtype, bool vec) {
@@ -394,7 +432,7 @@ __device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, i
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
   using L = Smem<BN, STAGES, PAIR>;
   static_assert(!PAIR || !A_MN, "pair tiles are MODE_ROWS only");
   constexpr int TM = PAIR ? 2 * BM : BM;    // rows of a MODE_ROWS tile
@@ -751,6 +789,10 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       if (!warp_wait(&tfull[buf], acc_phase, s_abort, ZS_DEVERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      // this warp's 32 output rows go out by TMA stores when all of them belong to the tile
+      const int crow0 = ti.r0 + (int)crank * BM + quarter * 32;
+      const bool tchunk = (EPI == EPI_STORE || EPI == EPI_AXPBY) && args.mode == MODE_ROWS && args.tma_store &&
+                          vec && crow0 + 32 <= ti.r1;
 
       if (args.mode == MODE_ROWS) {
         if (EPI == EPI_SWIGLU) {
@@ -957,11 +999,21 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             uint32_t pv[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) pv[j] = pack2(v[2 * j], v[2 * j + 1], DT);
-            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            if (tchunk && ncols == 32) {
+              tma_emit_chunk(&tmO, stg, pv, col0, crow0, false);
+            } else {
+              if (args.tma_store && lane == 0) bulk_wait_read_all();   // staging buffer free
+              __syncwarp();
+              emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            }
             if (args.sym_upper && ti.mt < ti.nt) {
               const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;   // first row of this square group
-              emit_packed_mirror(args.out, args.ldo_m, gbase + col0, ti.r0 - gbase + (int)crank * BM + quarter * 32,
-                                 pv, stg);
+              if (tchunk && ncols == 32)
+                tma_emit_chunk(&tmO, stg, pv, (int)(ti.r0 - gbase) + (int)crank * BM + quarter * 32,
+                               (int)(gbase + col0), true);
+              else
+                emit_packed_mirror(args.out, args.ldo_m, gbase + col0,
+                                   ti.r0 - gbase + (int)crank * BM + quarter * 32, pv, stg);
             }
           }
         } else if (EPI == EPI_F32) {
@@ -1008,11 +1060,21 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
             uint32_t pv[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) pv[j] = pack2(v[2 * j], v[2 * j + 1], DT);
-            emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            if (tchunk && ncols == 32) {
+              tma_emit_chunk(&tmO, stg, pv, col0, crow0, false);
+            } else {
+              if (args.tma_store && lane == 0) bulk_wait_read_all();
+              __syncwarp();
+              emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
+            }
             if (args.sym_upper && ti.mt < ti.nt) {
               const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;
-              emit_packed_mirror(args.out, args.ldo_m, gbase + col0, ti.r0 - gbase + (int)crank * BM + quarter * 32,
-                                 pv, stg);
+              if (tchunk && ncols == 32)
+                tma_emit_chunk(&tmO, stg, pv, (int)(ti.r0 - gbase) + (int)crank * BM + quarter * 32,
+                               (int)(gbase + col0), true);
+              else
+                emit_packed_mirror(args.out, args.ldo_m, gbase + col0,
+                                   ti.r0 - gbase + (int)crank * BM + quarter * 32, pv, stg);
             }
           }
         }
@@ -1058,6 +1120,9 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
       }
       ++acc_iter;
     }
+    // the TMA stores issued from this warp's staging buffer have completed
+    if (args.tma_store && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -1093,7 +1158,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D bf16/f16 tensor map with 128-byte swizzle.  inner/outer are the extents
 // in elements/rows, row_bytes the row pitch.
 static int make_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                     uint32_t box_inner, uint32_t box_outer) {
+                     uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return ZS_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return ZS_ERR_ALIGN;
@@ -1104,13 +1170,20 @@ static int make_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t inner
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, dtype == ZS_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     zs_last_cuda_error_ref() = 100000 + (int)r;  // driver result codes, offset
     return ZS_ERR_CUDA;
   }
   return ZS_OK;
+}
+
+// Tensor map of a 16-bit output [rows, cols] (row pitch row_bytes) for the
+// TMA-store epilogue: 32 x 32 boxes, 64-byte swizzle.
+static int make_out_tmap(CUtensorMap* m, const void* base, int dtype, uint64_t cols, uint64_t rows,
+                         uint64_t row_bytes) {
+  return make_tmap(m, base, dtype, cols, rows, row_bytes, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 static int& gemm_cta_limit_ref() {
@@ -1144,8 +1217,8 @@ static bool pair_enabled() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int DT>
-static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
-                       cudaStream_t stream) {
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& args,
+                       int64_t max_tiles, cudaStream_t stream) {
   constexpr int STAGES = 6;
   using L = Smem<BN, STAGES, true>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, DT, true>;
@@ -1187,17 +1260,21 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  ZS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, args));
+  ZS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, args));
   return ZS_OK;
 }
 
+// tmO: the output's tensor map for the TMA-store epilogue (args.tma_store), else unused.
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const CUtensorMap* tmO = nullptr) {
+  const CUtensorMap& tO = tmO != nullptr ? *tmO : tmA;
+  if (args.tma_store && tmO == nullptr) return ZS_ERR_ARG;
   if constexpr (!A_MN) {
     if (args.mode == MODE_ROWS && pair_enabled() && !(args.group_rows > 0 && args.group_rows < 2 * BM)) {
-      return args.out_dtype == ZS_F16 ? launch_pair<BN, A_MN, B_MN, EPI, ZS_F16>(tmA, tmB, args, max_tiles, stream)
-                                      : launch_pair<BN, A_MN, B_MN, EPI, ZS_BF16>(tmA, tmB, args, max_tiles, stream);
+      return args.out_dtype == ZS_F16
+                 ? launch_pair<BN, A_MN, B_MN, EPI, ZS_F16>(tmA, tmB, tO, args, max_tiles, stream)
+                 : launch_pair<BN, A_MN, B_MN, EPI, ZS_BF16>(tmA, tmB, tO, args, max_tiles, stream);
     }
   }
   using L = Smem<BN, STAGES>;
@@ -1210,7 +1287,7 @@ static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
   if (lim > 0 && grid > lim) grid = lim;
   if (max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, args);
+  kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, tO, args);
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
 }
@@ -1306,8 +1383,14 @@ extern "C" int zs_scatter2scatter(void* out, int64_t out_sm, const void* W, int6
   a.b_rows_per_expert = (int)(b_mn ? K : N);
   a.vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && ((out_sm * es) % 16 == 0);
   const int64_t max_tiles = (n / BM + num_experts) * a.n_tiles;
-  if (!b_mn) return launch_gemm<BN, 4, false, false, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
-  return launch_gemm<BN, 4, false, true, EPI_STORE>(tmA, tmB, a, max_tiles, stream);
+  // grouped output rows without a bias: full chunks go out by TMA stores
+  CUtensorMap tmO;
+  if (y_grouped && bias == nullptr && a.vec_ok &&
+      make_out_tmap(&tmO, out, dtype, (uint64_t)N, (uint64_t)n, (uint64_t)out_sm * es) == ZS_OK)
+    a.tma_store = 1;
+  const CUtensorMap* pO = a.tma_store ? &tmO : nullptr;
+  if (!b_mn) return launch_gemm<BN, 4, false, false, EPI_STORE>(tmA, tmB, a, max_tiles, stream, pO);
+  return launch_gemm<BN, 4, false, true, EPI_STORE>(tmA, tmB, a, max_tiles, stream, pO);
 }
 
 extern "C" int zs_group_xty(int num_experts, void* DW, int64_t dw_se, int64_t dw_sk, int64_t dw_sn, void* Db,
@@ -1880,8 +1963,12 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     if (rc != ZS_OK) return rc;
   }
   for (int it = 0; it < steps; ++it) {
-    CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128;
+    CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128, tO_A, tO_B, tO_X;
     int rc;
+    // outputs of the three products, written by TMA stores
+    if ((rc = make_out_tmap(&tO_A, Abuf, dtype, m, batch * m, m * es)) != ZS_OK) return rc;
+    if ((rc = make_out_tmap(&tO_B, Bbuf, dtype, m, batch * m, m * es)) != ZS_OK) return rc;
+    if ((rc = make_out_tmap(&tO_X, Xn, dtype, n, batch * m, n * es)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tX_k128, X, dtype, n, batch * m, n * es, 64, 128)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tX_k256, X, dtype, n, batch * m, n * es, 64, BN / 2)) != ZS_OK) return rc;
     if ((rc = make_tmap(&tX_mn, X, dtype, n, batch * m, n * es, 64, 64)) != ZS_OK) return rc;
@@ -1896,6 +1983,7 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.out_rows = batch * m;
     g.out_dtype = dtype;
     g.ldo_n = 1;
+    g.tma_store = 1;
     const int64_t mt = (m + BM - 1) / BM;
     // A = X X^T  (per matrix: M = m, N = m, K = n; B operand = X rows of the same matrix)
     g.n_tiles = (int)((m + BN - 1) / BN);
@@ -1909,7 +1997,8 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     // triangle of tiles is computed, each off-diagonal tile also writes its
     // transpose (the third product, B X, is not symmetric)
     g.sym_upper = (pair_enabled() && m % 256 == 0) ? 1 : 0;
-    if ((rc = launch_gemm<BN, 4, false, false, EPI_STORE>(tX_k128, tX_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+    if ((rc = launch_gemm<BN, 4, false, false, EPI_STORE>(tX_k128, tX_k256, g, batch * mt * g.n_tiles, stream,
+                                                          &tO_A)) != ZS_OK)
       return rc;
     // B = b A + c A A   (B operand = A^T = A)
     g.kb_rows = (int)((m + BK - 1) / BK);
@@ -1918,7 +2007,8 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.ld_aux = m;
     g.alpha = c;
     g.beta = b;
-    if ((rc = launch_gemm<BN, 4, false, false, EPI_AXPBY>(tA_k128, tA_k256, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+    if ((rc = launch_gemm<BN, 4, false, false, EPI_AXPBY>(tA_k128, tA_k256, g, batch * mt * g.n_tiles, stream,
+                                                          &tO_B)) != ZS_OK)
       return rc;
     // X' = a X + B X    (B operand = X^T: X is [K = m rows, N = n cols] per matrix, MN-major)
     g.sym_upper = 0;
@@ -1932,7 +2022,8 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.alpha = 1.0f;
     g.beta = a;
     g.b_rows_per_expert = (int)m;
-    if ((rc = launch_gemm<BN, 4, false, true, EPI_AXPBY>(tB_k128, tX_mn, g, batch * mt * g.n_tiles, stream)) != ZS_OK)
+    if ((rc = launch_gemm<BN, 4, false, true, EPI_AXPBY>(tB_k128, tX_mn, g, batch * mt * g.n_tiles, stream,
+                                                         &tO_X)) != ZS_OK)
       return rc;
     char* t = X;
     X = Xn;
