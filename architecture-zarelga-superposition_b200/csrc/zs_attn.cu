@@ -1323,3 +1323,79 @@ extern "C" int zs_attention_backward(const void* q, const void* k, const void* v
                                      nullptr, 0, 0, D, B, S, H, Hkv, hd, window, seg_start, k_sink, sink_dtype,
                                      ds_sink, softmax_scale, nullptr, 0, stream);
 }
+
+// ------------------------------------------------------------ sink gradient
+// dk_sink[h, :] = scale * sum over rows r = b*S + s of ds_sink[b, h, s] * q[r, h, :]
+// in two fixed-order passes (per-chunk partials, then their sum): the same
+// result on every run.  One block of 256 threads per (head, chunk of
+// SINK_CHUNK rows): four row groups of 64 threads, each thread two columns.
+namespace zs {
+namespace attn {
+constexpr int SINK_CHUNK = 256;
+
+__global__ void __launch_bounds__(256) sink_grad_partial_kernel(const float* __restrict__ ds, const __nv_bfloat16* q,
+                                                                int64_t ldq, int S, int H, int hd, int64_t rows,
+                                                                int n_chunks, float* __restrict__ part) {
+  const int h = blockIdx.y, chunk = blockIdx.x;
+  const int g = threadIdx.x >> 6, c2 = (threadIdx.x & 63) * 2;
+  __shared__ float red[4][256];
+  float a0 = 0.f, a1 = 0.f;
+  if (c2 < hd) {
+    const int64_t r0 = (int64_t)chunk * SINK_CHUNK;
+    const int64_t r1 = min(r0 + SINK_CHUNK, rows);
+    for (int64_t r = r0 + g; r < r1; r += 4) {
+      const int64_t b = r / S, s = r - b * S;
+      const float w = __ldg(ds + (b * H + h) * (int64_t)S + s);
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + r * ldq + (int64_t)h * hd + c2);
+      const float2 f = __bfloat1622float2(v);
+      a0 = fmaf(w, f.x, a0);
+      a1 = fmaf(w, f.y, a1);
+    }
+  }
+  red[g][c2] = a0;
+  red[g][c2 + 1] = a1;
+  __syncthreads();
+  if (g == 0 && c2 < hd) {
+    float* o = part + ((int64_t)h * n_chunks + chunk) * hd;
+    o[c2] = (red[0][c2] + red[1][c2]) + (red[2][c2] + red[3][c2]);
+    o[c2 + 1] = (red[0][c2 + 1] + red[1][c2 + 1]) + (red[2][c2 + 1] + red[3][c2 + 1]);
+  }
+}
+
+__global__ void sink_grad_finish_kernel(const float* __restrict__ part, int n_chunks, int hd, float scale,
+                                        float* __restrict__ dk_sink) {
+  const int h = blockIdx.x, c = threadIdx.x;
+  if (c >= hd) return;
+  const float* p = part + (int64_t)h * n_chunks * hd + c;
+  float acc = 0.f;
+  for (int i = 0; i < n_chunks; ++i) acc += p[(int64_t)i * hd];
+  dk_sink[h * hd + c] = acc * scale;
+}
+}  // namespace attn
+}  // namespace zs
+
+extern "C" size_t zs_attention_sink_grad_workspace(int B, int S, int H, int hd) {
+  const int64_t rows = (int64_t)B * S;
+  const int64_t n_chunks = (rows + attn::SINK_CHUNK - 1) / attn::SINK_CHUNK;
+  return (size_t)(H * n_chunks * hd) * sizeof(float) + 256;
+}
+
+extern "C" int zs_attention_sink_grad(const float* ds_sink, const void* q, int64_t ldq, int B, int S, int H, int hd,
+                                      float softmax_scale, float* dk_sink, void* workspace, size_t workspace_bytes,
+                                      void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ZS_REQUIRE(ds_sink && q && dk_sink, ZS_ERR_ARG);
+  ZS_REQUIRE(B >= 1 && S >= 1 && H >= 1 && (hd == 64 || hd == 128), ZS_ERR_SHAPE);
+  ZS_REQUIRE(ldq >= (int64_t)H * hd && ldq % 2 == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0, ZS_ERR_ALIGN);
+  ZS_REQUIRE(workspace && workspace_bytes >= zs_attention_sink_grad_workspace(B, S, H, hd), ZS_ERR_WORKSPACE);
+  ZS_BIND(q);
+  const int64_t rows = (int64_t)B * S;
+  const int n_chunks = (int)((rows + attn::SINK_CHUNK - 1) / attn::SINK_CHUNK);
+  float* part = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  attn::sink_grad_partial_kernel<<<dim3((unsigned)n_chunks, (unsigned)H), 256, 0, stream>>>(
+      ds_sink, reinterpret_cast<const __nv_bfloat16*>(q), ldq, S, H, hd, rows, n_chunks, part);
+  ZS_CUDA_TRY(cudaGetLastError());
+  attn::sink_grad_finish_kernel<<<(unsigned)H, 128, 0, stream>>>(part, n_chunks, hd, softmax_scale, dk_sink);
+  ZS_CUDA_TRY(cudaGetLastError());
+  return ZS_OK;
+}

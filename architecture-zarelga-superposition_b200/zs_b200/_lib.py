@@ -70,6 +70,8 @@ _SIGNATURES = {
                                     _f32, _vp]),
     "zs_attention_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                      _i32, _i32, _vp, _vp, _i32, _vp, _f32, _vp]),
+    "zs_attention_sink_grad_workspace": (_sz, [_i32, _i32, _i32, _i32]),
+    "zs_attention_sink_grad": (_i32, [_vp, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
     "zs_muonmd_pre_workspace": (_sz, [_i64, _i64, _i64]),
     "zs_ipc_handle_size": (_i32, []),
     "zs_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(_i64)]),

@@ -44,6 +44,18 @@ def seg_start_from_seq_ids(seq_ids: torch.Tensor) -> torch.Tensor:
     return torch.where(seq_ids >= 0, seg, torch.full_like(seg, -1)).to(torch.int32).contiguous()
 
 
+def sink_grad(ds_sink, q, ldq, B, S, H, hd, scale):
+    """dk_sink [H, hd] f32 = scale * sum_{b,s} ds_sink[b, h, s] * q[b, s, h, :], q bf16 rows of ldq
+    elements from q's first element (zs_attention_sink_grad: q read once, fixed-order sums)."""
+    dk = torch.empty(H, hd, dtype=torch.float32, device=q.device)
+    L = Z.lib()
+    ws = torch.empty(int(L.zs_attention_sink_grad_workspace(B, S, H, hd)), dtype=torch.uint8, device=q.device)
+    Z.count(2)
+    Z.check(L.zs_attention_sink_grad(ds_sink.data_ptr(), q.data_ptr(), ldq, B, S, H, hd, float(scale), dk.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), Z.stream_of(q)), "zs_attention_sink_grad")
+    return dk
+
+
 class _Attention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, k_sink, window, seg_start, scale):
@@ -84,7 +96,7 @@ class _Attention(torch.autograd.Function):
         Z.count(3)
         dk_sink = None
         if k_sink is not None and ctx.needs_input_grad[3]:
-            dk_sink = (torch.einsum("bhs,bshd->hd", ds_sink, q.float()) * ctx.scale).to(k_sink.dtype)
+            dk_sink = sink_grad(ds_sink, q, H * hd, B, S, H, hd, ctx.scale).to(k_sink.dtype)
         return dq, dk, dv, dk_sink, None, None, None
 
 
@@ -183,8 +195,7 @@ class _GatedAttentionCore(torch.autograd.Function):
                 "zs_qk_norm_rope_backward")
         dk_sink = None
         if k_sink is not None and ctx.needs_input_grad[3]:
-            q = qk[..., : H * hd].reshape(B, S, H, hd)
-            dk_sink = (torch.einsum("bhs,bshd->hd", ds_sink, q.float()) * scale).to(k_sink.dtype)
+            dk_sink = sink_grad(ds_sink, qk, ld_qk, B, S, H, hd, scale).to(k_sink.dtype)
         return (dqkvg, dwq.to(wq.dtype), dwk.to(wk.dtype), dk_sink) + (None,) * 11
 
 

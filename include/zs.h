@@ -448,6 +448,19 @@ int zs_gated_attention_backward(const void* q, int64_t ldq, const void* k, int64
                                 const void* k_sink, int sink_dtype, float* ds_sink, float softmax_scale,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Gradient of the sink key (modeling/hca.py:138-144: the sink logit of query
+ * row (b, s, h) is scale * q[b, s, h, :] . k_sink[h]):
+ *   dk_sink[h, :] = scale * sum_{b, s} ds_sink[b, h, s] * q[b, s, h, :]
+ * with ds_sink from zs_attention_backward / zs_gated_attention_backward and q
+ * the (normalised, rotated) bf16 queries, rows of ldq elements with head h at
+ * column h * hd.  dk_sink f32 [H, hd].  Fixed-order sums (bit-identical runs);
+ * workspace: zs_attention_sink_grad_workspace(B, S, H, hd) bytes.
+ */
+size_t zs_attention_sink_grad_workspace(int B, int S, int H, int hd);
+int zs_attention_sink_grad(const float* ds_sink, const void* q, int64_t ldq, int B, int S, int H, int hd,
+                           float softmax_scale, float* dk_sink, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ cross entropy (a16-a18) */
 
 /*

@@ -245,3 +245,20 @@ def test_fused_gated_attention_core_matches_f32_torch():
     assert torch.all(qkvg.grad[..., W:] == 0)
     for a_, b_ in ((wq.grad, wqr.grad), (wk.grad, wkr.grad)):
         assert cosine(a_, b_) > 0.999 and rel_err(a_, b_) < 3e-2
+
+
+@pytest.mark.parametrize("B,S,H,hd,extra", [(2, 300, 4, 64, 0), (1, 4096, 12, 128, 1024), (3, 17, 2, 128, 8)])
+def test_sink_key_gradient_kernel(B, S, H, hd, extra):
+    """zs_attention_sink_grad against the f64 sum over (batch, position), q read from rows wider
+    than the heads (the fused q|k buffer), and bit-identical on a second run."""
+    from zs_b200.attn import sink_grad
+
+    g = torch.Generator(device="cuda").manual_seed(S + hd)
+    ld = H * hd + extra
+    qbuf = torch.randn(B, S, ld, device="cuda", generator=g).bfloat16()
+    ds = torch.randn(B, H, S, device="cuda", generator=g)
+    got = sink_grad(ds, qbuf, ld, B, S, H, hd, 0.125)
+    q = qbuf[..., : H * hd].reshape(B, S, H, hd).double()
+    want = torch.einsum("bhs,bshd->hd", ds.double(), q) * 0.125
+    assert (got.double() - want).norm() / want.norm() < 1e-6
+    assert torch.equal(sink_grad(ds, qbuf, ld, B, S, H, hd, 0.125), got)
