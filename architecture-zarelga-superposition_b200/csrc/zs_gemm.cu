@@ -88,6 +88,11 @@ struct GemmArgs {
                                        // write their transpose (EPI_STORE / EPI_AXPBY)
   int tma_store;                       // EPI_STORE / EPI_AXPBY without row_map or bias: full 32 x 32
                                        // chunks go out through the third tensor map (TMA stores)
+  int sym_ops;                         // uniform square groups on pair tiles: bit 0 (A), bit 1 (B): the
+                                       // operand is a symmetric matrix of which only the upper 256 x 256
+                                       // tiles are stored; a k-block left of the diagonal tile is read
+                                       // transposed (MN-major) from tmAT / tmBT.  With sym_ops the
+                                       // symmetric products' outputs skip their mirrored lower tiles.
 };
 
 template <int BN, int STAGES, bool PAIR = false>
@@ -432,7 +437,8 @@ __device__ __forceinline__ void prefetch_chunk(const GemmArgs& a, int64_t row, i
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int DT, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmAT,
+                        const __grid_constant__ CUtensorMap tmBT, const GemmArgs args) {
   using L = Smem<BN, STAGES, PAIR>;
   static_assert(!PAIR || !A_MN, "pair tiles are MODE_ROWS only");
   constexpr int TM = PAIR ? 2 * BM : BM;    // rows of a MODE_ROWS tile
@@ -585,11 +591,36 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
               const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset;
               const int r = EPI == EPI_SWIGLU ? brow + (crank ? args.swiglu_half : 0) + ti.nt * (BN / 2)
                                               : brow + ti.nt * BN + (int)crank * (BN / 2);
-              tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
-              tma_load_2d_pair(sB, &tmB, &full[stage], kb * BK, r);
+              const int kt = (kb * BK) / TM;   // 256-wide tile of this k-block
+              if ((args.sym_ops & 1) && kt < ti.mt) {
+                // A[rows, k-block] = A[k-block, rows]^T: two 64-column boxes, MN-major
+                const int gbase = ti.r0 - ti.mt * TM;
+                const int il = ti.mt * TM + (int)crank * BM;
+#pragma unroll
+                for (int j = 0; j < BM / 64; ++j)
+                  tma_load_2d_pair(sA + j * (BK * 128), &tmAT, &full[stage], il + j * 64, gbase + kb * BK);
+              } else {
+                tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
+              }
+              if ((args.sym_ops & 2) && kt < ti.nt) {
+                const int nl = ti.nt * BN + (int)crank * (BN / 2);
+#pragma unroll
+                for (int j = 0; j < BN / 128; ++j)
+                  tma_load_2d_pair(sB + j * (BK * 128), &tmBT, &full[stage], nl + j * 64, brow + kb * BK);
+              } else {
+                tma_load_2d_pair(sB, &tmB, &full[stage], kb * BK, r);
+              }
             } else {
               const int brow = ti.e * args.b_rows_per_expert + (int)args.b_row_offset + kb * BK;
-              tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
+              if ((args.sym_ops & 1) && (kb * BK) / TM < ti.mt) {
+                const int gbase = ti.r0 - ti.mt * TM;
+                const int il = ti.mt * TM + (int)crank * BM;
+#pragma unroll
+                for (int j = 0; j < BM / 64; ++j)
+                  tma_load_2d_pair(sA + j * (BK * 128), &tmAT, &full[stage], il + j * 64, gbase + kb * BK);
+              } else {
+                tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, ti.r0 + (int)crank * BM);
+              }
 #pragma unroll
               for (int j = 0; j < BN / 128; ++j)
                 tma_load_2d_pair(sB + j * (BK * 128), &tmB, &full[stage], ti.nt * BN + (int)crank * (BN / 2) + j * 64,
@@ -693,16 +724,22 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
         if (lane == 0) {
           const uint32_t a_base = smem_u32(sA);
           const uint32_t b_base = smem_u32(sB);
+          // operands read transposed for this k-block (symmetric upper-stored operands)
+          const bool kt_left = PAIR && !A_MN && args.sym_ops != 0 && (kb * BK) / TM < ti.mt;
+          const bool a_mn = A_MN || (kt_left && (args.sym_ops & 1));
+          const bool b_mn = B_MN || (PAIR && !A_MN && (args.sym_ops & 2) && (kb * BK) / TM < ti.nt);
+          const uint32_t kid = idesc_f16(TM, BN, DT == ZS_BF16 ? 1u : 0u, a_mn ? 1u : 0u, b_mn ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = A_MN ? smem_desc(a_base + kk * 2048, BK * 128, 1024, 2)
+            const uint64_t adesc = a_mn ? smem_desc(a_base + kk * 2048, BK * 128, 1024, 2)
                                         : smem_desc(a_base + kk * 32, 16, 1024, 2);
-            const uint64_t bdesc = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024, 2)
+            const uint64_t bdesc = b_mn ? smem_desc(b_base + kk * 2048, BK * 128, 1024, 2)
                                         : smem_desc(b_base + kk * 32, 16, 1024, 2);
+            const uint32_t use_id = (A_MN == a_mn && B_MN == b_mn) ? idesc : kid;
             if (PAIR)
-              tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, use_id, (kb > 0 || kk > 0) ? 1u : 0u);
             else
-              tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_f16(d_tmem, adesc, bdesc, use_id, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           if (PAIR)
             tc_commit_pair(&empty[stage], 0x3);
@@ -1006,7 +1043,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
               __syncwarp();
               emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
             }
-            if (args.sym_upper && ti.mt < ti.nt) {
+            if (args.sym_upper && !args.sym_ops && ti.mt < ti.nt) {
               const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;   // first row of this square group
               if (tchunk && ncols == 32)
                 tma_emit_chunk(&tmO, stg, pv, (int)(ti.r0 - gbase) + (int)crank * BM + quarter * 32,
@@ -1067,7 +1104,7 @@ __global__ void __launch_bounds__(64 + 32 * NUM_EPI_WARPS, 1)
               __syncwarp();
               emit_packed<DT>(args.out, out_row * args.ldo_m, col0, ncols, valid, pv, vec, stg);
             }
-            if (args.sym_upper && ti.mt < ti.nt) {
+            if (args.sym_upper && !args.sym_ops && ti.mt < ti.nt) {
               const int64_t gbase = ti.r0 - (int64_t)ti.mt * TM;
               if (tchunk && ncols == 32)
                 tma_emit_chunk(&tmO, stg, pv, (int)(ti.r0 - gbase) + (int)crank * BM + quarter * 32,
@@ -1204,6 +1241,17 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
+// Newton-Schulz keeps only the upper tiles of its symmetric products unless
+// ZS_NS_MIRROR=1 in the environment asks for whole matrices (mirrored tiles).
+static bool sym_operands_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("ZS_NS_MIRROR");
+    on = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 // Pair (2-SM) tiles are used for MODE_ROWS unless disabled with
 // ZS_GEMM_PAIR=0 in the environment, or the groups are uniform and shorter
 // than a pair tile (small batched matrices waste less with 128-row tiles).
@@ -1217,8 +1265,9 @@ static bool pair_enabled() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int DT>
-static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO, const GemmArgs& args,
-                       int64_t max_tiles, cudaStream_t stream) {
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmO,
+                       const CUtensorMap& tmAT, const CUtensorMap& tmBT, const GemmArgs& args, int64_t max_tiles,
+                       cudaStream_t stream) {
   constexpr int STAGES = 6;
   using L = Smem<BN, STAGES, true>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, DT, true>;
@@ -1260,21 +1309,26 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUt
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  ZS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, args));
+  ZS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, tmAT, tmBT, args));
   return ZS_OK;
 }
 
 // tmO: the output's tensor map for the TMA-store epilogue (args.tma_store), else unused.
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// tmAT / tmBT: MN-major maps of symmetric operands stored as upper tiles (args.sym_ops).
 static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int64_t max_tiles,
-                       cudaStream_t stream, const CUtensorMap* tmO = nullptr) {
+                       cudaStream_t stream, const CUtensorMap* tmO = nullptr, const CUtensorMap* tmAT = nullptr,
+                       const CUtensorMap* tmBT = nullptr) {
   const CUtensorMap& tO = tmO != nullptr ? *tmO : tmA;
+  const CUtensorMap& tAT = tmAT != nullptr ? *tmAT : tmA;
+  const CUtensorMap& tBT = tmBT != nullptr ? *tmBT : tmB;
   if (args.tma_store && tmO == nullptr) return ZS_ERR_ARG;
+  if (((args.sym_ops & 1) && tmAT == nullptr) || ((args.sym_ops & 2) && tmBT == nullptr)) return ZS_ERR_ARG;
   if constexpr (!A_MN) {
     if (args.mode == MODE_ROWS && pair_enabled() && !(args.group_rows > 0 && args.group_rows < 2 * BM)) {
       return args.out_dtype == ZS_F16
-                 ? launch_pair<BN, A_MN, B_MN, EPI, ZS_F16>(tmA, tmB, tO, args, max_tiles, stream)
-                 : launch_pair<BN, A_MN, B_MN, EPI, ZS_BF16>(tmA, tmB, tO, args, max_tiles, stream);
+                 ? launch_pair<BN, A_MN, B_MN, EPI, ZS_F16>(tmA, tmB, tO, tAT, tBT, args, max_tiles, stream)
+                 : launch_pair<BN, A_MN, B_MN, EPI, ZS_BF16>(tmA, tmB, tO, tAT, tBT, args, max_tiles, stream);
     }
   }
   using L = Smem<BN, STAGES>;
@@ -1287,7 +1341,8 @@ static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
   if (lim > 0 && grid > lim) grid = lim;
   if (max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, tO, args);
+  if (args.sym_ops) return ZS_ERR_ARG;   // symmetric operands need pair tiles
+  kern<<<(unsigned)grid, 64 + 32 * NUM_EPI_WARPS, L::ALLOC, stream>>>(tmA, tmB, tO, tAT, tBT, args);
   ZS_CUDA_TRY(cudaGetLastError());
   return ZS_OK;
 }
@@ -1963,8 +2018,12 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     if (rc != ZS_OK) return rc;
   }
   for (int it = 0; it < steps; ++it) {
-    CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128, tO_A, tO_B, tO_X;
+    CUtensorMap tX_k128, tX_k256, tX_mn, tA_k128, tA_k256, tB_k128, tO_A, tO_B, tO_X, tA_mn, tB_mn;
     int rc;
+    // A and B are symmetric: with pair tiles only their upper 256 x 256 tiles are written,
+    // and the products that read them take the blocks left of the diagonal transposed
+    if ((rc = make_tmap(&tA_mn, Abuf, dtype, m, batch * m, m * es, 64, 64)) != ZS_OK) return rc;
+    if ((rc = make_tmap(&tB_mn, Bbuf, dtype, m, batch * m, m * es, 64, 64)) != ZS_OK) return rc;
     // outputs of the three products, written by TMA stores
     if ((rc = make_out_tmap(&tO_A, Abuf, dtype, m, batch * m, m * es)) != ZS_OK) return rc;
     if ((rc = make_out_tmap(&tO_B, Bbuf, dtype, m, batch * m, m * es)) != ZS_OK) return rc;
@@ -1997,6 +2056,8 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     // triangle of tiles is computed, each off-diagonal tile also writes its
     // transpose (the third product, B X, is not symmetric)
     g.sym_upper = (pair_enabled() && m % 256 == 0) ? 1 : 0;
+    const int sym = g.sym_upper && sym_operands_enabled();
+    g.sym_ops = sym ? 4 : 0;   // output only: neither operand is symmetric, the mirror is skipped
     if ((rc = launch_gemm<BN, 4, false, false, EPI_STORE>(tX_k128, tX_k256, g, batch * mt * g.n_tiles, stream,
                                                           &tO_A)) != ZS_OK)
       return rc;
@@ -2007,8 +2068,9 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.ld_aux = m;
     g.alpha = c;
     g.beta = b;
+    g.sym_ops = sym ? 3 : 0;   // both operands are A (upper tiles stored)
     if ((rc = launch_gemm<BN, 4, false, false, EPI_AXPBY>(tA_k128, tA_k256, g, batch * mt * g.n_tiles, stream,
-                                                          &tO_B)) != ZS_OK)
+                                                          &tO_B, &tA_mn, &tA_mn)) != ZS_OK)
       return rc;
     // X' = a X + B X    (B operand = X^T: X is [K = m rows, N = n cols] per matrix, MN-major)
     g.sym_upper = 0;
@@ -2022,8 +2084,9 @@ extern "C" int zs_newton_schulz5(const void* G, void* X_out, int64_t batch, int6
     g.alpha = 1.0f;
     g.beta = a;
     g.b_rows_per_expert = (int)m;
+    g.sym_ops = sym ? 1 : 0;   // A = B (upper tiles stored); X is whole
     if ((rc = launch_gemm<BN, 4, false, true, EPI_AXPBY>(tB_k128, tX_mn, g, batch * mt * g.n_tiles, stream,
-                                                         &tO_X)) != ZS_OK)
+                                                         &tO_X, &tB_mn)) != ZS_OK)
       return rc;
     char* t = X;
     X = Xn;
