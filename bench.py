@@ -889,6 +889,180 @@ def run_config5(args):
     dist.destroy_process_group()
 
 
+def config5_model_config(layers):
+    from modeling.model_config import ModelConfig
+
+    return ModelConfig(vocab_size=65536, embed_size=2048, hidden_size=2048, transformer_depth=layers,
+                       intermediate_size=1024, n_experts=129, n_shared_experts=1, n_experts_per_token=8,
+                       n_attention_heads=16, n_key_value_heads=4, attention_window_pattern=(None,) * layers,
+                       max_position_embeddings=8192, sequence_length=8192)
+
+
+def run_config5_model(args):
+    """BASELINE configs[4] as a whole training step: the 2048-wide MoE LM (16 heads of 128, 128
+    routed experts of ffn 1024 + 1 shared, top-8, V 65536) on token-superposition batches: 8192
+    latent positions per sequence, each a bag of 4 raw token ids (the bag-mean embedding), the
+    next position's 4 ids as the multi-target MCCE labels (s = 4 everywhere), micro-batch 4 per
+    GPU, uniform synthetic ids drawn fresh every step; forward, MCCE loss, backward, MuonMD +
+    AdamW + sparse-embedding optimizer, aux-loss-free bias update.  With N > 1 the routed
+    experts are split over the ranks (expert parallel, all-to-all dispatch/combine) and the
+    other parameters are data parallel.  Depth: --layers (default 4 per GPU up to 24: the
+    24-layer model holds 19 B expert parameters and needs several GPUs' memory)."""
+    import torch
+    import torch.distributed as dist
+
+    from modeling.mcce_fast_v2 import mcce_raw_token_mean_v2
+    from zs_b200 import _lib as Z
+    from zs_b200.data import bag_label_entropy_floor, ce_equivalent_reducible_loss
+    from zs_b200.lm import MoELM
+    from zs_b200.train import auxillary_loss_free_update, build_muonmd_optimizer, enable_fused_weight_grad
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pg = dist.group.WORLD if world > 1 else None
+    layers = args.layers_c5 or min(24, 4 * world)
+    cfg = config5_model_config(layers)
+    torch.manual_seed(4321)
+    model = MoELM(cfg).to(dev)
+    enable_fused_weight_grad(model)
+    expert_params = set()
+    if world > 1:
+        from scattermoe.expert_parallel import shard_experts
+
+        for m in shard_experts(model, pg):
+            expert_params.update(id(p) for p in m.parameters())
+    # expert weights differ between ranks, so Newton-Schulz is not split over them
+    opt = build_muonmd_optimizer(model, dev, capture_warmup_steps=3, process_group=None)
+    reducer = None
+    if world > 1:
+        from zs_b200.dp import GradAllReducer
+
+        reducer = GradAllReducer([p for p in model.parameters() if id(p) not in expert_params], bucket_mb=64.0,
+                                 average=True)
+    B, S, bag = args.micro_batch_c5, 8192, 4
+    V = cfg.vocab_size
+    warmup = max(args.warmup, 5)
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    nb = 3
+    batches = torch.randint(0, V, (nb, B, S, bag), device=dev, generator=g)
+    mask = torch.ones(B, S, dtype=torch.long, device=dev)
+    s_full = torch.full((B * (S - 1),), bag, dtype=torch.long, device=dev)
+    it = [0]
+
+    def train_step(ids):
+        opt.zero_grad(set_to_none=False)
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            emb, all_topk = model.headless_forward(ids)
+            hidden = emb[:, :-1].reshape(-1, emb.size(-1))
+            labels = ids[:, 1:].reshape(-1, bag)
+            raw = mcce_raw_token_mean_v2(hidden, model.get_classifier_weights(), labels, s_full)
+        floor = bag_label_entropy_floor(labels, s_full)
+        loss, _ = ce_equivalent_reducible_loss(raw, V, floor)
+        loss.backward()
+        if reducer is not None:
+            reducer.finish()
+        opt.step()
+        auxillary_loss_free_update(model, all_topk, 1e-3, mask, process_group=pg)
+        return loss
+
+    def step():
+        i = it[0] % nb
+        it[0] += 1
+        loss = train_step(batches[i])
+        batches[i].random_(0, V, generator=g)
+        return loss
+
+    Z.INSTR.timing = True
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.5)
+    Z.INSTR.events = {}
+    l0 = Z.INSTR.launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ht0 = time.time()
+    t0.record()
+    for _ in range(args.steps):
+        loss = step()
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ht1 = time.time()
+    Z.INSTR.timing = False
+    clocks = sampler.stop(ht0, ht1)
+    launches = Z.INSTR.launches - l0
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    table = kernel_table(args.steps)
+    loss_v = float(loss.item())
+    # end to end: the bags uploaded from pinned host memory and the loss read back every step
+    e_steps = 0 if args.no_e2e else max(1, min(args.steps, args.e2e_steps))
+    ids_h = torch.randint(0, V, (2, B, S, bag), generator=torch.Generator().manual_seed(6 + rank)).pin_memory()
+    loss_h = torch.empty(max(e_steps, 1), dtype=torch.float32).pin_memory()
+    ids_d = torch.empty(B, S, bag, dtype=torch.long, device=dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e_steps):
+        ids_d.copy_(ids_h[i % 2], non_blocking=True)
+        lo = train_step(ids_d)
+        loss_h[i:i + 1].copy_(lo.detach().reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = max(e0.elapsed_time(e1), 1e-9)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    err = Z.device_error()
+    if rank == 0:
+        burst, sustained, _, src = measured_peaks()
+        fpt = model_flops_per_token(cfg, S)
+        value = world * B * S * args.steps / (ms * 1e-3)
+        line = {"metric": METRIC, "value": value, "unit": "latent tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"config5 full training step at L={layers}: d=2048 H=16/4 hd=128, E=128+1 "
+                                       f"shared ffn=1024 top-8 ({128 // world} experts per GPU), V=65536, 8192 "
+                                       f"latent positions x micro-batch {B} per GPU, bags of 4 raw ids (bag-mean "
+                                       "embedding), MCCE with 4 targets, bf16",
+                           "model": "config5 MoE LM", "layers": layers, "global_batch": world * B, "seq_len": S,
+                           "bag": bag, "raw_tokens_per_s": value * bag,
+                           "parallelism": f"ep{world}+dp{world}" if world > 1 else "single GPU",
+                           "model_gflop_per_latent_token": fpt / 1e9,
+                           "mfu_of_sustained_peak": value * fpt / (world * sustained * 1e12),
+                           "l2": "working set per step tens of GB, far larger than the 126 MB L2",
+                           "ids": "fresh uniform token ids every step", "loss": loss_v},
+                "roofline": roofline_from_table(table, clocks), "kernels": table, "cpu_baseline": None,
+                "e2e": None if not e_steps else {
+                    "value": world * B * S * e_steps / (e_ms * 1e-3), "unit": "latent tokens/s",
+                    "h2d_bytes_per_step": ids_d.numel() * 8, "d2h_bytes_per_step": 4, "steps": e_steps,
+                    "last_loss": float(loss_h[e_steps - 1])},
+                "gpu_launches": launches, "clocks": clocks, "device_error": err}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------ kernel workloads
 # Fixed single-kernel workloads at the configs' shapes, for timing with CUDA events and for
 # capturing one kernel under a profiler (one process, one GPU):  bench.py --kernel NAME
@@ -1092,6 +1266,12 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="config 4: transformer depth")
     ap.add_argument("--micro-batch", type=int, default=8, help="config 4: sequences of 4096 per GPU")
     ap.add_argument("--mcce", action="store_true", help="config 3: the 4-target MCCE variant")
+    ap.add_argument("--full-model", action="store_true",
+                    help="config 5: the whole training step of the model instead of its MoE layer")
+    ap.add_argument("--layers-c5", type=int, default=0,
+                    help="config 5 --full-model: transformer depth (default 4 per GPU, at most 24)")
+    ap.add_argument("--micro-batch-c5", type=int, default=4,
+                    help="config 5 --full-model: sequences of 8192 latent positions per GPU")
     ap.add_argument("--kernel", default=None, choices=sorted(KERNEL_WORKLOADS),
                     help="time one fixed kernel workload instead of a config (for profiling)")
     ap.add_argument("--batch", type=int, default=0, help="--kernel attention: sequences of 4096 (default 8)")
@@ -1099,7 +1279,7 @@ def main():
                     help="config 2 with N > 1: gradient all-reduce on the copy engines (ce) or NCCL")
     args = ap.parse_args()
     if not args.steps:
-        args.steps = 10 if args.kernel else (20 if args.config == 4 else 200)
+        args.steps = 10 if args.kernel else (20 if args.config == 4 else (10 if args.full_model else 200))
     if args.kernel:
         run_kernel(args)
         return
@@ -1113,7 +1293,7 @@ def main():
     elif args.config == 4:
         run_config4(args)
     elif args.config == 5:
-        run_config5(args)
+        run_config5_model(args) if args.full_model else run_config5(args)
     else:
         run_gpu(args)
 
