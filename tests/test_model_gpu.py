@@ -125,3 +125,34 @@ def test_lazy_zero_grad_of_fused_expert_gradients_matches_filled_buffers():
         assert not stale, stale
     for n in runs[0]:
         assert torch.equal(runs[0][n], runs[1][n]), n
+
+
+def test_token_superposition_step_on_bags():
+    """BASELINE config 5's input format through the whole model: [B, S, 4] bags of token ids
+    (bag-mean embedding, sqrt(d) upscale of an untied table), the next position's bag as the
+    4-target MCCE labels; the loss of the untrained model is near log V, the bag embedding equals
+    the mean of the table rows, every lookup gets one COO gradient row, and the hidden states'
+    gradient and every parameter gradient are finite."""
+    from modeling.mcce_fast_v2 import mcce_raw_token_mean_v2
+
+    cfg, m = _tiny()
+    B, S, bag = 2, 256, 4
+    ids = torch.randint(0, cfg.vocab_size, (B, S, bag), device="cuda")
+    emb = m.embed(ids)
+    scale = 1.0 if m.tie_word_embeddings else math.sqrt(cfg.hidden_size)
+    want = m.embedding.weight[ids].mean(2) * scale
+    assert torch.allclose(emb, want, rtol=1e-5, atol=1e-6)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        h, routing = m.headless_forward(ids)
+        hidden = h[:, :-1].reshape(-1, h.size(-1))
+        labels = ids[:, 1:].reshape(-1, bag)
+        s = torch.full((labels.size(0),), bag, dtype=torch.long, device="cuda")
+        loss = mcce_raw_token_mean_v2(hidden, m.get_classifier_weights(), labels, s)
+    assert abs(float(loss) - math.log(cfg.vocab_size)) < 0.5
+    loss.backward()
+    g = m.embedding.weight.grad
+    assert g.is_sparse and g._nnz() == B * S * bag
+    for name, p in m.named_parameters():
+        if p.grad is not None and not p.grad.is_sparse:
+            assert torch.isfinite(p.grad).all(), name
+    assert len(routing) == cfg.transformer_depth
