@@ -253,15 +253,18 @@ def _world(process_group):
     return dist.get_world_size(process_group), dist.get_rank(process_group)
 
 
-def _ns_sharded(stack, steps, process_group, ns):
+def _ns_sharded(stack, steps, process_group, ns, async_op=False):
     """Newton-Schulz of the matrices stack[0..b) split over the ranks of process_group:
     rank r orthogonalises matrices [r*per, (r+1)*per) (per = ceil(b / world)), and one
     all_gather_into_tensor assembles the bf16 results on every rank.  Every rank must
     call this with the same stack shape (data-parallel ranks hold the same reduced
-    gradients, so the optimizer state and the Newton-Schulz inputs are identical)."""
+    gradients, so the optimizer state and the Newton-Schulz inputs are identical).
+    With async_op, returns (result, work): the gather is in flight and work.wait() makes
+    the current stream wait for it (work is None when nothing is gathered)."""
     world, rank = _world(process_group)
     if world == 1:
-        return ns(stack, steps)
+        y = ns(stack, steps)
+        return (y, None) if async_op else y
     b = stack.size(0)
     per = -(-b // world)
     lo, hi = min(rank * per, b), min((rank + 1) * per, b)
@@ -269,8 +272,8 @@ def _ns_sharded(stack, steps, process_group, ns):
     if hi > lo:
         mine[:hi - lo].copy_(ns(stack[lo:hi], steps))
     full = torch.empty((per * world,) + tuple(stack.shape[1:]), dtype=torch.bfloat16, device=stack.device)
-    dist.all_gather_into_tensor(full, mine, group=process_group)
-    return full[:b]
+    work = dist.all_gather_into_tensor(full, mine, group=process_group, async_op=async_op)
+    return (full[:b], work) if async_op else full[:b]
 
 
 def _ns_plan(shapes, steps, world):
@@ -359,6 +362,18 @@ def md_decoupled_steps(jobs, states, process_group=None):
         Z.require_cuda(p, p.grad)
         m, n = p.shape[-2], p.shape[-1]
         shapes.append((p.numel() // (m * n), m, n))
+    def post(chunk, pre, Us, direct, work):
+        if work is not None:
+            work.wait()   # the stream waits for this batch's all-gather (no host sync)
+        for i, (W, red, _), U in zip(chunk, pre, Us):
+            p, hp = jobs[i]
+            _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
+                     gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"],
+                     u_trans=direct and shapes[i][1] > shapes[i][2])
+
+    # With several ranks a batch's all-gather is left in flight while the next batch's
+    # element-wise pass and Newton-Schulz are issued; its post pass runs after them.
+    pending = None
     for mm, nn, st, chunk in _ns_plan(shapes, [hp["ns_steps"] for _, hp in jobs], world):
         total = sum(shapes[i][0] for i in chunk)
         # the kernels' 8-element granularity: other shapes are padded by the copying path
@@ -373,19 +388,20 @@ def md_decoupled_steps(jobs, states, process_group=None):
             pre.append(_md_pre(p, p.grad, states[p], momentum=hp["momentum"], gain_mode=hp["gain_mode"],
                                norm_axis=hp["norm_axis"], capturable=hp["capturable"], x_out=x_out,
                                x_trans=direct and m > n))
+        work = None
         if direct:
-            Y = _ns_sharded(stack, st, process_group, zeropower_via_newtonschulz5)
+            Y, work = _ns_sharded(stack, st, process_group, zeropower_via_newtonschulz5, async_op=True)
             Us, off = [], 0
             for i in chunk:
                 Us.append(Y[off:off + shapes[i][0]])
                 off += shapes[i][0]
         else:
             Us = _zeropower_many([x for _, _, x in pre], [st] * len(chunk), process_group)
-        for i, (W, red, _), U in zip(chunk, pre, Us):
-            p, hp = jobs[i]
-            _md_post(p, W, red, U, states[p], lr=hp["lr"], gain_lr=hp["gain_lr"], gain_betas=hp["gain_betas"],
-                     gain_eps=hp["gain_eps"], norm_axis=hp["norm_axis"], rescale_mode=hp["rescale_mode"],
-                     u_trans=direct and shapes[i][1] > shapes[i][2])
+        if pending is not None:
+            post(*pending)
+        pending = (chunk, pre, Us, direct, work)
+    if pending is not None:
+        post(*pending)
 
 
 def _muon_steps(jobs, states, process_group=None):
